@@ -1,0 +1,386 @@
+#!/usr/bin/env python
+"""Throughput of turt's GPU-resident GPT train step on B200 (fwd + bwd + clip + AdamW).
+
+Default workload: the 6-layer / 384-d "modern" GPT (6 heads, SwiGLU 1024, RMSNorm, RoPE,
+tied 8192 vocab, block 256, batch 32 sequences per GPU), synthetic uniform tokens and
+N(0, 0.02) weights.  One process per GPU (torchrun for N > 1); data parallel with per-layer
+NCCL gradient all-reduce inside the backward pass; per-GPU batch is fixed (weak scaling).
+
+Prints one JSON line (rank 0).  `value` is whole-job tokens/s with the token batches
+already resident in HBM; `e2e` is the same step through the public C ABI with host token
+arrays copied in and the loss copied out every step.  `--impl reference` times the
+reference's CPU data-parallel worker pool (a C restatement, see oracle/) on this host.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    # name: vocab, block, layers, heads, embd, arch, hidden, seqs per GPU, micro-batch seqs
+    "gpt-6L-384d": dict(V=8192, T=256, L=6, H=6, E=384, arch="modern", hidden=1024, batch=32, micro=32),
+    "gpt2-12L-768d": dict(V=8192, T=512, L=12, H=12, E=768, arch="gpt2", hidden=3072, batch=16, micro=16),
+    "gpt-12L-768d-dp": dict(V=8192, T=1024, L=12, H=12, E=768, arch="modern", hidden=2048, batch=256, micro=16,
+                            global_batch=True),
+    "gpt-tiny-4L-128d": dict(V=8192, T=128, L=4, H=4, E=128, arch="modern", hidden=352, batch=8, micro=8),
+}
+CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+def flops_per_token(w) -> int:
+    """Algorithmic FLOPs per trained token: 3 * [2L(4E^2 + kEh) + 2EV + 2LTE], k = 3 (SwiGLU) or 2 (GELU);
+    causal attention counted at half."""
+    k = 3 if w["arch"] == "modern" else 2
+    L, E, h, V, T = w["L"], w["E"], w["hidden"], w["V"], w["T"]
+    return 3 * (2 * L * (4 * E * E + k * E * h) + 2 * E * V + 2 * L * T * E)
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "200"], stdout=open(self.path, "w"),
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- reference arm
+def cpu_pool_sample(w, workers: int, seed: int):
+    """One step of the reference's CPU data-parallel pool (scripts/train-gpt.ts:200-242, C
+    restatement in oracle/) over a bounded sample: one full sequence per worker."""
+    import numpy as np
+
+    from oracle.oracle import Oracle
+    orc = Oracle()
+    cfg = orc.cfg(w["V"], w["T"], w["L"], w["H"], w["E"], w["arch"], w["hidden"])
+    params = orc.init(cfg, 7)
+    m = np.zeros_like(params)
+    v = np.zeros_like(params)
+    rng = np.random.default_rng(seed)
+    n = workers * w["T"]
+    ids = rng.integers(0, w["V"], n).astype(np.int32)
+    tgt = rng.integers(0, w["V"], n).astype(np.int32)
+
+    def step(k):
+        t0 = time.perf_counter()
+        orc.dp_step(cfg, params, m, v, k, ids, tgt, workers, w["T"], workers, 3e-4, 0.9, 0.95, 1e-8, 0.1, 1.0)
+        return time.perf_counter() - t0
+
+    return step, n
+
+
+def run_reference(args, w, rank: int) -> None:
+    if rank != 0:
+        return
+    workers = max(1, min((os.cpu_count() or 4) - 2, w["batch"]))
+    step, tokens = cpu_pool_sample(w, workers, 1)
+    for k in range(args.warmup):
+        step(k + 1)
+    secs = [step(args.warmup + k + 1) for k in range(args.steps)]
+    total = sum(secs)
+    value = tokens * args.steps / total
+    line = {
+        "impl": "reference", "metric": "train tokens/sec (fwd+bwd+clip+AdamW)", "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "model": args.workload, "global_batch": workers, "seq_len": w["T"],
+                   "parallelism": f"cpu-dp{workers}"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": workers, "kind": "port",
+                         "sample": f"{workers} sequences x {w['T']} tokens per step (one per worker thread), "
+                                   f"C restatement of the reference worker pool"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def init_weights(model, w, seed: int):
+    """N(0, 0.02) weights, residual projections scaled by 1/sqrt(2L), unit gains, zero biases
+    (src/models/gpt.ts:124-129,181-182,209-211)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    parts = []
+    res = 0.02 / math.sqrt(2 * w["L"])
+    for name, shp in zip(model.names, model.shapes):
+        n = int(np.prod(shp))
+        base = name.split(".")[-1]
+        if len(shp) == 1:
+            parts.append(np.ones(n, np.float32) if base.endswith("g") else np.zeros(n, np.float32))
+        else:
+            std = res if base in ("projW", "downW", "mpW") else 0.02
+            parts.append((rng.standard_normal(n) * std).astype(np.float32))
+    model.load_flat(np.concatenate(parts))
+
+
+def time_gemm(ctx, M, N, K, reps, precision):
+    """Average device time of one TF32 tensor-core GEMM launch (A [M,K], B [N,K] K-major),
+    the head-projection shape of the step, timed with CUDA events on the library's stream."""
+    import numpy as np
+    import torch
+
+    from turt_b200._lib import check, lib
+    a, b, c = ctx.buffer(M * K), ctx.buffer(N * K), ctx.buffer(M * N)
+    rng = np.random.default_rng(0)
+    ctx.upload(a, rng.standard_normal(M * K).astype(np.float32))
+    ctx.upload(b, rng.standard_normal(N * K).astype(np.float32))
+    stream = torch.cuda.current_stream()
+    for _ in range(3):
+        check(lib().turt_matmul_into(ctx.handle, a, b, c, M, K, N, 1, 0, 1, 0))
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        check(lib().turt_matmul_into(ctx.handle, a, b, c, M, K, N, 1, 0, 1, 0))
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    for p in (a, b, c):
+        ctx.free(p)
+    ctx.reclaim()
+    return ms
+
+
+def run_gpu(args, w, rank: int, world: int, local_rank: int) -> None:
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from turt_b200.runtime import Context, Model, make_config
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx = Context(local_rank)
+    ctx.set_stream(stream.cuda_stream)
+    ctx.set_precision(args.precision)
+    model = Model(ctx, make_config(w["V"], w["T"], w["L"], w["H"], w["E"], w["arch"], w["hidden"]))
+    init_weights(model, w, 1234)
+    if world > 1:
+        uid = [Model.dp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        model.dp_init(rank, world, uid[0])
+
+    seqs = w["batch"] // world if w.get("global_batch") else w["batch"]
+    micro = min(w["micro"], seqs)
+    assert seqs % micro == 0
+    n_micro = seqs // micro
+    T = w["T"]
+    global_seqs = seqs * world
+    rng = np.random.default_rng(100 + rank)
+    pool = 4  # distinct resident token batches, cycled
+    host_ids = [rng.integers(0, w["V"], seqs * T).astype(np.uint32) for _ in range(pool)]
+    host_tgt = [rng.integers(0, w["V"], seqs * T).astype(np.uint32) for _ in range(pool)]
+    dev_ids = [torch.from_numpy(a.view(np.int32)).cuda() for a in host_ids]
+    dev_tgt = [torch.from_numpy(a.view(np.int32)).cuda() for a in host_tgt]
+    torch.cuda.synchronize()
+
+    lr, b1, b2, eps, wd, clip = 3e-4, 0.9, 0.95, 1e-8, 0.1, 1.0
+    step_no = [0]
+
+    def adam():
+        step_no[0] += 1
+        k = step_no[0]
+        model.adamw_step(lr, b1, b2, eps, wd, 1 - b1 ** k, 1 - b2 ** k, clip=clip, grad_scale=1.0 / world)
+
+    def device_step(i):
+        model.zero_grad()
+        ids, tgt = dev_ids[i % pool], dev_tgt[i % pool]
+        for j in range(n_micro):
+            if world > 1:
+                model.dp_defer(j < n_micro - 1)
+            off = j * micro * T * 4
+            model.forward_backward_device(ids.data_ptr() + off, tgt.data_ptr() + off, micro, T,
+                                          loss_scale=micro / seqs)
+        adam()
+
+    def host_step(i):
+        model.zero_grad()
+        ids, tgt = host_ids[i % pool], host_tgt[i % pool]
+        loss = None
+        for j in range(n_micro):
+            if world > 1:
+                model.dp_defer(j < n_micro - 1)
+            sl = slice(j * micro * T, (j + 1) * micro * T)
+            loss = model.forward_backward(ids[sl], tgt[sl], micro, T, loss_scale=micro / seqs,
+                                          want_loss=(j == n_micro - 1))
+        adam()
+        return loss
+
+    def timed(fn, steps):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            fn(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = torch.tensor([e0.elapsed_time(e1)], device="cuda")
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return float(ms.item())
+
+    for i in range(args.warmup):
+        device_step(i)
+    model.read_loss()
+    launches0 = Context.launch_count()
+    with ClockSampler(local_rank) as clk:
+        ms = timed(device_step, args.steps)
+    launches = Context.launch_count() - launches0
+    clocks = clk.summary()
+    last_loss = model.read_loss()
+
+    # e2e: host token arrays in, loss out, every step
+    for i in range(2):
+        host_step(i)
+    ms_e2e = timed(host_step, args.steps)
+
+    tokens_per_step = global_seqs * T
+    value = tokens_per_step * args.steps / (ms / 1000.0)
+    e2e = tokens_per_step * args.steps / (ms_e2e / 1000.0)
+
+    peaks = measured_peaks()
+    tf32_peak = peaks["bf16_tflops"] / 2.0  # dense TF32 tensor rate is half the bf16 rate
+    tf32_peak_sust = peaks["bf16_tflops_sustained"] / 2.0
+    out = None
+    if rank == 0:
+        N_tok, V, E = micro * T, w["V"], w["E"]
+        gemm_ms = time_gemm(ctx, N_tok, V, E, 20, args.precision)
+        gemm_flops = 2.0 * N_tok * V * E
+        achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12
+        f_tok = flops_per_token(w)
+        step_tflops = f_tok * value / world / 1e12
+        out = {
+            "metric": "train tokens/sec (fwd+bwd+clip+AdamW)",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "tf32x3" if args.precision == 3 else "tf32", "data": "synthetic",
+            "config": {"workload": args.workload, "model": args.workload, "global_batch": global_seqs, "seq_len": T,
+                       "parallelism": f"dp{world}", "micro_batch": micro,
+                       "gemm_precision": "3xTF32 (error-compensated)" if args.precision == 3 else "TF32",
+                       "l2": "no flush: each step touches >1 GB of activations and weights (L2 is 126 MB)",
+                       "last_loss": last_loss},
+            "roofline": {"bound": "tensor", "kernel": "k_gemm_tf32 (head projection %dx%dx%d)" % (N_tok, V, E),
+                         "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s", "frac": achieved / tf32_peak,
+                         "traffic": None, "peak_source": f"{peaks['source']} bf16 dense / 2",
+                         "launch_ms": gemm_ms,
+                         "mma_issue_factor": 3 if args.precision == 3 else 1},
+            "step_roofline": {"flops_per_token": f_tok, "achieved_tflops_per_gpu": step_tflops,
+                              "peak_tflops": tf32_peak_sust, "frac": step_tflops / tf32_peak_sust,
+                              "peak_source": f"{peaks['source']} bf16 sustained / 2"},
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 2 * seqs * T * 4,
+                    "d2h_bytes_per_step": 4},
+            "gpu_launches": launches,
+            "clocks": clocks,
+        }
+    model.close()
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        workers = max(1, min((os.cpu_count() or 4) - 2, w["batch"]))
+        step, tokens = cpu_pool_sample(w, workers, 2)
+        secs = step(1)
+        out["cpu_baseline"] = {"value": tokens / secs, "unit": "tokens/s", "cores": workers, "kind": "port",
+                               "sample": f"one reference CPU data-parallel step over {workers} sequences x {w['T']} "
+                                         f"tokens ({workers} worker threads, C restatement of "
+                                         f"scripts/train-gpt.ts + train-worker.ts)"}
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="turt", choices=["turt", "reference"])
+    ap.add_argument("--workload", default="gpt-6L-384d", choices=sorted(WORKLOADS))
+    ap.add_argument("--precision", type=int, default=3, choices=[1, 3])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    w = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, w, rank)
+        return
+    run_gpu(args, w, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,198 @@
+/*
+ * turt_cuda.h -- C ABI of libturt_cuda.so, the B200 (sm_100a) backend for turt's
+ * GPU-resident GPT training step.
+ *
+ * Every entry point returns an int status (0 = TURT_OK); the message of the last failure
+ * on the calling thread is turt_last_error().  Pointers named `d_*` or documented as
+ * "device" are CUDA device pointers owned by the library (turt_buffer) or by the caller;
+ * everything else is host memory.  No C++ or torch types cross this boundary.
+ *
+ * The reference interfaces each group replaces are cited as path:line inside the turt
+ * project (TypeScript); INTEGRATION.md shows the Deno.dlopen binding for each symbol.
+ */
+#ifndef TURT_CUDA_H
+#define TURT_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define TURT_OK 0
+#define TURT_ERR_INVALID 1     /* bad argument or shape mismatch (reference: throws Error) */
+#define TURT_ERR_CUDA 2        /* CUDA runtime / driver failure */
+#define TURT_ERR_RANGE 3       /* token or target id out of range */
+#define TURT_ERR_TIMEOUT 4     /* a bounded device wait expired */
+#define TURT_ERR_NCCL 5        /* collective failed or was aborted */
+#define TURT_ERR_NONFINITE 6   /* non-finite loss / gradient norm */
+#define TURT_ERR_UNSUPPORTED 7 /* layout not handled */
+
+#define TURT_ARCH_GPT2 0
+#define TURT_ARCH_MODERN 1
+
+typedef struct turt_ctx turt_ctx;
+typedef struct turt_model turt_model;
+
+/* ------------------------------------------------------------------ context
+ * GpuEngine.create / device handling, src/infer/webgpu/autograd.ts:554-577. */
+const char* turt_last_error(void);
+int turt_version(void);
+int turt_init(int device, turt_ctx** out);
+int turt_ctx_destroy(turt_ctx* ctx);
+/* Run all of this context's work on an external CUDA stream (cudaStream_t as void*). */
+int turt_ctx_set_stream(turt_ctx* ctx, void* stream);
+void* turt_ctx_stream(turt_ctx* ctx);
+/* Waits for the context's stream and reports device-side error flags (range, timeout). */
+int turt_synchronize(turt_ctx* ctx);
+/* Tensor-core precision of every GEMM issued through this context (models included):
+ * TURT_PRECISION_TF32X3 (default) = error-compensated 3xTF32, ~fp32 accuracy, meets the
+ * reference's gradient tolerance; TURT_PRECISION_TF32 = one TF32 pass (10-bit mantissa). */
+#define TURT_PRECISION_TF32 1
+#define TURT_PRECISION_TF32X3 3
+int turt_set_precision(turt_ctx* ctx, int precision);
+int turt_get_precision(turt_ctx* ctx, int* precision);
+
+/* ------------------------------------------------------------------ buffers
+ * GpuEngine.buffer / free / reclaim / read / fill / tensor / indexBuffer,
+ * src/infer/webgpu/autograd.ts:589-595, 641-662, 701-709, 790-814.  Buffers are
+ * zero-filled; free is deferred to turt_reclaim (mirrors the reference's deferred destroy). */
+int turt_buffer(turt_ctx* ctx, size_t elems, float** d_out);
+int turt_index_buffer(turt_ctx* ctx, const uint32_t* host, size_t n, uint32_t** d_out);
+int turt_free(turt_ctx* ctx, void* d_ptr);
+int turt_reclaim(turt_ctx* ctx);
+int turt_upload(turt_ctx* ctx, void* d_dst, const void* host_src, size_t bytes);
+int turt_download(turt_ctx* ctx, void* host_dst, const void* d_src, size_t bytes);
+int turt_fill(turt_ctx* ctx, float* d_buf, float value, size_t elems);
+int turt_live_buffers(turt_ctx* ctx, int* live, int* peak);
+
+/* ----------------------------------------------------------------- op level
+ * One entry per GpuEngine kernel wrapper, same argument order and accumulate flags,
+ * src/infer/webgpu/autograd.ts:664-788.  All float / uint32 pointers are device pointers. */
+/* matmulInto :664-671 -- C (+)= op(A) op(B), batched; TF32 tensor cores when every pitch is a
+ * multiple of 4 elements, else an fp32 CUDA-core kernel. */
+int turt_matmul_into(turt_ctx* ctx, const float* a, const float* b, float* out, int M, int K, int N, int batch,
+                     int transA, int transB, int accum);
+/* ewise :672-674 -- out (+)= a op b[i % bLen]; op 0 add, 1 sub, 2 mul. */
+int turt_ewise(turt_ctx* ctx, const float* a, const float* b, float* out, size_t n, size_t bLen, int op, int accum);
+int turt_scale(turt_ctx* ctx, const float* a, float* out, size_t n, float s, int accum);            /* :675-678 */
+int turt_bcast_acc(turt_ctx* ctx, const float* src, float* out, size_t n, size_t bLen, float s);    /* :679-682 */
+int turt_segsum(turt_ctx* ctx, const float* g, float* out, size_t n, size_t bLen, float s, int accum); /* :683-686 */
+int turt_total(turt_ctx* ctx, const float* a, float* out, size_t n);                                /* :687-689 */
+int turt_relu(turt_ctx* ctx, const float* x, float* out, size_t n);                                 /* :690-692 */
+int turt_relu_bwd(turt_ctx* ctx, const float* x, const float* gOut, float* gIn, size_t n);          /* :693-695 */
+int turt_sgd(turt_ctx* ctx, const float* grad, float* param, size_t n, float lr);                   /* :696-699 */
+int turt_gelu(turt_ctx* ctx, const float* x, float* out, size_t n);                                 /* :711-713 */
+int turt_gelu_bwd(turt_ctx* ctx, const float* x, const float* gOut, float* gIn, size_t n);          /* :714-716 */
+int turt_silu(turt_ctx* ctx, const float* x, float* out, size_t n);                                 /* :717-719 */
+int turt_silu_bwd(turt_ctx* ctx, const float* x, const float* gOut, float* gIn, size_t n);          /* :720-722 */
+int turt_rms_fwd(turt_ctx* ctx, const float* x, const float* gamma, float* out, float* rstd, int rows, int d,
+                 float eps);                                                                         /* :723-726 */
+int turt_rms_dx(turt_ctx* ctx, const float* x, const float* gOut, const float* gamma, const float* rstd,
+                float* gIn, int rows, int d, float eps);                                             /* :727-730 */
+int turt_rms_dg(turt_ctx* ctx, const float* x, const float* gOut, const float* rstd, float* dgamma, int rows,
+                int d);                                                                              /* :731-734 */
+int turt_rope(turt_ctx* ctx, const float* x, float* out, int groups, int t, int hd, float base);    /* :735-738 */
+int turt_rope_bwd(turt_ctx* ctx, const float* gOut, float* gIn, int groups, int t, int hd, float base); /* :739-742 */
+int turt_softmax(turt_ctx* ctx, const float* x, float* out, int rows, int d);                       /* :743-745 */
+int turt_softmax_bwd(turt_ctx* ctx, const float* y, const float* gOut, float* gIn, int rows, int d); /* :746-748 */
+int turt_ln_fwd(turt_ctx* ctx, const float* x, const float* gamma, const float* beta, float* out, float* mean,
+                float* rstd, int rows, int d, float eps);                                           /* :749-752 */
+int turt_ln_dx(turt_ctx* ctx, const float* x, const float* gOut, const float* gamma, const float* mean,
+               const float* rstd, float* gIn, int rows, int d, float eps);                           /* :753-756 */
+int turt_ln_dgb(turt_ctx* ctx, const float* x, const float* gOut, const float* mean, const float* rstd,
+                float* dgamma, float* dbeta, int rows, int d);                                       /* :757-760 */
+/* gatherInto / gatherBwd :761-766 -- out-of-range ids raise TURT_ERR_RANGE at the next sync. */
+int turt_gather(turt_ctx* ctx, const float* table, const uint32_t* idx, float* out, int n, int d, int vocab);
+int turt_gather_bwd(turt_ctx* ctx, const uint32_t* idx, const float* gOut, float* dTable, int n, int d, int vocab);
+int turt_ce_fwd(turt_ctx* ctx, const float* logits, const uint32_t* targets, float* perRow, int rows,
+                int vocab);                                                                          /* :767-769 */
+int turt_ce_bwd(turt_ctx* ctx, const float* logits, const uint32_t* targets, const float* gLoss, float* dLogits,
+                int rows, int vocab);                                                                /* :770-772 */
+int turt_mask(turt_ctx* ctx, const float* x, float* out, int groups, int t);                        /* :773-775 */
+int turt_mask_bwd(turt_ctx* ctx, const float* gOut, float* gIn, int groups, int t);                 /* :776-778 */
+int turt_permute4(turt_ctx* ctx, const float* inp, float* out, const int* inShape4, const int* perm4, size_t n,
+                  int accum);                                                                        /* :779-782 */
+int turt_adamw(turt_ctx* ctx, const float* grad, float* param, float* m, float* v, size_t n, float lr, float b1,
+               float b2, float eps, float wd, float bc1, float bc2);                                 /* :783-788 */
+
+/* ----------------------------------------------------- host-array matmul
+ * GpuCompute.matmul / bmm, src/infer/webgpu/gpu.ts:66-141, and Backend.matmul,
+ * src/infer/backend.ts:11-16 / gpu-backend.ts:45-55: host arrays in, host array out. */
+int turt_host_matmul(turt_ctx* ctx, const float* a, int m, int k, const float* b, int n, float* out);
+int turt_host_bmm(turt_ctx* ctx, const float* a, int batch, int m, int k, const float* b, int n, float* out);
+
+/* -------------------------------------------------------------- model level
+ * GpuGPT, src/models/gpu-gpt.ts:54-202 (+ GPTConfig, src/models/gpt.ts:67-78) with the
+ * AdamW / clipGradNorm step of scripts/gpu-pretrain.ts:502-521 and scripts/train-gpt.ts:241-242. */
+typedef struct turt_config {
+  int vocab_size;
+  int block_size;
+  int n_layer;
+  int n_head;
+  int n_embd;
+  int arch;   /* TURT_ARCH_GPT2 or TURT_ARCH_MODERN */
+  int hidden; /* MLP width; 0 = mlpHidden(config) (gpt.ts:96-99) */
+} turt_config;
+
+int turt_model_create(turt_ctx* ctx, const turt_config* cfg, turt_model** out);
+int turt_model_destroy(turt_model* model);
+/* parameters() order, gpu-gpt.ts:118-132: count, total scalars, per-tensor name and shape. */
+int turt_param_count(turt_model* model, int* count);
+int turt_num_params(turt_model* model, size_t* total);
+int turt_param_info(turt_model* model, int index, char* name, int name_cap, int* shape2, int* ndim);
+/* Host <-> device copies of one parameter (or its gradient) in the reference's [in,out] layout. */
+int turt_param_upload(turt_model* model, int index, const float* host, size_t n);
+int turt_param_download(turt_model* model, int index, float* host, size_t n);
+int turt_grad_download(turt_model* model, int index, float* host, size_t n);
+/* zeroGrad on every parameter (gpu-gpt usage: scripts/gpu-pretrain.ts:502). */
+int turt_zero_grad(turt_model* model);
+/* GpuGPT.loss + backward (gpu-gpt.ts:185-201, autograd.ts:1196-1209): accumulates
+ * loss_scale * d(mean CE)/d(theta) into the gradients.  ids/targets are host arrays of b*t
+ * uint32.  loss_out (host, may be NULL) receives the mean loss; passing it synchronizes. */
+int turt_forward_backward(turt_model* model, const uint32_t* ids, const uint32_t* targets, int b, int t,
+                          float loss_scale, float* loss_out);
+/* Same step with ids/targets already in device memory (uint32[b*t] each): no host copies and
+ * no synchronization; the loss stays on the device (turt_read_loss fetches it). */
+int turt_forward_backward_device(turt_model* model, const uint32_t* d_ids, const uint32_t* d_targets, int b, int t,
+                                 float loss_scale);
+/* Synchronizes and returns the last step's mean loss (device flags are checked too). */
+int turt_read_loss(turt_model* model, float* loss_out);
+/* Number of kernels this library has launched in the process (all contexts). */
+int turt_launch_count(uint64_t* count);
+/* Forward only (evaluation loss), gpu-pretrain.ts:485-497. */
+int turt_forward(turt_model* model, const uint32_t* ids, const uint32_t* targets, int b, int t, float* loss_out);
+/* clipGradNorm (src/optim/clip.ts:7-24) over all gradients; norm_out may be NULL. */
+int turt_clip_grad_norm(turt_model* model, double max_norm, double* norm_out);
+/* AdamW over every parameter (one fused pass over the flat buffers), autograd.ts:516-531 with
+ * bias corrections from the host; clip > 0 folds the global-norm clip of clip.ts into the
+ * same pass (no host round trip); grad_scale multiplies the gradients first (1/world for DP). */
+int turt_adamw_step(turt_model* model, float lr, float b1, float b2, float eps, float wd, float bc1, float bc2,
+                    float clip, float grad_scale);
+
+/* ----------------------------------------------------------- data parallel
+ * The reference's worker-pool reduction (scripts/train-gpt.ts:200-219) as an NCCL all-reduce
+ * of the flat gradient buffer, issued per layer bucket during the backward pass. */
+int turt_dp_unique_id(char* id128);
+int turt_dp_init(turt_model* model, int rank, int world, const char* id128);
+int turt_dp_allreduce_grads(turt_model* model);
+/* defer = 1 skips the per-layer reduction (micro-batches before the last of a step). */
+int turt_dp_defer(turt_model* model, int defer);
+/* Waits for outstanding reductions; aborts the communicator after timeout_ms or on an
+ * asynchronous NCCL error and returns TURT_ERR_NCCL. */
+int turt_dp_wait(turt_model* model, int timeout_ms);
+int turt_dp_destroy(turt_model* model);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TURT_CUDA_H */

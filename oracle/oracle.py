@@ -93,6 +93,7 @@ class Oracle:
         L.oc_param_shapes.restype = i
         L.oc_param_shapes.argtypes = [vp, vp]
         L.oc_init.argtypes = [vp, C.c_uint32, vp]
+        L.oc_init_state.argtypes = [vp, vp, vp]
         L.oc_loss_grad.restype = d
         L.oc_loss_grad.argtypes = [vp, vp, vp, vp, vp, i, i, vp]
         L.oc_logits.restype = i
@@ -331,6 +332,12 @@ class Oracle:
     def init(self, cfg, seed: int) -> np.ndarray:
         p = np.zeros(self.num_params(cfg), dtype=self.dt)
         self.lib.oc_init(_f(cfg), seed, _f(p))
+        return p
+
+    def init_state(self, cfg, state) -> np.ndarray:
+        """GPT init drawing from (and advancing) a mulberry32 state cell."""
+        p = np.zeros(self.num_params(cfg), dtype=self.dt)
+        self.lib.oc_init_state(_f(cfg), _f(state), _f(p))
         return p
 
     def split(self, cfg, flat):

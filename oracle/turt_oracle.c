@@ -665,11 +665,19 @@ EXPORT int oc_param_shapes(const int* cfg, int* shapes) {
 
 /* GPT constructor init, src/models/gpt.ts:252-266 with Linear (src/nn/linear.ts:18-23):
    wte, [wpe], then per block q,k,v,proj, then gate,up,down | fc,proj.  Gains 1, biases 0. */
+EXPORT void oc_init_state(const int* cfg, uint32_t* state, real* params);
 EXPORT void oc_init(const int* cfg, uint32_t seed, real* params) {
+  uint32_t st = seed;
+  oc_init_state(cfg, &st, params);
+}
+
+/* Same, drawing from (and advancing) a caller-owned mulberry32 state, as when the reference
+   shares one rng between GPT construction and generate (tests/models/gpt.test.ts:46-69). */
+EXPORT void oc_init_state(const int* cfg, uint32_t* state, real* params) {
   gcfg c = read_cfg(cfg);
   moff o;
   layout(&c, &o);
-  uint32_t st = seed;
+  uint32_t st = *state;
   const double std0 = 0.02, stdr = 0.02 / sqrt(2.0 * c.L);
   size_t E = c.E, EE = E * E, Eh = E * (size_t)c.hid;
   oc_randn(params + o.wte, (size_t)c.V * E, &st, std0);
@@ -701,6 +709,7 @@ EXPORT void oc_init(const int* cfg, uint32_t seed, real* params) {
   }
   for (size_t i = 0; i < E; i++) params[o.lnfg + i] = 1;
   if (!c.modern) memset(params + o.lnfb, 0, sizeof(real) * E);
+  *state = st;
 }
 
 /* Per-layer saved activations. */

@@ -1,0 +1,64 @@
+// gemm.cuh -- TF32 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM, TMA-fed).
+#pragma once
+#include "common.cuh"
+
+namespace turt {
+
+// Epilogue variants.  The accumulator tile (fp32, TMEM) is combined with these before
+// it is written; each variant exists to remove one memory-bound pass of the train step.
+enum EpiKind : int {
+  EPI_STORE = 0,       // C = acc
+  EPI_ACCUM = 1,       // C += acc
+  EPI_RED = 2,         // C += acc with atomic adds (split-K partial sums)
+  EPI_ADD_RES = 3,     // C = acc + R            (residual add)
+  EPI_BIAS = 4,        // C = acc + bias[n]
+  EPI_BIAS_GELU = 5,   // C = acc + bias[n] (pre-activation), C2 = gelu(C)
+  EPI_SWIGLU_FWD = 6,  // C = acc (interleaved gate|up pre-activations), C2 = silu(gate) * up
+  EPI_SWIGLU_BWD = 7,  // acc = d(act); R = interleaved gate|up pre-acts; C = interleaved d(gate)|d(up)
+  EPI_GELU_BWD = 8,    // C = acc * gelu'(R)
+};
+
+// Interleave granularity of the fused gate|up weight and activations: columns
+// [64j, 64j+32) hold gate units [32j, 32j+32), columns [64j+32, 64j+64) the matching up units.
+constexpr int kGluBlock = 32;
+
+struct GemmEpi {
+  int kind = EPI_STORE;
+  float* C = nullptr;
+  long ldc = 0;
+  long strideC = 0;  // per batch
+  const float* R = nullptr;
+  long ldr = 0;
+  const float* bias = nullptr;
+  float* C2 = nullptr;
+  long ldc2 = 0;
+};
+
+// Operand description.  `mn_major` = the operand's contiguous dimension is M (for A) or N
+// (for B), i.e. it is stored [K][M] / [K][N]; otherwise it is stored [M][K] / [N][K].
+struct GemmOperand {
+  const float* ptr = nullptr;
+  long ld = 0;      // row pitch in elements
+  long stride = 0;  // batch stride in elements
+  bool mn_major = false;
+};
+
+// Tensor-core precision: plain TF32 (10 mantissa bits per operand) or error-compensated
+// 3xTF32 (three MMAs per k-step on hi/lo operand splits, ~fp32 accuracy).
+enum GemmPrecision : int { GEMM_TF32 = 1, GEMM_TF32X3 = 3 };
+
+// C[M,N] (per batch) = A[M,K] * B[K,N] with the epilogue applied.  K-splits > 1 are chosen
+// automatically for accumulate epilogues when the tile count is below the SM count.
+int gemm_tf32(cudaStream_t stream, int M, int N, int K, int batch, const GemmOperand& A,
+              const GemmOperand& B, const GemmEpi& epi, int* dev_flags, int precision = GEMM_TF32X3,
+              int force_splits = 0);
+
+// True when gemm_tf32 can take these operands (TMA needs 16-byte pitches and bases).
+bool gemm_tf32_supported(const GemmOperand& A, const GemmOperand& B);
+
+// CUDA-core fp32 GEMM for shapes the TMA path cannot address (odd pitches): same
+// flags as the reference's MATMUL kernel (src/infer/webgpu/autograd.ts:33-75).
+int gemm_simt(cudaStream_t stream, const float* A, const float* B, float* C, int M, int K, int N, int batch,
+              bool transA, bool transB, bool accum);
+
+}  // namespace turt

@@ -1,0 +1,615 @@
+// model.cu -- GPU-resident GPT train step (both architectures of src/models/gpt.ts).
+//
+// The reference builds the step as a tape of ~30 dispatches per block
+// (src/models/gpu-gpt.ts:143-201 over src/infer/webgpu/autograd.ts).  Here one block is:
+//   forward : norm1 -> GEMM(qkv) -> attention(+RoPE) -> GEMM(proj, +residual)
+//             -> norm2 -> GEMM(gate|up, SwiGLU epilogue  |  fc, bias+GELU epilogue)
+//             -> GEMM(down|mp, +residual)
+//   backward: GEMM(dact, SwiGLU'/GELU' epilogue) + GEMM(dW) ... norm backward with the
+//             residual gradient fused, attention backward, GEMM(dX) + GEMM(dW)
+// on a flat parameter/gradient buffer so clip, AdamW and the DP all-reduce are single passes.
+//
+// Internal weight layout (the C ABI converts to/from the reference's [in,out] tensors):
+//   Wqkv [E][3E]  = [qW | kW | vW] column blocks     bqkv [3E]
+//   W1   [E][2h]  = gate/up interleaved in 32-column blocks (modern)   |  fcW [E][h] (gpt2)
+//   W2   [h][E]   = downW (modern) | mpW (gpt2)
+// Flat order: wte, wpe, lnf(g,b), then layers 0..L-1 (each contiguous), so the head bucket
+// [0, head_end) and each layer are contiguous ranges for the gradient all-reduce.
+#include <math.h>
+
+#include <string>
+
+#include "attention.cuh"
+#include "gemm.cuh"
+#include "model.cuh"
+#include "model_kernels.cuh"
+#include "ops.cuh"
+
+using namespace turt;
+
+namespace {
+
+size_t align64(size_t x) { return (x + 63) & ~size_t(63); }
+
+int mlp_hidden(const turt_config& c) {
+  if (c.hidden > 0) return c.hidden;
+  if (c.arch == TURT_ARCH_GPT2) return 4 * c.n_embd;
+  // Math.max(64, Math.round((8 * nEmbd) / 3 / 64) * 64), src/models/gpt.ts:96-99
+  double v = floor((8.0 * c.n_embd) / 3.0 / 64.0 + 0.5) * 64.0;
+  return (int)(v < 64 ? 64 : v);
+}
+
+void build_layout(turt_model* m) {
+  const int E = m->cfg.n_embd, V = m->cfg.vocab_size, T = m->cfg.block_size, h = m->hid;
+  size_t p = 0;
+  auto take = [&](size_t n) {
+    size_t o = p;
+    p = align64(p + n);
+    return o;
+  };
+  m->wte = take((size_t)V * E);
+  m->wpe = m->modern ? 0 : take((size_t)T * E);
+  m->lnfg = take(E);
+  m->lnfb = m->modern ? 0 : take(E);
+  m->head_end = p;
+  m->layers.resize(m->cfg.n_layer);
+  for (auto& L : m->layers) {
+    L.begin = p;
+    L.ln1g = take(E);
+    L.ln1b = m->modern ? 0 : take(E);
+    L.wqkv = take((size_t)E * 3 * E);
+    L.bqkv = m->modern ? 0 : take(3 * E);
+    L.wproj = take((size_t)E * E);
+    L.bproj = m->modern ? 0 : take(E);
+    L.ln2g = take(E);
+    L.ln2b = m->modern ? 0 : take(E);
+    L.w1 = take((size_t)E * (m->modern ? 2 * h : h));
+    L.b1 = m->modern ? 0 : take(h);
+    L.w2 = take((size_t)h * E);
+    L.b2 = m->modern ? 0 : take(E);
+    L.end = p;
+  }
+  m->total = p;
+
+  // parameters() order (src/models/gpu-gpt.ts:118-132) -> slots
+  auto contig = [](const std::string& n, int r, int c, size_t off) {
+    ParamSlot s;
+    s.name = n;
+    s.shape[0] = r;
+    s.shape[1] = c;
+    s.ndim = c ? 2 : 1;
+    s.off = off;
+    s.width = c ? r * c : r;
+    s.rows = 1;
+    s.pitch = s.width;
+    return s;
+  };
+  auto block2d = [](const std::string& n, int r, int c, size_t off, int width, long rows, int pitch) {
+    ParamSlot s;
+    s.name = n;
+    s.shape[0] = r;
+    s.shape[1] = c;
+    s.ndim = 2;
+    s.off = off;
+    s.width = width;
+    s.rows = rows;
+    s.pitch = pitch;
+    return s;
+  };
+  auto& P = m->params;
+  P.clear();
+  P.push_back(contig("wte", V, E, m->wte));
+  if (!m->modern) P.push_back(contig("wpe", T, E, m->wpe));
+  for (int l = 0; l < m->cfg.n_layer; l++) {
+    const LayerOff& L = m->layers[l];
+    const std::string b = "blk" + std::to_string(l) + ".";
+    P.push_back(contig(b + "ln1g", E, 0, L.ln1g));
+    if (!m->modern) P.push_back(contig(b + "ln1b", E, 0, L.ln1b));
+    P.push_back(block2d(b + "qW", E, E, L.wqkv, E, E, 3 * E));
+    if (!m->modern) P.push_back(contig(b + "qb", E, 0, L.bqkv));
+    P.push_back(block2d(b + "kW", E, E, L.wqkv + E, E, E, 3 * E));
+    if (!m->modern) P.push_back(contig(b + "kb", E, 0, L.bqkv + E));
+    P.push_back(block2d(b + "vW", E, E, L.wqkv + 2 * E, E, E, 3 * E));
+    if (!m->modern) P.push_back(contig(b + "vb", E, 0, L.bqkv + 2 * E));
+    P.push_back(contig(b + "projW", E, E, L.wproj));
+    if (!m->modern) P.push_back(contig(b + "projb", E, 0, L.bproj));
+    P.push_back(contig(b + "ln2g", E, 0, L.ln2g));
+    if (!m->modern) P.push_back(contig(b + "ln2b", E, 0, L.ln2b));
+    if (m->modern) {
+      const long rows = (long)E * h / kGluBlock;
+      P.push_back(block2d(b + "gateW", E, h, L.w1, kGluBlock, rows, 2 * kGluBlock));
+      P.push_back(block2d(b + "upW", E, h, L.w1 + kGluBlock, kGluBlock, rows, 2 * kGluBlock));
+      P.push_back(contig(b + "downW", h, E, L.w2));
+    } else {
+      P.push_back(contig(b + "fcW", E, h, L.w1));
+      P.push_back(contig(b + "fcb", h, 0, L.b1));
+      P.push_back(contig(b + "mpW", h, E, L.w2));
+      P.push_back(contig(b + "mpb", E, 0, L.b2));
+    }
+  }
+  P.push_back(contig("lnfg", E, 0, m->lnfg));
+  if (!m->modern) P.push_back(contig("lnfb", E, 0, m->lnfb));
+}
+
+void free_workspace(turt_model* m) {
+  if (m->ws) cudaFree(m->ws);
+  m->ws = nullptr;
+  m->capN = 0;
+  m->act.clear();
+}
+
+// Carves every activation / scratch buffer for N = B*T tokens out of one allocation.
+int ensure_workspace(turt_model* m, int B, int T) {
+  const int N = B * T;
+  if (N <= m->capN && B * m->cfg.n_head * T <= m->capB) return OK;
+  free_workspace(m);
+  const int E = m->cfg.n_embd, H = m->cfg.n_head, V = m->cfg.vocab_size, h = m->hid, Lc = m->cfg.n_layer;
+  const int W1 = m->modern ? 2 * h : h;
+  size_t off = 0;
+  std::vector<size_t*> dummy;
+  auto take = [&](size_t n) {
+    size_t o = off;
+    off += (n * 4 + 255) & ~size_t(255);
+    return o;
+  };
+  struct LA {
+    size_t x, y1, rs1, mu1, qkv, att, lse, h, y2, rs2, mu2, pre, act;
+  };
+  std::vector<LA> la(Lc);
+  const size_t NE = (size_t)N * E, BHT = (size_t)B * H * T;
+  for (int l = 0; l < Lc; l++) {
+    LA& a = la[l];
+    a.x = take(NE);
+    a.y1 = take(NE);
+    a.rs1 = take(N);
+    a.mu1 = m->modern ? 0 : take(N);
+    a.qkv = take(3 * NE);
+    a.att = take(NE);
+    a.lse = take(BHT);
+    a.h = take(NE);
+    a.y2 = take(NE);
+    a.rs2 = take(N);
+    a.mu2 = m->modern ? 0 : take(N);
+    a.pre = take((size_t)N * W1);
+    a.act = take((size_t)N * h);
+  }
+  size_t xL = take(NE), yf = take(NE), rsf = take(N), muf = take(N);
+  size_t logits = take((size_t)N * V), loss_rows = take(N);
+  size_t dx = take(NE), dy = take(NE), datt = take(NE), dqkv = take(3 * NE), dpre = take((size_t)N * W1);
+  size_t Dsc = take(BHT);
+  const int C = 3 * E > W1 ? 3 * E : W1;
+  size_t part = take((size_t)2 * norm_parts(N) * (C > E ? C : E));
+  size_t ids = take(N), tgt = take(N);
+  void* ws = nullptr;
+  TURT_CHECK_CUDA(cudaMalloc(&ws, off));
+  m->ws = ws;
+  char* base = static_cast<char*>(ws);
+  auto F = [&](size_t o) { return reinterpret_cast<float*>(base + o); };
+  m->act.resize(Lc);
+  for (int l = 0; l < Lc; l++) {
+    LA& a = la[l];
+    LayerAct& A = m->act[l];
+    A.x = F(a.x);
+    A.y1 = F(a.y1);
+    A.rs1 = F(a.rs1);
+    A.mu1 = m->modern ? nullptr : F(a.mu1);
+    A.qkv = F(a.qkv);
+    A.att = F(a.att);
+    A.lse = F(a.lse);
+    A.h = F(a.h);
+    A.y2 = F(a.y2);
+    A.rs2 = F(a.rs2);
+    A.mu2 = m->modern ? nullptr : F(a.mu2);
+    A.pre = F(a.pre);
+    A.act = F(a.act);
+  }
+  m->xL = F(xL);
+  m->yf = F(yf);
+  m->rsf = F(rsf);
+  m->muf = F(muf);
+  m->logits = F(logits);
+  m->loss_rows = F(loss_rows);
+  m->dx = F(dx);
+  m->dy = F(dy);
+  m->datt = F(datt);
+  m->dqkv = F(dqkv);
+  m->dpre = F(dpre);
+  m->Dsc = F(Dsc);
+  m->part = F(part);
+  m->d_ids = reinterpret_cast<uint32_t*>(base + ids);
+  m->d_tgt = reinterpret_cast<uint32_t*>(base + tgt);
+  if (m->h_ids) cudaFreeHost(m->h_ids);
+  if (m->h_tgt) cudaFreeHost(m->h_tgt);
+  TURT_CHECK_CUDA(cudaMallocHost(&m->h_ids, (size_t)N * 4));
+  TURT_CHECK_CUDA(cudaMallocHost(&m->h_tgt, (size_t)N * 4));
+  m->capN = N;
+  m->capB = B * H * T;
+  return OK;
+}
+
+// ---------------------------------------------------------------- GEMM helpers
+inline GemmOperand opK(const float* p, long ld) { return GemmOperand{p, ld, 0, false}; }   // stored [rows][K]
+inline GemmOperand opMN(const float* p, long ld) { return GemmOperand{p, ld, 0, true}; }  // stored [K][rows]
+inline GemmEpi epi(int kind, float* C, long ldc) {
+  GemmEpi e;
+  e.kind = kind;
+  e.C = C;
+  e.ldc = ldc;
+  return e;
+}
+
+#define RC(x)          \
+  do {                 \
+    int rc__ = (x);    \
+    if (rc__) return rc__; \
+  } while (0)
+
+int stage_tokens(turt_model* m, const uint32_t* ids, const uint32_t* tgt, int N) {
+  cudaStream_t st = m->ctx->stream;
+  // Copy through pinned staging so the H2D transfer is a true async DMA on the stream.
+  TURT_CHECK_CUDA(cudaStreamSynchronize(st));
+  memcpy(m->h_ids, ids, (size_t)N * 4);
+  memcpy(m->h_tgt, tgt, (size_t)N * 4);
+  TURT_CHECK_CUDA(cudaMemcpyAsync(m->d_ids, m->h_ids, (size_t)N * 4, cudaMemcpyHostToDevice, st));
+  TURT_CHECK_CUDA(cudaMemcpyAsync(m->d_tgt, m->h_tgt, (size_t)N * 4, cudaMemcpyHostToDevice, st));
+  return OK;
+}
+
+int forward(turt_model* m, int B, int T, bool train, float loss_scale) {
+  cudaStream_t st = m->ctx->stream;
+  int* flags = m->ctx->flags;
+  const int N = B * T, E = m->cfg.n_embd, H = m->cfg.n_head, hd = E / H, V = m->cfg.vocab_size, h = m->hid;
+  const float* P = m->P;
+  RC(embed_fwd(st, P + m->wte, m->modern ? nullptr : P + m->wpe, m->d_ids, m->act.empty() ? m->xL : m->act[0].x, N, T,
+               E, V, flags));
+  for (int l = 0; l < m->cfg.n_layer; l++) {
+    const LayerOff& L = m->layers[l];
+    LayerAct& a = m->act[l];
+    float* xnext = (l + 1 < m->cfg.n_layer) ? m->act[l + 1].x : m->xL;
+    if (m->modern)
+      RC(rms_fwd(st, a.x, P + L.ln1g, a.y1, a.rs1, N, E, m->eps));
+    else
+      RC(ln_fwd(st, a.x, P + L.ln1g, P + L.ln1b, a.y1, a.mu1, a.rs1, N, E, m->eps));
+    GemmEpi e = epi(m->modern ? EPI_STORE : EPI_BIAS, a.qkv, 3 * E);
+    if (!m->modern) e.bias = P + L.bqkv;
+    RC(gemm_tf32(st, N, 3 * E, E, 1, opK(a.y1, E), opMN(P + L.wqkv, 3 * E), e, flags, m->ctx->precision));
+    RC(attention_fwd(st, a.qkv, m->rope_cs, a.att, a.lse, B, T, H, hd, m->modern ? 1 : 0));
+    e = epi(EPI_ADD_RES, a.h, E);
+    e.R = a.x;
+    e.ldr = E;
+    if (!m->modern) e.bias = P + L.bproj;
+    RC(gemm_tf32(st, N, E, E, 1, opK(a.att, E), opMN(P + L.wproj, E), e, flags, m->ctx->precision));
+    if (m->modern)
+      RC(rms_fwd(st, a.h, P + L.ln2g, a.y2, a.rs2, N, E, m->eps));
+    else
+      RC(ln_fwd(st, a.h, P + L.ln2g, P + L.ln2b, a.y2, a.mu2, a.rs2, N, E, m->eps));
+    if (m->modern) {
+      e = epi(EPI_SWIGLU_FWD, a.pre, 2 * h);
+      e.C2 = a.act;
+      e.ldc2 = h;
+      RC(gemm_tf32(st, N, 2 * h, E, 1, opK(a.y2, E), opMN(P + L.w1, 2 * h), e, flags, m->ctx->precision));
+    } else {
+      e = epi(EPI_BIAS_GELU, a.pre, h);
+      e.bias = P + L.b1;
+      e.C2 = a.act;
+      e.ldc2 = h;
+      RC(gemm_tf32(st, N, h, E, 1, opK(a.y2, E), opMN(P + L.w1, h), e, flags, m->ctx->precision));
+    }
+    e = epi(EPI_ADD_RES, xnext, E);
+    e.R = a.h;
+    e.ldr = E;
+    if (!m->modern) e.bias = P + L.b2;
+    RC(gemm_tf32(st, N, E, h, 1, opK(a.act, h), opMN(P + L.w2, E), e, flags, m->ctx->precision));
+  }
+  if (m->modern)
+    RC(rms_fwd(st, m->xL, P + m->lnfg, m->yf, m->rsf, N, E, m->eps));
+  else
+    RC(ln_fwd(st, m->xL, P + m->lnfg, P + m->lnfb, m->yf, m->muf, m->rsf, N, E, m->eps));
+  // tied head: logits = yf * wte^T (wte [V][E] is the K-major B operand)
+  RC(gemm_tf32(st, N, V, E, 1, opK(m->yf, E), opK(P + m->wte, E), epi(EPI_STORE, m->logits, V), flags, m->ctx->precision));
+  if (train)
+    RC(ce_fused(st, m->logits, m->d_tgt, m->loss_rows, N, V, loss_scale / (float)N, flags));
+  else
+    RC(ce_loss(st, m->logits, m->d_tgt, m->loss_rows, N, V, flags));
+  RC(loss_mean(st, m->loss_rows, N, m->loss_dev, flags));
+  return OK;
+}
+
+int backward(turt_model* m, int B, int T) {
+  cudaStream_t st = m->ctx->stream;
+  int* flags = m->ctx->flags;
+  const int N = B * T, E = m->cfg.n_embd, H = m->cfg.n_head, hd = E / H, V = m->cfg.vocab_size, h = m->hid;
+  const float* P = m->P;
+  float* G = m->G;
+  // head: dyf = dlogits * wte ; dwte += dlogits^T * yf
+  RC(gemm_tf32(st, N, E, V, 1, opK(m->logits, V), opMN(P + m->wte, E), epi(EPI_STORE, m->dy, E), flags, m->ctx->precision));
+  RC(gemm_tf32(st, V, E, N, 1, opMN(m->logits, V), opMN(m->yf, E), epi(EPI_ACCUM, G + m->wte, E), flags, m->ctx->precision));
+  if (m->modern)
+    RC(rms_bwd(st, m->xL, m->dy, P + m->lnfg, m->rsf, nullptr, m->dx, G + m->lnfg, m->part, N, E));
+  else
+    RC(ln_bwd(st, m->xL, m->dy, P + m->lnfg, m->muf, m->rsf, nullptr, m->dx, G + m->lnfg, G + m->lnfb, m->part, N, E));
+  for (int l = m->cfg.n_layer - 1; l >= 0; l--) {
+    const LayerOff& L = m->layers[l];
+    LayerAct& a = m->act[l];
+    // ---- MLP
+    if (m->modern) {
+      GemmEpi e = epi(EPI_SWIGLU_BWD, m->dpre, 2 * h);
+      e.R = a.pre;
+      e.ldr = 2 * h;
+      RC(gemm_tf32(st, N, h, E, 1, opK(m->dx, E), opK(P + L.w2, E), e, flags, m->ctx->precision));
+      RC(gemm_tf32(st, h, E, N, 1, opMN(a.act, h), opMN(m->dx, E), epi(EPI_ACCUM, G + L.w2, E), flags, m->ctx->precision));
+      RC(gemm_tf32(st, N, E, 2 * h, 1, opK(m->dpre, 2 * h), opK(P + L.w1, 2 * h), epi(EPI_STORE, m->dy, E), flags, m->ctx->precision));
+      RC(gemm_tf32(st, E, 2 * h, N, 1, opMN(a.y2, E), opMN(m->dpre, 2 * h), epi(EPI_ACCUM, G + L.w1, 2 * h), flags, m->ctx->precision));
+    } else {
+      GemmEpi e = epi(EPI_GELU_BWD, m->dpre, h);
+      e.R = a.pre;
+      e.ldr = h;
+      RC(gemm_tf32(st, N, h, E, 1, opK(m->dx, E), opK(P + L.w2, E), e, flags, m->ctx->precision));
+      RC(gemm_tf32(st, h, E, N, 1, opMN(a.act, h), opMN(m->dx, E), epi(EPI_ACCUM, G + L.w2, E), flags, m->ctx->precision));
+      RC(colsum_accum(st, m->dx, N, E, G + L.b2, m->part));
+      RC(gemm_tf32(st, N, E, h, 1, opK(m->dpre, h), opK(P + L.w1, h), epi(EPI_STORE, m->dy, E), flags, m->ctx->precision));
+      RC(gemm_tf32(st, E, h, N, 1, opMN(a.y2, E), opMN(m->dpre, h), epi(EPI_ACCUM, G + L.w1, h), flags, m->ctx->precision));
+      RC(colsum_accum(st, m->dpre, N, h, G + L.b1, m->part));
+    }
+    if (m->modern)
+      RC(rms_bwd(st, a.h, m->dy, P + L.ln2g, a.rs2, m->dx, m->dx, G + L.ln2g, m->part, N, E));
+    else
+      RC(ln_bwd(st, a.h, m->dy, P + L.ln2g, a.mu2, a.rs2, m->dx, m->dx, G + L.ln2g, G + L.ln2b, m->part, N, E));
+    // ---- attention
+    RC(gemm_tf32(st, N, E, E, 1, opK(m->dx, E), opK(P + L.wproj, E), epi(EPI_STORE, m->datt, E), flags, m->ctx->precision));
+    RC(gemm_tf32(st, E, E, N, 1, opMN(a.att, E), opMN(m->dx, E), epi(EPI_ACCUM, G + L.wproj, E), flags, m->ctx->precision));
+    if (!m->modern) RC(colsum_accum(st, m->dx, N, E, G + L.bproj, m->part));
+    RC(attention_bwd(st, a.qkv, m->rope_cs, a.att, m->datt, a.lse, m->Dsc, m->dqkv, B, T, H, hd, m->modern ? 1 : 0));
+    if (!m->modern) RC(colsum_accum(st, m->dqkv, N, 3 * E, G + L.bqkv, m->part));
+    RC(gemm_tf32(st, N, E, 3 * E, 1, opK(m->dqkv, 3 * E), opK(P + L.wqkv, 3 * E), epi(EPI_STORE, m->dy, E), flags, m->ctx->precision));
+    RC(gemm_tf32(st, E, 3 * E, N, 1, opMN(a.y1, E), opMN(m->dqkv, 3 * E), epi(EPI_ACCUM, G + L.wqkv, 3 * E), flags, m->ctx->precision));
+    if (m->modern)
+      RC(rms_bwd(st, a.x, m->dy, P + L.ln1g, a.rs1, m->dx, m->dx, G + L.ln1g, m->part, N, E));
+    else
+      RC(ln_bwd(st, a.x, m->dy, P + L.ln1g, a.mu1, a.rs1, m->dx, m->dx, G + L.ln1g, G + L.ln1b, m->part, N, E));
+    if (dp_active(m) && !m->dp_defer) RC(dp_after_layer(m, l));
+  }
+  RC(embed_bwd(st, m->dx, m->d_ids, G + m->wte, m->modern ? nullptr : G + m->wpe, N, T, E, V));
+  if (dp_active(m) && !m->dp_defer) {
+    RC(dp_after_head(m));
+    RC(dp_finish(m));
+  }
+  return OK;
+}
+
+int read_loss(turt_model* m, float* loss_out) {
+  if (!loss_out) return OK;
+  TURT_CHECK_CUDA(cudaMemcpyAsync(m->h_loss, m->loss_dev, 4, cudaMemcpyDeviceToHost, m->ctx->stream));
+  int rc = ctx_check_flags(m->ctx);  // synchronizes
+  *loss_out = *m->h_loss;
+  return rc;
+}
+
+int check_batch(turt_model* m, const uint32_t* ids, const uint32_t* tgt, int b, int t) {
+  TURT_REQUIRE(m && ids && tgt, "null model or token array");
+  TURT_REQUIRE(b > 0 && t > 0, "batch and time must be positive");
+  if (t > m->cfg.block_size) {
+    set_error("Sequence length " + std::to_string(t) + " exceeds block size " + std::to_string(m->cfg.block_size));
+    return ERR_INVALID;
+  }
+  return OK;
+}
+
+}  // namespace
+
+#define MODEL_GUARD(m)                                   \
+  do {                                                   \
+    if (!(m)) {                                          \
+      set_error("null model");                           \
+      return ERR_INVALID;                                \
+    }                                                    \
+    TURT_CHECK_CUDA(cudaSetDevice((m)->ctx->device));    \
+  } while (0)
+
+extern "C" {
+
+int turt_model_create(turt_ctx* ctx, const turt_config* cfg, turt_model** out) {
+  TURT_REQUIRE(ctx && cfg && out, "turt_model_create: null argument");
+  TURT_REQUIRE(cfg->vocab_size > 0 && cfg->block_size > 0 && cfg->n_layer > 0 && cfg->n_head > 0 && cfg->n_embd > 0,
+               "turt_model_create: non-positive dimension");
+  if (cfg->n_embd % cfg->n_head != 0) {
+    set_error("nEmbd (" + std::to_string(cfg->n_embd) + ") must be divisible by nHead (" +
+              std::to_string(cfg->n_head) + ")");
+    return ERR_INVALID;
+  }
+  TURT_REQUIRE(cfg->arch == TURT_ARCH_GPT2 || cfg->arch == TURT_ARCH_MODERN, "arch must be gpt2 (0) or modern (1)");
+  const int hd = cfg->n_embd / cfg->n_head;
+  if (!attention_supported_hd(hd)) {
+    set_error("head dim " + std::to_string(hd) + " not supported (16, 32 or 64)");
+    return ERR_UNSUPPORTED;
+  }
+  TURT_REQUIRE(cfg->n_embd % 32 == 0 && cfg->n_embd <= 1024, "nEmbd must be a multiple of 32, at most 1024");
+  TURT_REQUIRE(cfg->vocab_size % 4 == 0, "vocab size must be a multiple of 4");
+  TURT_CHECK_CUDA(cudaSetDevice(ctx->device));
+  turt_model* m = new turt_model();
+  m->ctx = ctx;
+  m->cfg = *cfg;
+  m->modern = cfg->arch == TURT_ARCH_MODERN;
+  m->hid = mlp_hidden(*cfg);
+  if (m->hid % kGluBlock != 0) {
+    delete m;
+    set_error("MLP hidden width must be a multiple of 32");
+    return ERR_UNSUPPORTED;
+  }
+  build_layout(m);
+  const size_t bytes = m->total * 4;
+  TURT_CHECK_CUDA(cudaMalloc(&m->P, bytes));
+  TURT_CHECK_CUDA(cudaMalloc(&m->G, bytes));
+  TURT_CHECK_CUDA(cudaMalloc(&m->M, bytes));
+  TURT_CHECK_CUDA(cudaMalloc(&m->V, bytes));
+  cudaStream_t st = ctx->stream;
+  TURT_CHECK_CUDA(cudaMemsetAsync(m->P, 0, bytes, st));
+  TURT_CHECK_CUDA(cudaMemsetAsync(m->G, 0, bytes, st));
+  TURT_CHECK_CUDA(cudaMemsetAsync(m->M, 0, bytes, st));
+  TURT_CHECK_CUDA(cudaMemsetAsync(m->V, 0, bytes, st));
+  // gains start at 1 (src/nn/rmsnorm.ts:21, layernorm.ts:22); weights arrive via turt_param_upload
+  const int E = cfg->n_embd;
+  op_fill(st, m->P + m->lnfg, 1.0f, E);
+  for (auto& L : m->layers) {
+    op_fill(st, m->P + L.ln1g, 1.0f, E);
+    op_fill(st, m->P + L.ln2g, 1.0f, E);
+  }
+  const int hdim = E / cfg->n_head;
+  TURT_CHECK_CUDA(cudaMalloc(&m->rope_cs, sizeof(float2) * (size_t)cfg->block_size * (hdim / 2) + 16));
+  RC(op_rope_table(st, m->rope_cs, cfg->block_size, hdim, 10000.0));
+  TURT_CHECK_CUDA(cudaMalloc(&m->loss_dev, 16));
+  TURT_CHECK_CUDA(cudaMalloc(&m->coef_dev, 16));
+  TURT_CHECK_CUDA(cudaMalloc(&m->norm_dev, 16));
+  TURT_CHECK_CUDA(cudaMalloc(&m->norm_scratch, sizeof(double) * norm_scratch_doubles()));
+  TURT_CHECK_CUDA(cudaMallocHost(&m->h_loss, 16));
+  TURT_CHECK_CUDA(cudaStreamSynchronize(st));
+  *out = m;
+  return OK;
+}
+
+int turt_model_destroy(turt_model* m) {
+  MODEL_GUARD(m);
+  cudaStreamSynchronize(m->ctx->stream);
+  if (m->dp) turt_dp_destroy(m);
+  free_workspace(m);
+  cudaFree(m->P);
+  cudaFree(m->G);
+  cudaFree(m->M);
+  cudaFree(m->V);
+  cudaFree(m->rope_cs);
+  cudaFree(m->loss_dev);
+  cudaFree(m->coef_dev);
+  cudaFree(m->norm_dev);
+  cudaFree(m->norm_scratch);
+  cudaFreeHost(m->h_loss);
+  if (m->h_ids) cudaFreeHost(m->h_ids);
+  if (m->h_tgt) cudaFreeHost(m->h_tgt);
+  delete m;
+  return OK;
+}
+
+int turt_param_count(turt_model* m, int* count) {
+  MODEL_GUARD(m);
+  *count = (int)m->params.size();
+  return OK;
+}
+
+int turt_num_params(turt_model* m, size_t* total) {
+  MODEL_GUARD(m);
+  size_t s = 0;
+  for (auto& p : m->params) s += p.count();
+  *total = s;
+  return OK;
+}
+
+int turt_param_info(turt_model* m, int i, char* name, int cap, int* shape2, int* ndim) {
+  MODEL_GUARD(m);
+  TURT_REQUIRE(i >= 0 && i < (int)m->params.size(), "param index out of range");
+  const ParamSlot& s = m->params[i];
+  if (name && cap > 0) {
+    snprintf(name, cap, "%s", s.name.c_str());
+  }
+  if (shape2) {
+    shape2[0] = s.shape[0];
+    shape2[1] = s.shape[1];
+  }
+  if (ndim) *ndim = s.ndim;
+  return OK;
+}
+
+static int copy_param(turt_model* m, int i, float* host, size_t n, bool up, bool grad) {
+  MODEL_GUARD(m);
+  TURT_REQUIRE(i >= 0 && i < (int)m->params.size(), "param index out of range");
+  const ParamSlot& s = m->params[i];
+  if (n != s.count()) {
+    set_error("param " + std::to_string(i) + " size mismatch: expected " + std::to_string(s.count()) + ", got " +
+              std::to_string(n));
+    return ERR_INVALID;
+  }
+  float* dev = (grad ? m->G : m->P) + s.off;
+  cudaStream_t st = m->ctx->stream;
+  if (up)
+    TURT_CHECK_CUDA(cudaMemcpy2DAsync(dev, (size_t)s.pitch * 4, host, (size_t)s.width * 4, (size_t)s.width * 4, s.rows,
+                                      cudaMemcpyHostToDevice, st));
+  else
+    TURT_CHECK_CUDA(cudaMemcpy2DAsync(host, (size_t)s.width * 4, dev, (size_t)s.pitch * 4, (size_t)s.width * 4, s.rows,
+                                      cudaMemcpyDeviceToHost, st));
+  TURT_CHECK_CUDA(cudaStreamSynchronize(st));
+  return OK;
+}
+
+int turt_param_upload(turt_model* m, int i, const float* host, size_t n) {
+  return copy_param(m, i, const_cast<float*>(host), n, true, false);
+}
+int turt_param_download(turt_model* m, int i, float* host, size_t n) { return copy_param(m, i, host, n, false, false); }
+int turt_grad_download(turt_model* m, int i, float* host, size_t n) { return copy_param(m, i, host, n, false, true); }
+
+int turt_zero_grad(turt_model* m) {
+  MODEL_GUARD(m);
+  TURT_CHECK_CUDA(cudaMemsetAsync(m->G, 0, m->total * 4, m->ctx->stream));
+  return OK;
+}
+
+int turt_forward_backward(turt_model* m, const uint32_t* ids, const uint32_t* tgt, int b, int t, float loss_scale,
+                          float* loss_out) {
+  MODEL_GUARD(m);
+  RC(check_batch(m, ids, tgt, b, t));
+  RC(ensure_workspace(m, b, t));
+  RC(stage_tokens(m, ids, tgt, b * t));
+  RC(forward(m, b, t, true, loss_scale));
+  RC(backward(m, b, t));
+  return read_loss(m, loss_out);
+}
+
+int turt_forward_backward_device(turt_model* m, const uint32_t* d_ids, const uint32_t* d_tgt, int b, int t,
+                                 float loss_scale) {
+  MODEL_GUARD(m);
+  RC(check_batch(m, d_ids, d_tgt, b, t));
+  RC(ensure_workspace(m, b, t));
+  cudaStream_t st = m->ctx->stream;
+  TURT_CHECK_CUDA(cudaMemcpyAsync(m->d_ids, d_ids, (size_t)b * t * 4, cudaMemcpyDeviceToDevice, st));
+  TURT_CHECK_CUDA(cudaMemcpyAsync(m->d_tgt, d_tgt, (size_t)b * t * 4, cudaMemcpyDeviceToDevice, st));
+  RC(forward(m, b, t, true, loss_scale));
+  return backward(m, b, t);
+}
+
+int turt_read_loss(turt_model* m, float* loss_out) {
+  MODEL_GUARD(m);
+  TURT_REQUIRE(loss_out, "null loss_out");
+  return read_loss(m, loss_out);
+}
+
+int turt_forward(turt_model* m, const uint32_t* ids, const uint32_t* tgt, int b, int t, float* loss_out) {
+  MODEL_GUARD(m);
+  RC(check_batch(m, ids, tgt, b, t));
+  RC(ensure_workspace(m, b, t));
+  RC(stage_tokens(m, ids, tgt, b * t));
+  RC(forward(m, b, t, false, 1.0f));
+  return read_loss(m, loss_out);
+}
+
+int turt_clip_grad_norm(turt_model* m, double max_norm, double* norm_out) {
+  MODEL_GUARD(m);
+  cudaStream_t st = m->ctx->stream;
+  RC(grad_norm(st, m->G, m->total, 1.0f, (float)max_norm, m->norm_scratch, m->norm_dev, m->coef_dev, m->ctx->flags));
+  RC(scale_by(st, m->G, m->total, m->coef_dev, 1.0f));
+  if (norm_out) {
+    TURT_CHECK_CUDA(cudaMemcpyAsync(norm_out, m->norm_dev, 8, cudaMemcpyDeviceToHost, st));
+    TURT_CHECK_CUDA(cudaStreamSynchronize(st));
+  }
+  return OK;
+}
+
+int turt_adamw_step(turt_model* m, float lr, float b1, float b2, float eps, float wd, float bc1, float bc2, float clip,
+                    float grad_scale) {
+  MODEL_GUARD(m);
+  cudaStream_t st = m->ctx->stream;
+  const float* coef = nullptr;
+  if (clip > 0.f) {
+    RC(grad_norm(st, m->G, m->total, grad_scale, clip, m->norm_scratch, m->norm_dev, m->coef_dev, m->ctx->flags));
+    coef = m->coef_dev;
+  }
+  return adamw_flat(st, m->P, m->G, m->M, m->V, m->total, lr, b1, b2, eps, wd, bc1, bc2, grad_scale, coef);
+}
+
+}  // extern "C"

@@ -1,0 +1,74 @@
+// model.cuh -- the GPT model object behind turt_model*.
+#pragma once
+#include <string>
+#include <vector>
+
+#include "../../include/turt_cuda.h"
+#include "ctx.cuh"
+
+namespace turt {
+
+// Where one reference parameter (parameters() order) lives in the internal flat buffer:
+// `rows` runs of `width` floats, `pitch` floats apart, starting at `off`.
+struct ParamSlot {
+  std::string name;
+  int shape[2];
+  int ndim;
+  size_t off;
+  int width;
+  long rows;
+  int pitch;
+  size_t count() const { return (size_t)width * rows; }
+};
+
+struct LayerOff {
+  size_t ln1g, ln1b, wqkv, bqkv, wproj, bproj, ln2g, ln2b, w1, b1, w2, b2;
+  size_t begin, end;  // [begin, end) range of this layer in the flat buffer
+};
+
+struct LayerAct {
+  float *x, *y1, *rs1, *mu1, *qkv, *att, *lse, *h, *y2, *rs2, *mu2, *pre, *act;
+};
+
+struct DpState;
+
+}  // namespace turt
+
+struct turt_model {
+  turt_ctx* ctx = nullptr;
+  turt_config cfg{};
+  int hid = 0;
+  bool modern = true;
+  float eps = 1e-5f;
+  // flat buffers (internal layout), 256-byte aligned tensors
+  size_t total = 0;
+  float *P = nullptr, *G = nullptr, *M = nullptr, *V = nullptr;
+  size_t wte = 0, wpe = 0, lnfg = 0, lnfb = 0, head_end = 0;
+  std::vector<turt::LayerOff> layers;
+  std::vector<turt::ParamSlot> params;
+  float2* rope_cs = nullptr;
+  // workspace for the current token capacity
+  int capN = 0, capB = 0;
+  void* ws = nullptr;
+  std::vector<turt::LayerAct> act;
+  float *xL = nullptr, *yf = nullptr, *rsf = nullptr, *muf = nullptr, *logits = nullptr, *loss_rows = nullptr;
+  float *dx = nullptr, *dy = nullptr, *datt = nullptr, *dqkv = nullptr, *dpre = nullptr, *Dsc = nullptr,
+        *part = nullptr;
+  uint32_t *d_ids = nullptr, *d_tgt = nullptr;
+  uint32_t *h_ids = nullptr, *h_tgt = nullptr;  // pinned staging
+  float* loss_dev = nullptr;
+  float* coef_dev = nullptr;
+  double* norm_dev = nullptr;
+  double* norm_scratch = nullptr;
+  float* h_loss = nullptr;  // pinned
+  turt::DpState* dp = nullptr;
+  bool dp_defer = false;
+};
+
+namespace turt {
+// DP hooks called by the backward pass (dp.cu).
+int dp_after_layer(turt_model* m, int layer);
+int dp_after_head(turt_model* m);
+int dp_finish(turt_model* m);  // compute stream waits for outstanding reductions
+bool dp_active(turt_model* m);
+}  // namespace turt

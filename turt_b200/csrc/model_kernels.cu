@@ -1,0 +1,615 @@
+// model_kernels.cu -- fused memory-bound kernels of the train step (model path).
+// Each kernel replaces a run of reference dispatches (src/infer/webgpu/autograd.ts) with
+// one coalesced pass: 128-bit loads where rows allow, one warp per row, warp-shuffle
+// reductions, and deterministic two-stage column reductions for parameter gradients.
+#include "model_kernels.cuh"
+
+namespace turt {
+namespace {
+
+#define GRID_STRIDE(i, n) \
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < (n); i += (size_t)gridDim.x * blockDim.x)
+
+// ------------------------------------------------------------- embedding
+// x[n,:] = wte[ids[n],:] (+ wpe[n % T,:]); GATHER (+EWISE add), autograd.ts:416-425.
+__global__ void k_embed(const float* __restrict__ wte, const float* __restrict__ wpe, const uint32_t* __restrict__ ids,
+                        float* __restrict__ x, int N, int T, int E, int V, int* flags) {
+  const int e4 = E / 4;
+  GRID_STRIDE(i, (size_t)N * e4) {
+    const int n = (int)(i / e4), c = (int)(i % e4);
+    uint32_t id = ids[n];
+    if (id >= (uint32_t)V) {
+      atomicExch(&flags[FLAG_RANGE], 1);
+      id = 0;
+    }
+    float4 v = reinterpret_cast<const float4*>(wte + (size_t)id * E)[c];
+    if (wpe) {
+      const float4 p = reinterpret_cast<const float4*>(wpe + (size_t)(n % T) * E)[c];
+      v.x += p.x;
+      v.y += p.y;
+      v.z += p.z;
+      v.w += p.w;
+    }
+    reinterpret_cast<float4*>(x + (size_t)n * E)[c] = v;
+  }
+}
+
+// dwte[ids[n],:] += dx[n,:] (and dwpe[n % T,:] += dx[n,:]); GATHER_BWD, autograd.ts:428-438,
+// as atomics over the N*E gradient elements instead of the reference's O(V*N) scan.
+__global__ void k_embed_bwd(const float* __restrict__ dx, const uint32_t* __restrict__ ids, float* __restrict__ dwte,
+                            float* __restrict__ dwpe, int N, int T, int E, int V) {
+  GRID_STRIDE(i, (size_t)N * E) {
+    const int n = (int)(i / E), c = (int)(i % E);
+    const uint32_t id = ids[n];
+    const float g = dx[i];
+    if (id < (uint32_t)V) atomicAdd(dwte + (size_t)id * E + c, g);
+    if (dwpe) atomicAdd(dwpe + (size_t)(n % T) * E + c, g);
+  }
+}
+
+// ------------------------------------------------------------------ norms
+// One warp per row; E/32 values per lane kept in registers (E <= 32*MAXV).
+constexpr int MAXV = 32;  // E <= 1024
+
+// RMSNorm forward: y = x * rs * g, rs = (mean(x^2) + eps)^-1/2 (autograd.ts:315-330).
+__global__ void k_rms_fwd(const float* __restrict__ x, const float* __restrict__ g, float* __restrict__ y,
+                          float* __restrict__ rstd, int rows, int E, float eps) {
+  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* xr = x + (size_t)row * E;
+  float v[MAXV];
+  float ss = 0.f;
+  const int nv = E / 32;
+#pragma unroll
+  for (int k = 0; k < MAXV; k++)
+    if (k < nv) {
+      v[k] = xr[k * 32 + lane];
+      ss += v[k] * v[k];
+    }
+  ss = warp_sum(ss);
+  const float rs = rsqrtf(ss / E + eps);
+  if (lane == 0) rstd[row] = rs;
+  float* yr = y + (size_t)row * E;
+#pragma unroll
+  for (int k = 0; k < MAXV; k++)
+    if (k < nv) yr[k * 32 + lane] = v[k] * rs * g[k * 32 + lane];
+}
+
+// RMSNorm backward with the residual gradient fused in:
+//   dx = dres + rs*g*dy - (rs^3/E) * (sum_j dy_j g_j x_j) * x      (RMS_DX, autograd.ts:331-351)
+// and per-block partial dgamma = sum_rows dy * x * rs              (RMS_DG, :352-365).
+// dx may alias dres.  Block = 8 warps, ROWS_PER_BLOCK rows.
+constexpr int NORM_ROWS = 64;
+__global__ void k_rms_bwd(const float* __restrict__ x, const float* __restrict__ dy, const float* __restrict__ g,
+                          const float* __restrict__ rstd, const float* dres, float* dx, float* __restrict__ dg_part,
+                          int rows, int E) {
+  __shared__ float acc[8][MAXV * 32];
+  const int w = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int nv = E / 32;
+  float dgl[MAXV];
+#pragma unroll
+  for (int k = 0; k < MAXV; k++) dgl[k] = 0.f;
+  const int r0 = blockIdx.x * NORM_ROWS;
+  for (int r = r0 + w; r < min(rows, r0 + NORM_ROWS); r += 8) {
+    const float* xr = x + (size_t)r * E;
+    const float* dyr = dy + (size_t)r * E;
+    const float rs = rstd[r];
+    float xv[MAXV], dv[MAXV];
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < MAXV; k++)
+      if (k < nv) {
+        xv[k] = xr[k * 32 + lane];
+        dv[k] = dyr[k * 32 + lane];
+        s += dv[k] * g[k * 32 + lane] * xv[k];
+        dgl[k] += dv[k] * xv[k] * rs;
+      }
+    s = warp_sum(s);
+    const float kf = rs * rs * rs * s / E;
+    const float* dr = dres ? dres + (size_t)r * E : nullptr;
+    float* dxr = dx + (size_t)r * E;
+#pragma unroll
+    for (int k = 0; k < MAXV; k++)
+      if (k < nv) {
+        float o = rs * dv[k] * g[k * 32 + lane] - kf * xv[k];
+        if (dr) o += dr[k * 32 + lane];
+        dxr[k * 32 + lane] = o;
+      }
+  }
+#pragma unroll
+  for (int k = 0; k < MAXV; k++)
+    if (k < nv) acc[w][k * 32 + lane] = dgl[k];
+  __syncthreads();
+  for (int c = threadIdx.x; c < E; c += blockDim.x) {
+    float s = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; q++) s += acc[q][c];
+    dg_part[(size_t)blockIdx.x * E + c] = s;
+  }
+}
+
+// LayerNorm forward (biased variance), autograd.ts:256-274.
+__global__ void k_ln_fwd(const float* __restrict__ x, const float* __restrict__ g, const float* __restrict__ b,
+                         float* __restrict__ y, float* __restrict__ mean, float* __restrict__ rstd, int rows, int E,
+                         float eps) {
+  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* xr = x + (size_t)row * E;
+  const int nv = E / 32;
+  float v[MAXV];
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < MAXV; k++)
+    if (k < nv) {
+      v[k] = xr[k * 32 + lane];
+      s += v[k];
+    }
+  const float mu = warp_sum(s) / E;
+  float q = 0.f;
+#pragma unroll
+  for (int k = 0; k < MAXV; k++)
+    if (k < nv) q += (v[k] - mu) * (v[k] - mu);
+  const float rs = rsqrtf(warp_sum(q) / E + eps);
+  if (lane == 0) {
+    mean[row] = mu;
+    rstd[row] = rs;
+  }
+  float* yr = y + (size_t)row * E;
+#pragma unroll
+  for (int k = 0; k < MAXV; k++)
+    if (k < nv) yr[k * 32 + lane] = (v[k] - mu) * rs * g[k * 32 + lane] + b[k * 32 + lane];
+}
+
+// LayerNorm backward (LN_DX + LN_DGB, autograd.ts:275-308) with the residual gradient fused.
+__global__ void k_ln_bwd(const float* __restrict__ x, const float* __restrict__ dy, const float* __restrict__ g,
+                         const float* __restrict__ mean, const float* __restrict__ rstd, const float* dres, float* dx,
+                         float* __restrict__ dg_part, float* __restrict__ db_part, int rows, int E) {
+  __shared__ float accg[8][MAXV * 32];
+  const int w = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int nv = E / 32;
+  float dgl[MAXV], dbl[MAXV];
+#pragma unroll
+  for (int k = 0; k < MAXV; k++) dgl[k] = dbl[k] = 0.f;
+  const int r0 = blockIdx.x * NORM_ROWS;
+  for (int r = r0 + w; r < min(rows, r0 + NORM_ROWS); r += 8) {
+    const float* xr = x + (size_t)r * E;
+    const float* dyr = dy + (size_t)r * E;
+    const float mu = mean[r], rs = rstd[r];
+    float xh[MAXV], dv[MAXV];
+    float sdy = 0.f, sdyx = 0.f;
+#pragma unroll
+    for (int k = 0; k < MAXV; k++)
+      if (k < nv) {
+        xh[k] = (xr[k * 32 + lane] - mu) * rs;
+        const float gy = dyr[k * 32 + lane];
+        dgl[k] += gy * xh[k];
+        dbl[k] += gy;
+        dv[k] = gy * g[k * 32 + lane];
+        sdy += dv[k];
+        sdyx += dv[k] * xh[k];
+      }
+    sdy = warp_sum(sdy) / E;
+    sdyx = warp_sum(sdyx) / E;
+    const float* dr = dres ? dres + (size_t)r * E : nullptr;
+    float* dxr = dx + (size_t)r * E;
+#pragma unroll
+    for (int k = 0; k < MAXV; k++)
+      if (k < nv) {
+        float o = rs * (dv[k] - sdy - xh[k] * sdyx);
+        if (dr) o += dr[k * 32 + lane];
+        dxr[k * 32 + lane] = o;
+      }
+  }
+#pragma unroll
+  for (int k = 0; k < MAXV; k++)
+    if (k < nv) accg[w][k * 32 + lane] = dgl[k];
+  __syncthreads();
+  for (int c = threadIdx.x; c < E; c += blockDim.x) {
+    float s = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; q++) s += accg[q][c];
+    dg_part[(size_t)blockIdx.x * E + c] = s;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < MAXV; k++)
+    if (k < nv) accg[w][k * 32 + lane] = dbl[k];
+  __syncthreads();
+  for (int c = threadIdx.x; c < E; c += blockDim.x) {
+    float s = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; q++) s += accg[q][c];
+    db_part[(size_t)blockIdx.x * E + c] = s;
+  }
+}
+
+// out[c] += sum_b part[b][c] (fixed order: deterministic).
+__global__ void k_reduce_parts(const float* __restrict__ part, int nparts, int C, float* __restrict__ out) {
+  GRID_STRIDE(c, (size_t)C) {
+    float s = 0.f;
+    for (int b = 0; b < nparts; b++) s += part[(size_t)b * C + c];
+    out[c] += s;
+  }
+}
+
+// Column sums of g[rows][C] into partials (bias gradients; SEGSUM, autograd.ts:122-135).
+__global__ void k_colsum_parts(const float* __restrict__ g, int rows, int C, float* __restrict__ part) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const int r0 = blockIdx.y * NORM_ROWS;
+  float s = 0.f;
+  for (int r = r0; r < min(rows, r0 + NORM_ROWS); r++) s += g[(size_t)r * C + c];
+  part[(size_t)blockIdx.y * C + c] = s;
+}
+
+// -------------------------------------------------- fused softmax + cross-entropy
+// One block per row of logits[N][V]: per-row loss (CE_FWD, autograd.ts:441-454) and the
+// gradient (CE_BWD, :455-471) written in place over the logits: one HBM read, one write.
+__global__ void __launch_bounds__(512) k_ce_fused(float* __restrict__ logits, const uint32_t* __restrict__ tgt,
+                                                  float* __restrict__ loss_rows, int V, float gscale, int* flags) {
+  const int row = blockIdx.x;
+  float* x = logits + (size_t)row * V;
+  __shared__ float red_m[32], red_s[32];
+  __shared__ float bc[2];
+  // online (max, sum) over this thread's elements
+  float m = -INFINITY, s = 0.f;
+  const int V4 = V / 4;
+  const bool vec = (V % 4) == 0;
+  if (vec) {
+    for (int j = threadIdx.x; j < V4; j += blockDim.x) {
+      const float4 v = reinterpret_cast<const float4*>(x)[j];
+      const float mx = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+      if (mx > m) {
+        s *= __expf(m - mx);
+        m = mx;
+      }
+      s += __expf(v.x - m) + __expf(v.y - m) + __expf(v.z - m) + __expf(v.w - m);
+    }
+  } else {
+    for (int j = threadIdx.x; j < V; j += blockDim.x) {
+      const float v = x[j];
+      if (v > m) {
+        s *= __expf(m - v);
+        m = v;
+      }
+      s += __expf(v - m);
+    }
+  }
+  // warp combine
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    const float mm = fmaxf(m, m2);
+    s = (m == -INFINITY ? 0.f : s * __expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - mm));
+    m = mm;
+  }
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    red_m[w] = m;
+    red_s[w] = s;
+  }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x / 32;
+    m = lane < nw ? red_m[lane] : -INFINITY;
+    s = lane < nw ? red_s[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      const float mm = fmaxf(m, m2);
+      s = (m == -INFINITY ? 0.f : s * __expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - mm));
+      m = mm;
+    }
+    if (lane == 0) {
+      bc[0] = m;
+      bc[1] = s;
+    }
+  }
+  __syncthreads();
+  m = bc[0];
+  s = bc[1];
+  uint32_t t = tgt[row];
+  const bool bad = t >= (uint32_t)V;
+  if (threadIdx.x == 0) {
+    if (bad) atomicExch(&flags[FLAG_RANGE], 1);
+    loss_rows[row] = bad ? 0.f : m + logf(s) - x[t];
+  }
+  __syncthreads();  // the target logit is read before it is overwritten
+  const float inv = 1.0f / s;
+  if (vec) {
+    for (int j = threadIdx.x; j < V4; j += blockDim.x) {
+      float4 v = reinterpret_cast<float4*>(x)[j];
+      v.x = gscale * __expf(v.x - m) * inv;
+      v.y = gscale * __expf(v.y - m) * inv;
+      v.z = gscale * __expf(v.z - m) * inv;
+      v.w = gscale * __expf(v.w - m) * inv;
+      const int base = 4 * j;
+      if (!bad && (uint32_t)(t - base) < 4u) {
+        const int q = (int)(t - base);
+        if (q == 0) v.x -= gscale;
+        if (q == 1) v.y -= gscale;
+        if (q == 2) v.z -= gscale;
+        if (q == 3) v.w -= gscale;
+      }
+      reinterpret_cast<float4*>(x)[j] = v;
+    }
+  } else {
+    for (int j = threadIdx.x; j < V; j += blockDim.x) {
+      float v = gscale * __expf(x[j] - m) * inv;
+      if (!bad && (uint32_t)j == t) v -= gscale;
+      x[j] = v;
+    }
+  }
+}
+
+// Forward-only variant: per-row loss, logits untouched.
+__global__ void __launch_bounds__(512) k_ce_loss(const float* __restrict__ logits, const uint32_t* __restrict__ tgt,
+                                                 float* __restrict__ loss_rows, int V, int* flags) {
+  const int row = blockIdx.x;
+  const float* x = logits + (size_t)row * V;
+  __shared__ float red_m[32], red_s[32];
+  float m = -INFINITY, s = 0.f;
+  for (int j = threadIdx.x; j < V; j += blockDim.x) {
+    const float v = x[j];
+    if (v > m) {
+      s *= __expf(m - v);
+      m = v;
+    }
+    s += __expf(v - m);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    const float mm = fmaxf(m, m2);
+    s = (m == -INFINITY ? 0.f : s * __expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - mm));
+    m = mm;
+  }
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    red_m[w] = m;
+    red_s[w] = s;
+  }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x / 32;
+    m = lane < nw ? red_m[lane] : -INFINITY;
+    s = lane < nw ? red_s[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      const float mm = fmaxf(m, m2);
+      s = (m == -INFINITY ? 0.f : s * __expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - mm));
+      m = mm;
+    }
+    if (lane == 0) {
+      const uint32_t t = tgt[row];
+      if (t >= (uint32_t)V) {
+        atomicExch(&flags[FLAG_RANGE], 1);
+        loss_rows[row] = 0.f;
+      } else {
+        loss_rows[row] = m + logf(s) - x[t];
+      }
+    }
+  }
+}
+
+// loss = (sum of per-row losses, in double) / n; one block, fixed order.
+__global__ void k_loss_mean(const float* __restrict__ rows, int n, float* __restrict__ out, int* flags) {
+  __shared__ double part[32];
+  double s = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += rows[i];
+  s = warp_sum_d(s);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double v = threadIdx.x < blockDim.x / 32 ? part[threadIdx.x] : 0.0;
+    v = warp_sum_d(v);
+    if (threadIdx.x == 0) {
+      const float l = (float)(v / n);
+      out[0] = l;
+      if (!isfinite(l)) atomicExch(&flags[FLAG_NONFINITE], 1);
+    }
+  }
+}
+
+// ---------------------------------------------------------- optimizer
+// Sum of squares of scale*g in double: per-block partials, then a fixed-order final pass.
+constexpr int NORM_BLOCKS = 592;  // 4 x 148 SMs
+__global__ void k_sumsq_parts(const float* __restrict__ g, size_t n, float scale, double* __restrict__ part) {
+  __shared__ double red[32];
+  double s = 0;
+  const size_t n4 = n / 4;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(g)[i];
+    const double a = (double)(v.x * scale), b = (double)(v.y * scale), c = (double)(v.z * scale),
+                 d = (double)(v.w * scale);
+    s += a * a + b * b + c * c + d * d;
+  }
+  if (blockIdx.x == 0)
+    for (size_t i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) {
+      const double a = (double)(g[i] * scale);
+      s += a * a;
+    }
+  s = warp_sum_d(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.0;
+    v = warp_sum_d(v);
+    if (threadIdx.x == 0) part[blockIdx.x] = v;
+  }
+}
+// norm = sqrt(sum); coef = clip > 0 && norm > clip ? clip / norm : 1 (src/optim/clip.ts:7-24).
+__global__ void k_norm_final(const double* __restrict__ part, int nparts, float clip, double* __restrict__ norm_out,
+                             float* __restrict__ coef_out, int* flags) {
+  __shared__ double red[32];
+  double s = 0;
+  for (int i = threadIdx.x; i < nparts; i += blockDim.x) s += part[i];
+  s = warp_sum_d(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.0;
+    v = warp_sum_d(v);
+    if (threadIdx.x == 0) {
+      const double norm = sqrt(v);
+      norm_out[0] = norm;
+      float coef = 1.0f;
+      if (clip > 0.f && norm > (double)clip && norm > 0) coef = (float)((double)clip / norm);
+      if (!isfinite(norm)) {
+        atomicExch(&flags[FLAG_NONFINITE], 1);
+        coef = 0.0f;  // a non-finite step is skipped rather than applied
+      }
+      coef_out[0] = coef;
+    }
+  }
+}
+// g *= coef (standalone clipGradNorm).
+__global__ void k_scale_by(float* __restrict__ g, size_t n, const float* __restrict__ coef, float pre) {
+  const float c = coef[0] * pre;
+  GRID_STRIDE(i, n) g[i] *= c;
+}
+
+// AdamW over the flat parameter buffer (ADAMW, autograd.ts:516-531 / src/optim/adam.ts:50-55)
+// with the gradient pre-scaled by gscale * coef (DP mean and global-norm clip).
+__global__ void k_adamw_flat(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                             float* __restrict__ v, size_t n, float lr, float b1, float b2, float eps, float wd,
+                             float bc1, float bc2, float gscale, const float* __restrict__ coef) {
+  const float cs = gscale * (coef ? coef[0] : 1.0f);
+  const float rbc1 = 1.0f / bc1, rbc2 = 1.0f / bc2;
+  const size_t n4 = n / 4;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+    float4 pp = reinterpret_cast<float4*>(p)[i];
+    const float4 gg = reinterpret_cast<const float4*>(g)[i];
+    float4 mm = reinterpret_cast<float4*>(m)[i];
+    float4 vv = reinterpret_cast<float4*>(v)[i];
+#define ADAM1(c)                                                      \
+  {                                                                   \
+    const float gr = gg.c * cs;                                       \
+    mm.c = b1 * mm.c + (1.f - b1) * gr;                               \
+    vv.c = b2 * vv.c + (1.f - b2) * gr * gr;                          \
+    const float mh = mm.c * rbc1, vh = vv.c * rbc2;                   \
+    pp.c = pp.c - lr * (mh / (sqrtf(vh) + eps) + wd * pp.c);          \
+  }
+    ADAM1(x) ADAM1(y) ADAM1(z) ADAM1(w)
+#undef ADAM1
+    reinterpret_cast<float4*>(p)[i] = pp;
+    reinterpret_cast<float4*>(m)[i] = mm;
+    reinterpret_cast<float4*>(v)[i] = vv;
+  }
+  if (blockIdx.x == 0)
+    for (size_t i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) {
+      const float gr = g[i] * cs;
+      m[i] = b1 * m[i] + (1.f - b1) * gr;
+      v[i] = b2 * v[i] + (1.f - b2) * gr * gr;
+      p[i] = p[i] - lr * ((m[i] * rbc1) / (sqrtf(v[i] * rbc2) + eps) + wd * p[i]);
+    }
+}
+
+}  // namespace
+
+int embed_fwd(cudaStream_t st, const float* wte, const float* wpe, const uint32_t* ids, float* x, int N, int T, int E,
+              int V, int* flags) {
+  TURT_REQUIRE(E % 4 == 0, "embedding width must be a multiple of 4");
+  const size_t n = (size_t)N * (E / 4);
+  k_embed<<<(int)std::min<size_t>((n + 255) / 256, 148 * 32), 256, 0, st>>>(wte, wpe, ids, x, N, T, E, V, flags);
+  TURT_LAUNCH_CHECK();
+  return OK;
+}
+int embed_bwd(cudaStream_t st, const float* dx, const uint32_t* ids, float* dwte, float* dwpe, int N, int T, int E,
+              int V) {
+  const size_t n = (size_t)N * E;
+  k_embed_bwd<<<(int)std::min<size_t>((n + 255) / 256, 148 * 32), 256, 0, st>>>(dx, ids, dwte, dwpe, N, T, E, V);
+  TURT_LAUNCH_CHECK();
+  return OK;
+}
+int rms_fwd(cudaStream_t st, const float* x, const float* g, float* y, float* rstd, int rows, int E, float eps) {
+  TURT_REQUIRE(E % 32 == 0 && E <= 32 * MAXV, "norm width must be a multiple of 32, at most 1024");
+  k_rms_fwd<<<ceil_div(rows, 8), 256, 0, st>>>(x, g, y, rstd, rows, E, eps);
+  TURT_LAUNCH_CHECK();
+  return OK;
+}
+int norm_parts(int rows) { return ceil_div(rows, NORM_ROWS); }
+int rms_bwd(cudaStream_t st, const float* x, const float* dy, const float* g, const float* rstd, const float* dres,
+            float* dx, float* dg_accum, float* part, int rows, int E) {
+  TURT_REQUIRE(E % 32 == 0 && E <= 32 * MAXV, "norm width must be a multiple of 32, at most 1024");
+  const int nb = norm_parts(rows);
+  k_rms_bwd<<<nb, 256, 0, st>>>(x, dy, g, rstd, dres, dx, part, rows, E);
+  TURT_LAUNCH_CHECK();
+  k_reduce_parts<<<ceil_div(E, 128), 128, 0, st>>>(part, nb, E, dg_accum);
+  TURT_LAUNCH_CHECK();
+  return OK;
+}
+int ln_fwd(cudaStream_t st, const float* x, const float* g, const float* b, float* y, float* mean, float* rstd, int rows,
+           int E, float eps) {
+  TURT_REQUIRE(E % 32 == 0 && E <= 32 * MAXV, "norm width must be a multiple of 32, at most 1024");
+  k_ln_fwd<<<ceil_div(rows, 8), 256, 0, st>>>(x, g, b, y, mean, rstd, rows, E, eps);
+  TURT_LAUNCH_CHECK();
+  return OK;
+}
+int ln_bwd(cudaStream_t st, const float* x, const float* dy, const float* g, const float* mean, const float* rstd,
+           const float* dres, float* dx, float* dg_accum, float* db_accum, float* part, int rows, int E) {
+  TURT_REQUIRE(E % 32 == 0 && E <= 32 * MAXV, "norm width must be a multiple of 32, at most 1024");
+  const int nb = norm_parts(rows);
+  k_ln_bwd<<<nb, 256, 0, st>>>(x, dy, g, mean, rstd, dres, dx, part, part + (size_t)nb * E, rows, E);
+  TURT_LAUNCH_CHECK();
+  k_reduce_parts<<<ceil_div(E, 128), 128, 0, st>>>(part, nb, E, dg_accum);
+  TURT_LAUNCH_CHECK();
+  k_reduce_parts<<<ceil_div(E, 128), 128, 0, st>>>(part + (size_t)nb * E, nb, E, db_accum);
+  TURT_LAUNCH_CHECK();
+  return OK;
+}
+int colsum_accum(cudaStream_t st, const float* g, int rows, int C, float* out_accum, float* part) {
+  const int nb = norm_parts(rows);
+  dim3 grid(ceil_div(C, 128), nb);
+  k_colsum_parts<<<grid, 128, 0, st>>>(g, rows, C, part);
+  TURT_LAUNCH_CHECK();
+  k_reduce_parts<<<ceil_div(C, 128), 128, 0, st>>>(part, nb, C, out_accum);
+  TURT_LAUNCH_CHECK();
+  return OK;
+}
+int ce_fused(cudaStream_t st, float* logits, const uint32_t* tgt, float* loss_rows, int N, int V, float gscale,
+             int* flags) {
+  k_ce_fused<<<N, 512, 0, st>>>(logits, tgt, loss_rows, V, gscale, flags);
+  TURT_LAUNCH_CHECK();
+  return OK;
+}
+int ce_loss(cudaStream_t st, const float* logits, const uint32_t* tgt, float* loss_rows, int N, int V, int* flags) {
+  k_ce_loss<<<N, 512, 0, st>>>(logits, tgt, loss_rows, V, flags);
+  TURT_LAUNCH_CHECK();
+  return OK;
+}
+int loss_mean(cudaStream_t st, const float* rows, int n, float* out, int* flags) {
+  k_loss_mean<<<1, 1024, 0, st>>>(rows, n, out, flags);
+  TURT_LAUNCH_CHECK();
+  return OK;
+}
+size_t norm_scratch_doubles() { return NORM_BLOCKS + 1; }
+int grad_norm(cudaStream_t st, const float* g, size_t n, float gscale, float clip, double* scratch, double* norm_out,
+              float* coef_out, int* flags) {
+  k_sumsq_parts<<<NORM_BLOCKS, 512, 0, st>>>(g, n, gscale, scratch);
+  TURT_LAUNCH_CHECK();
+  k_norm_final<<<1, 1024, 0, st>>>(scratch, NORM_BLOCKS, clip, norm_out, coef_out, flags);
+  TURT_LAUNCH_CHECK();
+  return OK;
+}
+int scale_by(cudaStream_t st, float* g, size_t n, const float* coef, float pre) {
+  k_scale_by<<<148 * 8, 256, 0, st>>>(g, n, coef, pre);
+  TURT_LAUNCH_CHECK();
+  return OK;
+}
+int adamw_flat(cudaStream_t st, float* p, const float* g, float* m, float* v, size_t n, float lr, float b1, float b2,
+               float eps, float wd, float bc1, float bc2, float gscale, const float* coef) {
+  TURT_REQUIRE(((uintptr_t)p & 15) == 0 && ((uintptr_t)g & 15) == 0 && ((uintptr_t)m & 15) == 0 &&
+                   ((uintptr_t)v & 15) == 0,
+               "adamw: buffers must be 16-byte aligned");
+  k_adamw_flat<<<148 * 8, 256, 0, st>>>(p, g, m, v, n, lr, b1, b2, eps, wd, bc1, bc2, gscale, coef);
+  TURT_LAUNCH_CHECK();
+  return OK;
+}
+
+}  // namespace turt
