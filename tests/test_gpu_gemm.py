@@ -4,14 +4,14 @@ Covers every operand layout the train step uses (K-major / MN-major A and B), ba
 accumulate, tile residues (M, N, K not multiples of the tile), the host-array entry point
 (GpuCompute.matmul, scripts/gpu-bench.ts cases incl. [17,33,9]) and the CUDA-core path.
 Tolerances (normalised error max|C - C_ref| / max|C_ref|): plain TF32 keeps 10 mantissa
-bits per operand -> 4e-3; error-compensated 3xTF32 -> 2e-6 (fp32-level).
+bits per operand -> 4e-3; error-compensated 3xTF32 -> 2e-5 (fp32 accumulation level).
 """
 import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
 
-TOL = {1: 4e-3, 3: 2e-6}
+TOL = {1: 4e-3, 3: 2e-5}
 
 
 @pytest.fixture(scope="module")
