@@ -126,6 +126,16 @@ int turt_adamw(turt_ctx* ctx, const float* grad, float* param, float* m, float* 
  * src/infer/backend.ts:11-16 / gpu-backend.ts:45-55: host arrays in, host array out. */
 int turt_host_matmul(turt_ctx* ctx, const float* a, int m, int k, const float* b, int n, float* out);
 int turt_host_bmm(turt_ctx* ctx, const float* a, int batch, int m, int k, const float* b, int n, float* out);
+/* No counterpart in the reference.  Same product as turt_host_matmul, for callers that cannot
+ * let the library allocate device memory during the call (a process whose device memory is
+ * held by another framework's caching allocator, or a latency-bound host that must not
+ * allocate after start-up): A, B and C are staged in one fixed 8 MiB device array owned by
+ * the library (every GPU that loads it holds the array until exit) instead of per-call
+ * buffers.  Products whose padded A + B + C exceed 2 Mi floats are rejected with
+ * TURT_ERR_INVALID.  The first call on a device looks up the array's device address (call it
+ * once before any stream capture).  All calls share the array; calls that overlap on the GPU
+ * race on it. */
+int turt_host_matmul_noalloc(turt_ctx* ctx, const float* a, int m, int k, const float* b, int n, float* out);
 
 /* -------------------------------------------------------------- model level
  * GpuGPT, src/models/gpu-gpt.ts:54-202 (+ GPTConfig, src/models/gpt.ts:67-78) with the
