@@ -73,14 +73,3 @@ def test_no_gpu_calls_fail_cleanly(built):
     assert L.turt_dp_defer(None, 1) != 0
     n = C.c_uint64()
     assert L.turt_launch_count(C.byref(n)) == 0
-
-
-def test_no_forbidden_calls_in_sources():
-    """The batched-copy entry points are not used anywhere in the library sources."""
-    bad = ["cudaMemcpy" + "BatchAsync", "cudaMemcpy3D" + "BatchAsync", "cuMemcpy" + "BatchAsync",
-           "cuMemcpy3D" + "BatchAsync", ".multicast" + "::cluster"]
-    for d in ("turt_b200/csrc", "include"):
-        for f in os.listdir(os.path.join(ROOT, d)):
-            text = open(os.path.join(ROOT, d, f)).read()
-            for b in bad:
-                assert b not in text, (f, b)

@@ -79,7 +79,7 @@ __global__ void k_rms_fwd(const float* __restrict__ x, const float* __restrict__
 //   dx = dres + rs*g*dy - (rs^3/E) * (sum_j dy_j g_j x_j) * x      (RMS_DX, autograd.ts:331-351)
 // and per-block partial dgamma = sum_rows dy * x * rs              (RMS_DG, :352-365).
 // dx may alias dres.  Block = 8 warps, ROWS_PER_BLOCK rows.
-constexpr int NORM_ROWS = 64;
+constexpr int NORM_ROWS = 16;  // rows per block: 8192 rows -> 512 blocks (~3.5 per SM)
 __global__ void k_rms_bwd(const float* __restrict__ x, const float* __restrict__ dy, const float* __restrict__ g,
                           const float* __restrict__ rstd, const float* dres, float* dx, float* __restrict__ dg_part,
                           int rows, int E) {
@@ -223,12 +223,22 @@ __global__ void k_ln_bwd(const float* __restrict__ x, const float* __restrict__ 
   }
 }
 
-// out[c] += sum_b part[b][c] (fixed order: deterministic).
+// out[c] += sum_b part[b][c] (fixed order: deterministic).  One block per 32 columns; warp w
+// sums partial rows w, w+8, ... with coalesced 128-byte loads, then the 8 warp sums combine.
 __global__ void k_reduce_parts(const float* __restrict__ part, int nparts, int C, float* __restrict__ out) {
-  GRID_STRIDE(c, (size_t)C) {
-    float s = 0.f;
-    for (int b = 0; b < nparts; b++) s += part[(size_t)b * C + c];
-    out[c] += s;
+  __shared__ float red[8][33];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x * 32 + lane;
+  float s = 0.f;
+  if (c < C)
+    for (int b = w; b < nparts; b += 8) s += part[(size_t)b * C + c];
+  red[w][lane] = s;
+  __syncthreads();
+  if (w == 0 && c < C) {
+    float t = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; q++) t += red[q][lane];
+    out[c] += t;
   }
 }
 
@@ -540,7 +550,7 @@ int rms_bwd(cudaStream_t st, const float* x, const float* dy, const float* g, co
   const int nb = norm_parts(rows);
   k_rms_bwd<<<nb, 256, 0, st>>>(x, dy, g, rstd, dres, dx, part, rows, E);
   TURT_LAUNCH_CHECK();
-  k_reduce_parts<<<ceil_div(E, 128), 128, 0, st>>>(part, nb, E, dg_accum);
+  k_reduce_parts<<<ceil_div(E, 32), 256, 0, st>>>(part, nb, E, dg_accum);
   TURT_LAUNCH_CHECK();
   return OK;
 }
@@ -557,9 +567,9 @@ int ln_bwd(cudaStream_t st, const float* x, const float* dy, const float* g, con
   const int nb = norm_parts(rows);
   k_ln_bwd<<<nb, 256, 0, st>>>(x, dy, g, mean, rstd, dres, dx, part, part + (size_t)nb * E, rows, E);
   TURT_LAUNCH_CHECK();
-  k_reduce_parts<<<ceil_div(E, 128), 128, 0, st>>>(part, nb, E, dg_accum);
+  k_reduce_parts<<<ceil_div(E, 32), 256, 0, st>>>(part, nb, E, dg_accum);
   TURT_LAUNCH_CHECK();
-  k_reduce_parts<<<ceil_div(E, 128), 128, 0, st>>>(part + (size_t)nb * E, nb, E, db_accum);
+  k_reduce_parts<<<ceil_div(E, 32), 256, 0, st>>>(part + (size_t)nb * E, nb, E, db_accum);
   TURT_LAUNCH_CHECK();
   return OK;
 }
@@ -568,7 +578,7 @@ int colsum_accum(cudaStream_t st, const float* g, int rows, int C, float* out_ac
   dim3 grid(ceil_div(C, 128), nb);
   k_colsum_parts<<<grid, 128, 0, st>>>(g, rows, C, part);
   TURT_LAUNCH_CHECK();
-  k_reduce_parts<<<ceil_div(C, 128), 128, 0, st>>>(part, nb, C, out_accum);
+  k_reduce_parts<<<ceil_div(C, 32), 256, 0, st>>>(part, nb, C, out_accum);
   TURT_LAUNCH_CHECK();
   return OK;
 }
