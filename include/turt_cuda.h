@@ -50,9 +50,13 @@ int turt_ctx_set_stream(turt_ctx* ctx, void* stream);
 void* turt_ctx_stream(turt_ctx* ctx);
 /* Waits for the context's stream and reports device-side error flags (range, timeout). */
 int turt_synchronize(turt_ctx* ctx);
-/* Tensor-core precision of every GEMM issued through this context (models included):
- * TURT_PRECISION_TF32X3 (default) = error-compensated 3xTF32, ~fp32 accuracy, meets the
- * reference's gradient tolerance; TURT_PRECISION_TF32 = one TF32 pass (10-bit mantissa). */
+/* Precision of every GEMM issued through this context:
+ * TURT_PRECISION_TF32X3 (default) = error-compensated 3xTF32 on the tensor cores (~2^-20
+ * relative per product), meets the reference's gradient tolerance;
+ * TURT_PRECISION_TF32 = one TF32 tensor-core pass (10-bit mantissa);
+ * TURT_PRECISION_FP32 = fp32 FMA on the CUDA cores, the arithmetic of the reference's WGSL
+ * matmul (op-level and host-array matmuls only; model GEMMs then use 3xTF32). */
+#define TURT_PRECISION_FP32 0
 #define TURT_PRECISION_TF32 1
 #define TURT_PRECISION_TF32X3 3
 int turt_set_precision(turt_ctx* ctx, int precision);

@@ -115,7 +115,8 @@ void* turt_ctx_stream(turt_ctx* ctx) { return ctx ? reinterpret_cast<void*>(ctx-
 
 int turt_set_precision(turt_ctx* ctx, int precision) {
   CTX_GUARD(ctx);
-  TURT_REQUIRE(precision == GEMM_TF32 || precision == GEMM_TF32X3, "precision must be 1 (TF32) or 3 (3xTF32)");
+  TURT_REQUIRE(precision == 0 || precision == GEMM_TF32 || precision == GEMM_TF32X3,
+               "precision must be 0 (FP32), 1 (TF32) or 3 (3xTF32)");
   ctx->precision = precision;
   return OK;
 }
@@ -222,7 +223,7 @@ int turt_matmul_into(turt_ctx* ctx, const float* a, const float* b, float* out, 
   epi.C = out;
   epi.ldc = N;
   epi.strideC = (long)M * N;
-  if (gemm_tf32_supported(A, B) && N % 4 == 0 && ((uintptr_t)out & 15) == 0)
+  if (ctx->precision != 0 && gemm_tf32_supported(A, B) && N % 4 == 0 && ((uintptr_t)out & 15) == 0)
     return gemm_tf32(ctx->stream, M, N, K, batch, A, B, epi, ctx->flags, ctx->precision);
   return gemm_simt(ctx->stream, a, b, out, M, K, N, batch, transA != 0, transB != 0, accum != 0);
 }
@@ -397,7 +398,10 @@ int turt_host_bmm(turt_ctx* ctx, const float* a, int batch, int m, int k, const 
   const size_t na = (size_t)batch * m * k, nb = (size_t)batch * k * n, nc = (size_t)batch * m * n;
   if (nc == 0) return OK;
   // Pitch rows up to a multiple of 4 floats so every call takes the tensor-core path.
-  const int kp = (k + 3) & ~3, np = (n + 3) & ~3;
+  // Tensor-core path: pitch rows up to a multiple of 4 floats (TMA needs 16-byte pitches).
+  // CUDA-core (FP32) path: dense rows.
+  const bool simt = ctx->precision == 0;
+  const int kp = simt ? k : (k + 3) & ~3, np = simt ? n : (n + 3) & ~3;
   float *da = nullptr, *db = nullptr, *dc = nullptr;
   TURT_CHECK_CUDA(cudaMallocAsync(&da, (size_t)batch * m * kp * 4 + 16, ctx->stream));
   TURT_CHECK_CUDA(cudaMallocAsync(&db, (size_t)batch * k * np * 4 + 16, ctx->stream));
@@ -419,7 +423,10 @@ int turt_host_bmm(turt_ctx* ctx, const float* a, int batch, int m, int k, const 
     epi.C = dc;
     epi.ldc = np;
     epi.strideC = (long)m * np;
-    rc = gemm_tf32(ctx->stream, m, n, k, batch, A, B, epi, ctx->flags, ctx->precision);
+    if (ctx->precision == 0)
+      rc = gemm_simt(ctx->stream, da, db, dc, m, k, n, batch, false, false, false);
+    else
+      rc = gemm_tf32(ctx->stream, m, n, k, batch, A, B, epi, ctx->flags, ctx->precision);
   }
   if (rc == OK)
     TURT_CHECK_CUDA(cudaMemcpy2DAsync(out, n * 4, dc, np * 4, n * 4, (size_t)batch * m, cudaMemcpyDeviceToHost,

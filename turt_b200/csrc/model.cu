@@ -238,6 +238,9 @@ inline GemmEpi epi(int kind, float* C, long ldc) {
   return e;
 }
 
+// Model GEMMs run on the tensor cores: FP32 (CUDA-core) precision applies to op-level calls only.
+inline int mp(const turt_model* m) { return m->ctx->precision == 0 ? GEMM_TF32X3 : m->ctx->precision; }
+
 #define RC(x)          \
   do {                 \
     int rc__ = (x);    \
@@ -272,13 +275,13 @@ int forward(turt_model* m, int B, int T, bool train, float loss_scale) {
       RC(ln_fwd(st, a.x, P + L.ln1g, P + L.ln1b, a.y1, a.mu1, a.rs1, N, E, m->eps));
     GemmEpi e = epi(m->modern ? EPI_STORE : EPI_BIAS, a.qkv, 3 * E);
     if (!m->modern) e.bias = P + L.bqkv;
-    RC(gemm_tf32(st, N, 3 * E, E, 1, opK(a.y1, E), opMN(P + L.wqkv, 3 * E), e, flags, m->ctx->precision));
+    RC(gemm_tf32(st, N, 3 * E, E, 1, opK(a.y1, E), opMN(P + L.wqkv, 3 * E), e, flags, mp(m)));
     RC(attention_fwd(st, a.qkv, m->rope_cs, a.att, a.lse, B, T, H, hd, m->modern ? 1 : 0));
     e = epi(EPI_ADD_RES, a.h, E);
     e.R = a.x;
     e.ldr = E;
     if (!m->modern) e.bias = P + L.bproj;
-    RC(gemm_tf32(st, N, E, E, 1, opK(a.att, E), opMN(P + L.wproj, E), e, flags, m->ctx->precision));
+    RC(gemm_tf32(st, N, E, E, 1, opK(a.att, E), opMN(P + L.wproj, E), e, flags, mp(m)));
     if (m->modern)
       RC(rms_fwd(st, a.h, P + L.ln2g, a.y2, a.rs2, N, E, m->eps));
     else
@@ -287,26 +290,26 @@ int forward(turt_model* m, int B, int T, bool train, float loss_scale) {
       e = epi(EPI_SWIGLU_FWD, a.pre, 2 * h);
       e.C2 = a.act;
       e.ldc2 = h;
-      RC(gemm_tf32(st, N, 2 * h, E, 1, opK(a.y2, E), opMN(P + L.w1, 2 * h), e, flags, m->ctx->precision));
+      RC(gemm_tf32(st, N, 2 * h, E, 1, opK(a.y2, E), opMN(P + L.w1, 2 * h), e, flags, mp(m)));
     } else {
       e = epi(EPI_BIAS_GELU, a.pre, h);
       e.bias = P + L.b1;
       e.C2 = a.act;
       e.ldc2 = h;
-      RC(gemm_tf32(st, N, h, E, 1, opK(a.y2, E), opMN(P + L.w1, h), e, flags, m->ctx->precision));
+      RC(gemm_tf32(st, N, h, E, 1, opK(a.y2, E), opMN(P + L.w1, h), e, flags, mp(m)));
     }
     e = epi(EPI_ADD_RES, xnext, E);
     e.R = a.h;
     e.ldr = E;
     if (!m->modern) e.bias = P + L.b2;
-    RC(gemm_tf32(st, N, E, h, 1, opK(a.act, h), opMN(P + L.w2, E), e, flags, m->ctx->precision));
+    RC(gemm_tf32(st, N, E, h, 1, opK(a.act, h), opMN(P + L.w2, E), e, flags, mp(m)));
   }
   if (m->modern)
     RC(rms_fwd(st, m->xL, P + m->lnfg, m->yf, m->rsf, N, E, m->eps));
   else
     RC(ln_fwd(st, m->xL, P + m->lnfg, P + m->lnfb, m->yf, m->muf, m->rsf, N, E, m->eps));
   // tied head: logits = yf * wte^T (wte [V][E] is the K-major B operand)
-  RC(gemm_tf32(st, N, V, E, 1, opK(m->yf, E), opK(P + m->wte, E), epi(EPI_STORE, m->logits, V), flags, m->ctx->precision));
+  RC(gemm_tf32(st, N, V, E, 1, opK(m->yf, E), opK(P + m->wte, E), epi(EPI_STORE, m->logits, V), flags, mp(m)));
   if (train)
     RC(ce_fused(st, m->logits, m->d_tgt, m->loss_rows, N, V, loss_scale / (float)N, flags));
   else
@@ -322,8 +325,8 @@ int backward(turt_model* m, int B, int T) {
   const float* P = m->P;
   float* G = m->G;
   // head: dyf = dlogits * wte ; dwte += dlogits^T * yf
-  RC(gemm_tf32(st, N, E, V, 1, opK(m->logits, V), opMN(P + m->wte, E), epi(EPI_STORE, m->dy, E), flags, m->ctx->precision));
-  RC(gemm_tf32(st, V, E, N, 1, opMN(m->logits, V), opMN(m->yf, E), epi(EPI_ACCUM, G + m->wte, E), flags, m->ctx->precision));
+  RC(gemm_tf32(st, N, E, V, 1, opK(m->logits, V), opMN(P + m->wte, E), epi(EPI_STORE, m->dy, E), flags, mp(m)));
+  RC(gemm_tf32(st, V, E, N, 1, opMN(m->logits, V), opMN(m->yf, E), epi(EPI_ACCUM, G + m->wte, E), flags, mp(m)));
   if (m->modern)
     RC(rms_bwd(st, m->xL, m->dy, P + m->lnfg, m->rsf, nullptr, m->dx, G + m->lnfg, m->part, N, E));
   else
@@ -336,19 +339,19 @@ int backward(turt_model* m, int B, int T) {
       GemmEpi e = epi(EPI_SWIGLU_BWD, m->dpre, 2 * h);
       e.R = a.pre;
       e.ldr = 2 * h;
-      RC(gemm_tf32(st, N, h, E, 1, opK(m->dx, E), opK(P + L.w2, E), e, flags, m->ctx->precision));
-      RC(gemm_tf32(st, h, E, N, 1, opMN(a.act, h), opMN(m->dx, E), epi(EPI_ACCUM, G + L.w2, E), flags, m->ctx->precision));
-      RC(gemm_tf32(st, N, E, 2 * h, 1, opK(m->dpre, 2 * h), opK(P + L.w1, 2 * h), epi(EPI_STORE, m->dy, E), flags, m->ctx->precision));
-      RC(gemm_tf32(st, E, 2 * h, N, 1, opMN(a.y2, E), opMN(m->dpre, 2 * h), epi(EPI_ACCUM, G + L.w1, 2 * h), flags, m->ctx->precision));
+      RC(gemm_tf32(st, N, h, E, 1, opK(m->dx, E), opK(P + L.w2, E), e, flags, mp(m)));
+      RC(gemm_tf32(st, h, E, N, 1, opMN(a.act, h), opMN(m->dx, E), epi(EPI_ACCUM, G + L.w2, E), flags, mp(m)));
+      RC(gemm_tf32(st, N, E, 2 * h, 1, opK(m->dpre, 2 * h), opK(P + L.w1, 2 * h), epi(EPI_STORE, m->dy, E), flags, mp(m)));
+      RC(gemm_tf32(st, E, 2 * h, N, 1, opMN(a.y2, E), opMN(m->dpre, 2 * h), epi(EPI_ACCUM, G + L.w1, 2 * h), flags, mp(m)));
     } else {
       GemmEpi e = epi(EPI_GELU_BWD, m->dpre, h);
       e.R = a.pre;
       e.ldr = h;
-      RC(gemm_tf32(st, N, h, E, 1, opK(m->dx, E), opK(P + L.w2, E), e, flags, m->ctx->precision));
-      RC(gemm_tf32(st, h, E, N, 1, opMN(a.act, h), opMN(m->dx, E), epi(EPI_ACCUM, G + L.w2, E), flags, m->ctx->precision));
+      RC(gemm_tf32(st, N, h, E, 1, opK(m->dx, E), opK(P + L.w2, E), e, flags, mp(m)));
+      RC(gemm_tf32(st, h, E, N, 1, opMN(a.act, h), opMN(m->dx, E), epi(EPI_ACCUM, G + L.w2, E), flags, mp(m)));
       RC(colsum_accum(st, m->dx, N, E, G + L.b2, m->part));
-      RC(gemm_tf32(st, N, E, h, 1, opK(m->dpre, h), opK(P + L.w1, h), epi(EPI_STORE, m->dy, E), flags, m->ctx->precision));
-      RC(gemm_tf32(st, E, h, N, 1, opMN(a.y2, E), opMN(m->dpre, h), epi(EPI_ACCUM, G + L.w1, h), flags, m->ctx->precision));
+      RC(gemm_tf32(st, N, E, h, 1, opK(m->dpre, h), opK(P + L.w1, h), epi(EPI_STORE, m->dy, E), flags, mp(m)));
+      RC(gemm_tf32(st, E, h, N, 1, opMN(a.y2, E), opMN(m->dpre, h), epi(EPI_ACCUM, G + L.w1, h), flags, mp(m)));
       RC(colsum_accum(st, m->dpre, N, h, G + L.b1, m->part));
     }
     if (m->modern)
@@ -356,13 +359,13 @@ int backward(turt_model* m, int B, int T) {
     else
       RC(ln_bwd(st, a.h, m->dy, P + L.ln2g, a.mu2, a.rs2, m->dx, m->dx, G + L.ln2g, G + L.ln2b, m->part, N, E));
     // ---- attention
-    RC(gemm_tf32(st, N, E, E, 1, opK(m->dx, E), opK(P + L.wproj, E), epi(EPI_STORE, m->datt, E), flags, m->ctx->precision));
-    RC(gemm_tf32(st, E, E, N, 1, opMN(a.att, E), opMN(m->dx, E), epi(EPI_ACCUM, G + L.wproj, E), flags, m->ctx->precision));
+    RC(gemm_tf32(st, N, E, E, 1, opK(m->dx, E), opK(P + L.wproj, E), epi(EPI_STORE, m->datt, E), flags, mp(m)));
+    RC(gemm_tf32(st, E, E, N, 1, opMN(a.att, E), opMN(m->dx, E), epi(EPI_ACCUM, G + L.wproj, E), flags, mp(m)));
     if (!m->modern) RC(colsum_accum(st, m->dx, N, E, G + L.bproj, m->part));
     RC(attention_bwd(st, a.qkv, m->rope_cs, a.att, m->datt, a.lse, m->Dsc, m->dqkv, B, T, H, hd, m->modern ? 1 : 0));
     if (!m->modern) RC(colsum_accum(st, m->dqkv, N, 3 * E, G + L.bqkv, m->part));
-    RC(gemm_tf32(st, N, E, 3 * E, 1, opK(m->dqkv, 3 * E), opK(P + L.wqkv, 3 * E), epi(EPI_STORE, m->dy, E), flags, m->ctx->precision));
-    RC(gemm_tf32(st, E, 3 * E, N, 1, opMN(a.y1, E), opMN(m->dqkv, 3 * E), epi(EPI_ACCUM, G + L.wqkv, 3 * E), flags, m->ctx->precision));
+    RC(gemm_tf32(st, N, E, 3 * E, 1, opK(m->dqkv, 3 * E), opK(P + L.wqkv, 3 * E), epi(EPI_STORE, m->dy, E), flags, mp(m)));
+    RC(gemm_tf32(st, E, 3 * E, N, 1, opMN(a.y1, E), opMN(m->dqkv, 3 * E), epi(EPI_ACCUM, G + L.wqkv, 3 * E), flags, mp(m)));
     if (m->modern)
       RC(rms_bwd(st, a.x, m->dy, P + L.ln1g, a.rs1, m->dx, m->dx, G + L.ln1g, m->part, N, E));
     else

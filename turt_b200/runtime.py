@@ -30,7 +30,7 @@ class Context:
         check(lib().turt_ctx_set_stream(self._h, stream_ptr))
 
     def set_precision(self, precision: int) -> None:
-        """1 = plain TF32, 3 = error-compensated 3xTF32 (default)."""
+        """0 = fp32 CUDA cores (op level only), 1 = plain TF32, 3 = error-compensated 3xTF32 (default)."""
         check(lib().turt_set_precision(self._h, precision))
 
     @staticmethod
