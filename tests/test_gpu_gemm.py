@@ -97,3 +97,40 @@ def test_simt_fallback_odd_pitch(ctx):
     check(lib().turt_matmul_into(ctx.handle, da, db, dc, M, K, N, 1, 0, 0, 0))
     got = ctx.download(dc, M * N).reshape(M, N)
     np.testing.assert_allclose(got, a.astype(np.float64) @ b, rtol=1e-5, atol=1e-5)
+
+
+@pytest.fixture
+def tile():
+    """Forces the GEMM tile width for one test and restores automatic selection after it."""
+    from turt_b200._lib import check, lib
+    yield lambda bn: check(lib().turt_gemm_set_tile(bn))
+    check(lib().turt_gemm_set_tile(0))
+
+
+@pytest.mark.parametrize("bn", [64, 128, 192, 256])
+@pytest.mark.parametrize("M,K,N", [(1000, 200, 520), (2048, 384, 1152), (384, 8192, 384)])
+@pytest.mark.parametrize("transA,transB", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("prec", [1, 3])
+def test_tile_widths(ctx, tile, bn, M, K, N, transA, transB, prec):
+    """Every tile width on every layout: ragged edges, several work units per persistent CTA
+    (both TMEM accumulator buffers, ring phases wrapping), and split-K (K 8192 output 384^2)."""
+    from turt_b200._lib import check, lib
+    tile(bn)
+    check(lib().turt_set_precision(ctx.handle, prec))
+    rng = np.random.default_rng(bn + M + K + N + 10 * transA + transB + prec)
+    a = rng.uniform(-1, 1, (K, M) if transA else (M, K)).astype(np.float32)
+    b = rng.uniform(-1, 1, (N, K) if transB else (K, N)).astype(np.float32)
+    ref = (a.T if transA else a).astype(np.float64) @ (b.T if transB else b).astype(np.float64)
+    da, db, dc = ctx.buffer(a.size), ctx.buffer(b.size), ctx.buffer(M * N)
+    try:
+        ctx.upload(da, a)
+        ctx.upload(db, b)
+        check(lib().turt_matmul_into(ctx.handle, da, db, dc, M, K, N, 1, transA, transB, 0))
+        assert _norm_err(ctx.download(dc, M * N).reshape(M, N), ref) < TOL[prec]
+        check(lib().turt_matmul_into(ctx.handle, da, db, dc, M, K, N, 1, transA, transB, 1))
+        assert _norm_err(ctx.download(dc, M * N).reshape(M, N), 2 * ref) < TOL[prec]
+    finally:
+        check(lib().turt_set_precision(ctx.handle, 3))
+        for p in (da, db, dc):
+            ctx.free(p)
+        ctx.reclaim()

@@ -148,3 +148,17 @@ def test_sequence_longer_than_block_rejected(ctx):
         assert ei.value.code == ERR_INVALID
     finally:
         model.close()
+
+
+@pytest.mark.parametrize("bn", [64, 128, 192, 256])
+@pytest.mark.parametrize("arch", ["gpt2", "modern"])
+def test_fused_epilogues_every_tile_width(ctx, orc, arch, bn):
+    """Bias / GELU / SwiGLU / residual epilogues under each forced GEMM tile width."""
+    from turt_b200._lib import check, lib
+    check(lib().turt_gemm_set_tile(bn))
+    try:
+        loss, ref, le, ge, name = _run_parity(ctx, orc, 512, 96, 2, 2, 128, arch, 3, 80, 352 if arch == "modern" else 0)
+    finally:
+        check(lib().turt_gemm_set_tile(0))
+    assert le <= LOSS_TOL, (loss, ref)
+    assert ge <= GRAD_TOL, (ge, name)

@@ -128,6 +128,12 @@ int turt_get_precision(turt_ctx* ctx, int* precision) {
   return OK;
 }
 
+int turt_gemm_set_tile(int bn) {
+  TURT_REQUIRE(bn == 0 || bn == 64 || bn == 128 || bn == 192 || bn == 256, "tile width must be 0, 64, 128, 192 or 256");
+  gemm_set_tile_override(bn);
+  return OK;
+}
+
 int turt_synchronize(turt_ctx* ctx) {
   CTX_GUARD(ctx);
   TURT_CHECK_CUDA(cudaStreamSynchronize(ctx->stream));

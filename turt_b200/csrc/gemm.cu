@@ -11,6 +11,8 @@
 // the tensors where they lie.
 #include <cuda.h>
 
+#include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "gemm.cuh"
@@ -20,9 +22,6 @@ namespace turt {
 namespace {
 
 constexpr int BM = 128;
-constexpr int BK = 32;  // fp32 elements per k-tile = one 128-byte swizzle row
-constexpr int A_TILE_BYTES = BM * BK * 4;
-constexpr int MN_BOX_BYTES = 32 * BK * 4;  // one 32(MN) x 32(K) box of an MN-major operand
 
 // ------------------------------------------------------------ PTX wrappers
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
@@ -39,11 +38,13 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 
 // Shared-memory matrix descriptor (tcgen05 format): start>>4 [0,14), LBO>>4 [16,30),
 // SBO>>4 [32,46), version 1 [46,48), layout type [61,64).
-// K-major operands use the 128-byte swizzle (type 2: 16-byte chunks XOR row%8, 8-row atoms).
+// K-major operands use the 128-byte swizzle (type 2: 16-byte chunks XOR row%8, 8-row atoms)
+// for 32-float k-tiles, or the 64-byte swizzle (type 4: 8 rows of 64 bytes) for 16-float ones.
 // MN-major tf32 operands must use the 128-byte swizzle with 32-byte atomicity (type 1:
 // 32-byte chunks XOR row%4, 4-row atoms); it is the only MN-major layout tf32 accepts.
 constexpr uint32_t kLayoutSW128 = 2;
 constexpr uint32_t kLayoutSW128Atom32 = 1;
+constexpr uint32_t kLayoutSW64 = 4;
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
@@ -54,14 +55,8 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
   return d;
 }
 
-// Instruction descriptor for kind::tf32: D fp32 [4,6)=1, A tf32 [7,10)=2, B tf32 [10,13)=2,
-// A major [15], B major [16], N>>3 [17,23), M>>4 [24,29).
-template <int BN, bool A_MN, bool B_MN>
-__device__ __forceinline__ uint32_t instr_desc() {
-  return (1u << 4) | (2u << 7) | (2u << 10) | ((A_MN ? 1u : 0u) << 15) | ((B_MN ? 1u : 0u) << 16) |
-         ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-}
-
+// Instruction descriptor for kind::tf32 (built inside the kernel): D fp32 [4,6)=1, A tf32
+// [7,10)=2, B tf32 [10,13)=2, A major [15], B major [16], N>>3 [17,23), M>>4 [24,29).
 __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                          uint32_t accumulate) {
   asm volatile(
@@ -95,21 +90,23 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 }
 
 // ------------------------------------------------------------ epilogue
-// Applies the epilogue to 32 consecutive accumulator columns [col0, col0+32) of `row`.
-__device__ __forceinline__ void store32(float* dst, const float* v, int ncols, bool vec) {
-  if (vec && ncols >= 32) {
+// One epilogue lane owns one accumulator row; `v` holds 32 consecutive columns of it.
+__device__ __forceinline__ void st32(float* dst, const float* v, int n, bool vec) {
+  if (vec && n >= 32) {
 #pragma unroll
     for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
   } else {
-    for (int j = 0; j < ncols && j < 32; j++) dst[j] = v[j];
+#pragma unroll
+    for (int j = 0; j < 32; j++)
+      if (j < n) dst[j] = v[j];
   }
 }
 
-__device__ __forceinline__ void load32(const float* src, float* v, int ncols, bool vec) {
-  if (vec && ncols >= 32) {
+__device__ __forceinline__ void ld32(const float* src, float* v, int n, bool vec) {
+  if (vec && n >= 32) {
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
-      float4 t = *reinterpret_cast<const float4*>(src + j);
+      const float4 t = *reinterpret_cast<const float4*>(src + j);
       v[j] = t.x;
       v[j + 1] = t.y;
       v[j + 2] = t.z;
@@ -117,40 +114,163 @@ __device__ __forceinline__ void load32(const float* src, float* v, int ncols, bo
     }
   } else {
 #pragma unroll
-    for (int j = 0; j < 32; j++) v[j] = j < ncols ? src[j] : 0.0f;
+    for (int j = 0; j < 32; j++) v[j] = j < n ? src[j] : 0.0f;
   }
 }
 
+struct EpiVec {
+  bool C, R, C2;
+};
+
+// Columns [col0, col0 + 32) of one output row (every kind except the fused SwiGLU forward).
+__device__ __forceinline__ void epi_chunk(const GemmEpi& epi, const EpiVec& vec, float* v, float* Cb, long row,
+                                          int col0, int n, int batch) {
+  float* dst = Cb + row * epi.ldc + col0;
+  switch (epi.kind) {
+    case EPI_STORE:
+      st32(dst, v, n, vec.C);
+      break;
+    case EPI_ACCUM: {
+      float o[32];
+      ld32(dst, o, n, vec.C);
+#pragma unroll
+      for (int j = 0; j < 32; j++) v[j] += o[j];
+      st32(dst, v, n, vec.C);
+    } break;
+    case EPI_RED:
+      if (vec.C && n >= 32) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          atomicAdd(reinterpret_cast<float4*>(dst + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+          if (j < n) atomicAdd(dst + j, v[j]);
+      }
+      break;
+    case EPI_ADD_RES: {
+      float o[32];
+      ld32(epi.R + (long)batch * epi.strideC + row * epi.ldr + col0, o, n, vec.R);
+#pragma unroll
+      for (int j = 0; j < 32; j++) v[j] += o[j];
+      if (epi.bias) {
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] += j < n ? epi.bias[col0 + j] : 0.0f;
+      }
+      st32(dst, v, n, vec.C);
+    } break;
+    case EPI_BIAS:
+    case EPI_BIAS_GELU:
+#pragma unroll
+      for (int j = 0; j < 32; j++) v[j] += j < n ? epi.bias[col0 + j] : 0.0f;
+      st32(dst, v, n, vec.C);
+      if (epi.kind == EPI_BIAS_GELU) {
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] = gelu_f(v[j]);
+        st32(epi.C2 + row * epi.ldc2 + col0, v, n, vec.C2);
+      }
+      break;
+    case EPI_GELU_BWD: {
+      float z[32];
+      ld32(epi.R + row * epi.ldr + col0, z, n, vec.R);
+#pragma unroll
+      for (int j = 0; j < 32; j++) v[j] *= gelu_grad_f(z[j]);
+      st32(dst, v, n, vec.C);
+    } break;
+    case EPI_SWIGLU_BWD: {
+      // v = d(act) for hidden units [col0, col0+32); pre-activations and outputs are interleaved.
+      const long ic = (long)(col0 / kGluBlock) * (2 * kGluBlock);
+      const float* pg = epi.R + row * epi.ldr + ic;
+      float* o = epi.C + row * epi.ldc + ic;
+#pragma unroll
+      for (int j0 = 0; j0 < 32; j0 += 8) {
+        float g[8], u[8], dg[8], du[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          g[j] = j0 + j < n ? pg[j0 + j] : 0.0f;
+          u[j] = j0 + j < n ? pg[kGluBlock + j0 + j] : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const float s = sigmoid_f(g[j]);
+          const float sl = g[j] * s;
+          du[j] = v[j0 + j] * sl;
+          dg[j] = v[j0 + j] * u[j] * (s + sl * (1.0f - s));
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+          if (j0 + j < n) {
+            o[j0 + j] = dg[j];
+            o[kGluBlock + j0 + j] = du[j];
+          }
+      }
+    } break;
+    default:
+      break;
+  }
+}
+
+// ------------------------------------------------------------ kernel
+// Persistent: one CTA per SM walks the (batch, k-split, n-tile, m-tile) work units
+// blockIdx.x, blockIdx.x + gridDim.x, ...  The producer and the MMA issuer run ahead
+// across unit boundaries; the accumulator is double-buffered in TMEM (2 x BN columns), so
+// the epilogue of one unit overlaps the mainloop of the next.
+//
+// Warp roles:
+//   warp 0        TMA producer (one elected lane)
+//   warp 1        TMEM allocator + MMA issuer (one elected lane)
+//   warps 2..5    epilogue; warp w reads TMEM lanes 32*(w%4) .. 32*(w%4)+31
+//   warps 6..9    (X3 only) lo-part converters
+//
 // X3 = error-compensated 3xTF32 (Ootomo & Yokota, 2022): every operand x is split as
 // x = hi + lo with hi = x truncated to tf32 (what the tensor core reads from the raw fp32
 // bits) and lo = x - hi (exact in fp32); the product is accumulated as
-// hi*hi + hi*lo + lo*hi, which keeps ~21 mantissa bits instead of tf32's 10.  The lo
-// tiles are produced in shared memory by the (otherwise idle) epilogue warps while the
-// mainloop runs, in the same swizzled layout as the TMA-written tiles.
-template <int BN, bool A_MN, bool B_MN, int STAGES, bool X3>
-__global__ void __launch_bounds__(192, 1)
+// lo*hi + hi*lo + hi*hi, which keeps ~21 mantissa bits instead of tf32's 10.  The lo tiles
+// are written to shared memory by the converter warps in the same swizzled layout as the
+// TMA-written hi tiles.
+//
+// Shared-memory layouts (per stage: [A hi | B hi | A lo | B lo]):
+//   K-major, BK = 32: rows of 128 B, 128-byte swizzle (8-row atoms of 1 KB)
+//   K-major, BK = 16: rows of 64 B, 64-byte swizzle (8-row atoms of 512 B)
+//   MN-major: 32 (MN) x BK (K) TMA boxes of 128-byte K-rows, 128-byte swizzle with 32-byte
+//             atomicity (4-row atoms of 512 B); the only MN-major layout tf32 accepts.
+template <int BN, int BK, bool X3>
+struct GemmShape {
+  static constexpr int A_BYTES = BM * BK * 4;
+  static constexpr int B_BYTES = BN * BK * 4;
+  static constexpr int HI_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGE_BYTES = HI_BYTES * (X3 ? 2 : 1);
+  static constexpr int MN_BOX = 32 * BK * 4;
+  static constexpr int THREADS = X3 ? 320 : 192;
+  static constexpr uint32_t TMEM_COLS = 2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512);
+  static constexpr int STAGES_FIT = (232448 - 1024 - 256) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+template <int BN, int BK, bool A_MN, bool B_MN, bool X3>
+__global__ void __launch_bounds__(GemmShape<BN, BK, X3>::THREADS, 1)
     k_gemm_tf32(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmEpi epi,
-                int M, int N, int K, int ksplits, int kt_per_split, int* flags) {
-  constexpr int B_TILE_BYTES = BN * BK * 4;
-  constexpr int HI_BYTES = A_TILE_BYTES + B_TILE_BYTES;
-  constexpr int STAGE_BYTES = HI_BYTES * (X3 ? 2 : 1);
-  constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+                int M, int N, int K, int batches, int ksplits, int kt_per_split, int* flags) {
+  using S = GemmShape<BN, BK, X3>;
+  constexpr int STAGES = S::STAGES;
+  static_assert(BK == 16 || BK == 32, "BK");
+  static_assert(BN % 64 == 0 && BN <= 256, "BN");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * S::STAGE_BYTES);
   uint64_t* conv = full + STAGES;
   uint64_t* empty = conv + STAGES;
-  uint64_t* accum_bar = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_bar + 1);
+  uint64_t* tfull = empty + STAGES;  // [2] accumulator ready (MMA -> epilogue)
+  uint64_t* tempty = tfull + 2;      // [2] accumulator drained (epilogue -> MMA)
+  uint64_t* done = tempty + 2;       // every MMA of this CTA retired
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
-  const int batch = blockIdx.z / ksplits, split = blockIdx.z % ksplits;
+  const int mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;
+  const int units = mt * nt * ksplits * batches;
   const int kt_total = (K + BK - 1) / BK;
-  const int kt0 = split * kt_per_split;
-  const int kt1 = min(kt_total, kt0 + kt_per_split);
-  const int nkt = kt1 - kt0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
@@ -158,13 +278,17 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&conv[s], 4);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum_bar, 1);
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    mbar_init(done, 1);
     *abort_flag = 0;
     mbar_fence_init();
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(TMEM_COLS)
+                 "r"(S::TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -173,21 +297,25 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // unit -> (m0, n0, batch, first k-tile, k-tile count)
+  auto decode = [&](int u, int& m0, int& n0, int& b, int& kt0, int& nkt) {
+    m0 = (u % mt) * BM;
+    u /= mt;
+    n0 = (u % nt) * BN;
+    u /= nt;
+    const int split = u % ksplits;
+    b = u / ksplits;
+    kt0 = split * kt_per_split;
+    nkt = min(kt_total, kt0 + kt_per_split) - kt0;
+  };
+
   if (warp == 0) {
-    if (lane == 0 && nkt > 0) {
+    if (lane == 0) {
       // ------------------------------------------------ TMA producer
-      for (int i = 0; i < nkt; i++) {
-        const int s = i % STAGES;
-        if (i >= STAGES) {
-          if (!mbar_wait(&empty[s], ((i / STAGES) + 1) & 1, flags, 101)) {
-            *abort_flag = 1;
-            break;
-          }
-        }
-        if (*abort_flag) break;
-        const int kc = (kt0 + i) * BK;
-        const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
-        const uint32_t sb = sa + A_TILE_BYTES;
+      uint32_t it = 0;
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+        int m0, n0, b, kt0, nkt;
+        decode(u, m0, n0, b, kt0, nkt);
         // Boxes that start beyond M (or N) only feed output rows (columns) that are never
         // written, so they are skipped and not counted.
         int na = 1, nb = 1;
@@ -199,73 +327,111 @@ __global__ void __launch_bounds__(192, 1)
           nb = 0;
           for (int j = 0; j < BN / 32; j++) nb += (n0 + 32 * j < N);
         }
-        const uint32_t bytes = (A_MN ? na * MN_BOX_BYTES : A_TILE_BYTES) + (B_MN ? nb * MN_BOX_BYTES : B_TILE_BYTES);
-        mbar_arrive_expect_tx(&full[s], bytes);
-        if (!A_MN) {
-          tma_load_3d(sa, &tmA, kc, m0, batch, &full[s]);
-        } else {
-          for (int j = 0; j < BM / 32; j++)
-            if (m0 + 32 * j < M) tma_load_3d(sa + j * MN_BOX_BYTES, &tmA, m0 + 32 * j, kc, batch, &full[s]);
-        }
-        if (!B_MN) {
-          tma_load_3d(sb, &tmB, kc, n0, batch, &full[s]);
-        } else {
-          for (int j = 0; j < BN / 32; j++)
-            if (n0 + 32 * j < N) tma_load_3d(sb + j * MN_BOX_BYTES, &tmB, n0 + 32 * j, kc, batch, &full[s]);
+        const uint32_t bytes = (A_MN ? na * S::MN_BOX : S::A_BYTES) + (B_MN ? nb * S::MN_BOX : S::B_BYTES);
+        for (int i = 0; i < nkt; i++, it++) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&empty[s], ((it / STAGES) + 1) & 1, flags, 101)) {
+            *abort_flag = 1;
+            break;
+          }
+          const int kc = (kt0 + i) * BK;
+          const uint32_t sa = smem_u32(smem + s * S::STAGE_BYTES);
+          const uint32_t sb = sa + S::A_BYTES;
+          mbar_arrive_expect_tx(&full[s], bytes);
+          if (!A_MN) {
+            tma_load_3d(sa, &tmA, kc, m0, b, &full[s]);
+          } else {
+            for (int j = 0; j < BM / 32; j++)
+              if (m0 + 32 * j < M) tma_load_3d(sa + j * S::MN_BOX, &tmA, m0 + 32 * j, kc, b, &full[s]);
+          }
+          if (!B_MN) {
+            tma_load_3d(sb, &tmB, kc, n0, b, &full[s]);
+          } else {
+            for (int j = 0; j < BN / 32; j++)
+              if (n0 + 32 * j < N) tma_load_3d(sb + j * S::MN_BOX, &tmB, n0 + 32 * j, kc, b, &full[s]);
+          }
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && nkt > 0) {
+    if (lane == 0) {
       // ------------------------------------------------ MMA issuer
-      const uint32_t idesc = instr_desc<BN, A_MN, B_MN>();
-      for (int i = 0; i < nkt; i++) {
-        const int s = i % STAGES;
-        if (!mbar_wait(X3 ? &conv[s] : &full[s], (i / STAGES) & 1, flags, 102)) {
+      constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((A_MN ? 1u : 0u) << 15) |
+                                 ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+      constexpr uint32_t kKLayout = BK == 32 ? kLayoutSW128 : kLayoutSW64;
+      constexpr uint32_t kKSbo = BK == 32 ? 1024 : 512;
+      uint32_t it = 0;
+      int t = 0;
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x, t++) {
+        int m0, n0, b, kt0, nkt;
+        decode(u, m0, n0, b, kt0, nkt);
+        const int acc = t & 1;
+        if (!mbar_wait(&tempty[acc], ((t >> 1) + 1) & 1, flags, 105)) {
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
-        const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
-        const uint32_t sb = sa + A_TILE_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < BK / 8; kk++) {
-          // K-major: advance 8 tf32 (32 bytes) inside the 128-byte swizzle row; 8-row atoms 1 KB apart.
-          // MN-major: advance 8 K-rows (two 4-row atoms, 1 KB); atoms along K are 512 B apart,
-          // 32-element MN column blocks (one TMA box each) 4 KB apart.
-          const uint32_t oa = A_MN ? kk * 1024 : kk * 32, ob = B_MN ? kk * 1024 : kk * 32;
-          const uint64_t da = A_MN ? smem_desc(sa + oa, MN_BOX_BYTES, 512, kLayoutSW128Atom32)
-                                   : smem_desc(sa + oa, 16, 1024, kLayoutSW128);
-          const uint64_t db = B_MN ? smem_desc(sb + ob, MN_BOX_BYTES, 512, kLayoutSW128Atom32)
-                                   : smem_desc(sb + ob, 16, 1024, kLayoutSW128);
-          if (X3) {
-            // lo tiles sit HI_BYTES after the hi tiles with the same layout: bump the start address.
-            const uint64_t lo = (uint64_t)(HI_BYTES >> 4);
-            mma_tf32(tmem, da + lo, db, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-            mma_tf32(tmem, da, db + lo, idesc, 1u);
-            mma_tf32(tmem, da, db, idesc, 1u);
-          } else {
-            mma_tf32(tmem, da, db, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+        const uint32_t d = tmem + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int i = 0; i < nkt; i++, it++) {
+          const int s = it % STAGES;
+          if (!mbar_wait(X3 ? &conv[s] : &full[s], (it / STAGES) & 1, flags, 102)) {
+            ok = false;
+            break;
           }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * S::STAGE_BYTES);
+          const uint32_t sb = sa + S::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; kk++) {
+            // K-major: advance 8 tf32 (32 bytes) inside the swizzle row.  MN-major: advance 8
+            // K-rows (two 4-row atoms, 1 KB); TMA boxes (32-element MN blocks) MN_BOX apart.
+            const uint32_t oa = A_MN ? kk * 1024 : kk * 32, ob = B_MN ? kk * 1024 : kk * 32;
+            const uint64_t da = A_MN ? smem_desc(sa + oa, S::MN_BOX, 512, kLayoutSW128Atom32)
+                                     : smem_desc(sa + oa, 16, kKSbo, kKLayout);
+            const uint64_t db = B_MN ? smem_desc(sb + ob, S::MN_BOX, 512, kLayoutSW128Atom32)
+                                     : smem_desc(sb + ob, 16, kKSbo, kKLayout);
+            const uint32_t first = (i > 0 || kk > 0) ? 1u : 0u;
+            if (X3) {
+              // lo tiles sit HI_BYTES after the hi tiles with the same layout: bump the start address.
+              const uint64_t lo = (uint64_t)(S::HI_BYTES >> 4);
+              mma_tf32(d, da + lo, db, idesc, first);
+              mma_tf32(d, da, db + lo, idesc, 1u);
+              mma_tf32(d, da, db, idesc, 1u);
+            } else {
+              mma_tf32(d, da, db, idesc, first);
+            }
+          }
+          mma_commit(&empty[s]);
         }
-        mma_commit(&empty[s]);
-      }
-      mma_commit(accum_bar);
-    }
-  } else {
-    if (X3) {
-      // ------------------------------------------ lo-part converters (warps 2..5)
-      const int ct = threadIdx.x - 64;
-      for (int i = 0; i < nkt; i++) {
-        const int s = i % STAGES;
-        if (!mbar_wait(&full[s], (i / STAGES) & 1, flags, 104)) {
+        if (!ok) {
           *abort_flag = 1;
           break;
         }
-        const float4* hi = reinterpret_cast<const float4*>(smem + s * STAGE_BYTES);
-        float4* lo = reinterpret_cast<float4*>(smem + s * STAGE_BYTES + HI_BYTES);
+        mma_commit(&tfull[acc]);
+      }
+      // TMEM is released only after every MMA this thread issued has retired.
+      mma_commit(done);
+      if (!mbar_wait(done, 0, flags, 106)) *abort_flag = 1;
+    }
+  } else if (warp >= 6) {
+    // -------------------------------------------------- lo-part converters (X3)
+    const int ct = threadIdx.x - 192;
+    uint32_t it = 0;
+    for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+      int m0, n0, b, kt0, nkt;
+      decode(u, m0, n0, b, kt0, nkt);
+      bool ok = true;
+      for (int i = 0; i < nkt; i++, it++) {
+        const int s = it % STAGES;
+        if (!mbar_wait(&full[s], (it / STAGES) & 1, flags, 104)) {
+          ok = false;
+          break;
+        }
+        const float4* hi = reinterpret_cast<const float4*>(smem + s * S::STAGE_BYTES);
+        float4* lo = reinterpret_cast<float4*>(smem + s * S::STAGE_BYTES + S::HI_BYTES);
 #pragma unroll 4
-        for (int e = ct; e < HI_BYTES / 16; e += 128) {
+        for (int e = ct; e < S::HI_BYTES / 16; e += 128) {
           const float4 v = hi[e];
           float4 r;
           r.x = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
@@ -279,120 +445,67 @@ __global__ void __launch_bounds__(192, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&conv[s]);
       }
+      if (!ok) {
+        *abort_flag = 1;
+        break;
+      }
     }
-    // -------------------------------------------------- epilogue warps
-    const bool ok = nkt > 0 && mbar_wait(accum_bar, 0, flags, 103);
-    tc_fence_after();
-    if (ok && !*abort_flag) {
-      const int q = warp & 3;
-      const int row = m0 + q * 32 + lane;
-      const bool row_ok = row < M;
-      float* Cb = epi.C + (long)batch * epi.strideC;
-      const bool vecC = (epi.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(epi.C) & 15) == 0) &&
-                        ((epi.strideC % 4) == 0);
+  } else {
+    // -------------------------------------------------- epilogue warps (2..5)
+    const int q = warp & 3;
+    const EpiVec vec{(epi.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(epi.C) & 15) == 0) && (epi.strideC % 4 == 0),
+                     epi.R && (epi.ldr % 4 == 0) && ((reinterpret_cast<uintptr_t>(epi.R) & 15) == 0),
+                     epi.C2 && (epi.ldc2 % 4 == 0) && ((reinterpret_cast<uintptr_t>(epi.C2) & 15) == 0)};
+    int t = 0;
+    for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x, t++) {
+      int m0, n0, b, kt0, nkt;
+      decode(u, m0, n0, b, kt0, nkt);
+      const int acc = t & 1;
+      if (!mbar_wait(&tfull[acc], (t >> 1) & 1, flags, 103)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const long row = m0 + q * 32 + lane;
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      float* Cb = epi.C + (long)b * epi.strideC;
       if (epi.kind == EPI_SWIGLU_FWD) {
-        // Chunk pairs (gate, up) -> C keeps the pre-activations, C2 gets silu(gate) * up.
+        // Chunk pairs (gate, up): C keeps both pre-activations, C2 gets silu(gate) * up.
+#pragma unroll 1
         for (int c = 0; c < BN / 32; c += 2) {
-          float g[32], u[32];
-          tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, g);
-          tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (c + 1) * 32, u);
-          const int col = n0 + c * 32;
-          if (row_ok && col < N) {
-            float* dst = Cb + (long)row * epi.ldc + col;
-            store32(dst, g, N - col, vecC);
-            store32(dst + 32, u, N - col - 32, vecC);
-            float a[32];
+          const int col0 = n0 + c * 32;
+          float g[32], v[32];
+          tmem_ld32(tbase + c * 32, g);
+          tmem_ld32(tbase + (c + 1) * 32, v);
+          if (row < M && col0 < N) {
+            st32(Cb + row * epi.ldc + col0, g, min(32, N - col0), vec.C);
+            st32(Cb + row * epi.ldc + col0 + 32, v, min(32, N - col0 - 32), vec.C);
 #pragma unroll
-            for (int j = 0; j < 32; j++) a[j] = g[j] * sigmoid_f(g[j]) * u[j];
-            store32(epi.C2 + (long)row * epi.ldc2 + col / 2, a, (N - col) / 2, vecC && (epi.ldc2 % 4 == 0));
+            for (int j = 0; j < 32; j++) v[j] *= g[j] * sigmoid_f(g[j]);
+            st32(epi.C2 + row * epi.ldc2 + col0 / 2, v, min(32, N - col0 - 32), vec.C2);
           }
         }
       } else {
+#pragma unroll 1
         for (int c = 0; c < BN / 32; c++) {
+          const int col0 = n0 + c * 32;
+          if (col0 >= N) break;  // warp-uniform
           float v[32];
-          tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, v);
-          const int col = n0 + c * 32;
-          if (!row_ok || col >= N) continue;
-          const int ncols = min(32, N - col);
-          float* dst = Cb + (long)row * epi.ldc + col;
-          switch (epi.kind) {
-            case EPI_STORE:
-              store32(dst, v, ncols, vecC);
-              break;
-            case EPI_ACCUM: {
-              float o[32];
-              load32(dst, o, ncols, vecC);
-#pragma unroll
-              for (int j = 0; j < 32; j++) v[j] += o[j];
-              store32(dst, v, ncols, vecC);
-            } break;
-            case EPI_RED:
-              if (vecC && ncols == 32) {
-#pragma unroll
-                for (int j = 0; j < 32; j += 4)
-                  atomicAdd(reinterpret_cast<float4*>(dst + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
-              } else {
-                for (int j = 0; j < ncols; j++) atomicAdd(dst + j, v[j]);
-              }
-              break;
-            case EPI_ADD_RES: {
-              float o[32];
-              const bool vecR = vecC && (epi.ldr % 4 == 0) && ((reinterpret_cast<uintptr_t>(epi.R) & 15) == 0);
-              load32(epi.R + (long)batch * epi.strideC + (long)row * epi.ldr + col, o, ncols, vecR);
-#pragma unroll
-              for (int j = 0; j < 32; j++) v[j] += o[j];
-              if (epi.bias)
-                for (int j = 0; j < ncols; j++) v[j] += epi.bias[col + j];
-              store32(dst, v, ncols, vecC);
-            } break;
-            case EPI_BIAS:
-            case EPI_BIAS_GELU: {
-              for (int j = 0; j < 32; j++) v[j] += (j < ncols) ? epi.bias[col + j] : 0.0f;
-              store32(dst, v, ncols, vecC);
-              if (epi.kind == EPI_BIAS_GELU) {
-#pragma unroll
-                for (int j = 0; j < 32; j++) v[j] = gelu_f(v[j]);
-                store32(epi.C2 + (long)row * epi.ldc2 + col, v, ncols, vecC && (epi.ldc2 % 4 == 0));
-              }
-            } break;
-            case EPI_GELU_BWD: {
-              float x[32];
-              load32(epi.R + (long)row * epi.ldr + col, x, ncols, vecC && (epi.ldr % 4 == 0));
-#pragma unroll
-              for (int j = 0; j < 32; j++) v[j] *= gelu_grad_f(x[j]);
-              store32(dst, v, ncols, vecC);
-            } break;
-            case EPI_SWIGLU_BWD: {
-              // v = d(act) for hidden units [col, col+32); pre-activations and outputs are interleaved.
-              const long ic = (long)(col / kGluBlock) * (2 * kGluBlock);
-              const float* pg = epi.R + (long)row * epi.ldr + ic;
-              float g[32], u[32];
-              load32(pg, g, 32, vecC && (epi.ldr % 4 == 0));
-              load32(pg + kGluBlock, u, 32, vecC && (epi.ldr % 4 == 0));
-              float dg[32], du[32];
-#pragma unroll
-              for (int j = 0; j < 32; j++) {
-                const float s = sigmoid_f(g[j]);
-                const float sl = g[j] * s;
-                du[j] = v[j] * sl;
-                dg[j] = v[j] * u[j] * (s + sl * (1.0f - s));
-              }
-              float* o = epi.C + (long)row * epi.ldc + ic;
-              store32(o, dg, ncols, vecC);
-              store32(o + kGluBlock, du, ncols, vecC);
-            } break;
-            default:
-              break;
-          }
+          tmem_ld32(tbase + c * 32, v);
+          if (row < M) epi_chunk(epi, vec, v, Cb, row, col0, min(32, N - col0), b);
         }
       }
+      // hand the accumulator back to the MMA issuer
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S::TMEM_COLS) : "memory");
   }
 }
 
@@ -462,6 +575,8 @@ EncodeTiledFn get_encode() {
 }
 
 // 3-D tensor map over a row-major [batch][rows][inner] view with `ld` elements per row.
+// K-major operands take a box_inner-float-wide swizzle (128 B for 32 floats, 64 B for 16);
+// MN-major ones the 128-byte swizzle with 32-byte atomicity.
 int make_map(CUtensorMap* map, const float* base, long inner, long rows, long batch, long ld, long bstride,
              int box_inner, int box_rows, bool mn_major) {
   EncodeTiledFn enc = get_encode();
@@ -475,42 +590,16 @@ int make_map(CUtensorMap* map, const float* base, long inner, long rows, long ba
   cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)bs * 4};
   cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapSwizzle sw = mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                         : (box_inner == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (code " + std::to_string((int)r) + ")");
     return ERR_CUDA;
   }
   return OK;
-}
-
-template <int BN, bool A_MN, bool B_MN, int STAGES, bool X3>
-int launch(cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb, const GemmEpi& epi, int M, int N, int K,
-           int batch, int ksplits, int kt_per, int* flags) {
-  constexpr int smem = STAGES * (A_TILE_BYTES + BN * BK * 4) * (X3 ? 2 : 1) + 1024 + 256;
-  static_assert(smem <= 232448, "gemm: shared memory budget exceeded");
-  static bool configured = false;
-  auto kfn = k_gemm_tf32<BN, A_MN, B_MN, STAGES, X3>;
-  if (!configured) {
-    TURT_CHECK_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    configured = true;
-  }
-  dim3 grid(ceil_div(M, BM), ceil_div(N, BN), batch * ksplits);
-  kfn<<<grid, 192, smem, st>>>(ma, mb, epi, M, N, K, ksplits, kt_per, flags);
-  TURT_LAUNCH_CHECK();
-  return OK;
-}
-
-template <int BN, int STAGES, bool X3>
-int dispatch_major(cudaStream_t st, bool amn, bool bmn, const CUtensorMap& ma, const CUtensorMap& mb,
-                   const GemmEpi& epi, int M, int N, int K, int batch, int ks, int kt, int* flags) {
-  if (!amn && !bmn) return launch<BN, false, false, STAGES, X3>(st, ma, mb, epi, M, N, K, batch, ks, kt, flags);
-  if (!amn && bmn) return launch<BN, false, true, STAGES, X3>(st, ma, mb, epi, M, N, K, batch, ks, kt, flags);
-  if (amn && !bmn) return launch<BN, true, false, STAGES, X3>(st, ma, mb, epi, M, N, K, batch, ks, kt, flags);
-  return launch<BN, true, true, STAGES, X3>(st, ma, mb, epi, M, N, K, batch, ks, kt, flags);
 }
 
 int num_sms() {
@@ -524,7 +613,104 @@ int num_sms() {
   return n;
 }
 
+struct LaunchArgs {
+  cudaStream_t st;
+  CUtensorMap ma, mb;
+  GemmEpi epi;
+  int M, N, K, batch, ks, kt_per;
+  int* flags;
+};
+
+template <int BN, int BK, bool A_MN, bool B_MN, bool X3>
+int launch(const LaunchArgs& a) {
+  using S = GemmShape<BN, BK, X3>;
+  static_assert(S::SMEM <= 232448, "gemm: shared memory budget exceeded");
+  static_assert(S::STAGES >= 2, "gemm: fewer than two pipeline stages fit");
+  static bool configured = false;
+  auto kfn = k_gemm_tf32<BN, BK, A_MN, B_MN, X3>;
+  if (!configured) {
+    TURT_CHECK_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM));
+    configured = true;
+  }
+  const long units = (long)ceil_div(a.M, BM) * ceil_div(a.N, BN) * a.batch * a.ks;
+  const int grid = (int)(units < num_sms() ? units : num_sms());
+  kfn<<<grid, S::THREADS, S::SMEM, a.st>>>(a.ma, a.mb, a.epi, a.M, a.N, a.K, a.batch, a.ks, a.kt_per, a.flags);
+  TURT_LAUNCH_CHECK();
+  return OK;
+}
+
+template <int BN, int BK, bool X3>
+int dispatch_major(bool amn, bool bmn, const LaunchArgs& a) {
+  if (!amn && !bmn) return launch<BN, BK, false, false, X3>(a);
+  if (!amn && bmn) return launch<BN, BK, false, true, X3>(a);
+  if (amn && !bmn) return launch<BN, BK, true, false, X3>(a);
+  return launch<BN, BK, true, true, X3>(a);
+}
+
+template <bool X3>
+int dispatch_bn(int bn, bool amn, bool bmn, const LaunchArgs& a) {
+  constexpr int BK = X3 ? 16 : 32;
+  switch (bn) {
+    case 64:
+      return dispatch_major<64, BK, X3>(amn, bmn, a);
+    case 128:
+      return dispatch_major<128, BK, X3>(amn, bmn, a);
+    case 192:
+      return dispatch_major<192, BK, X3>(amn, bmn, a);
+    default:
+      return dispatch_major<256, BK, X3>(amn, bmn, a);
+  }
+}
+
+// Cost of one 32-deep k-step of a 128 x BN tile, in SM cycles, from the shared-memory
+// traffic it needs (TMA writes, tensor-core operand reads, 3xTF32 lo-part conversion) at
+// 128 B/cycle; it is above the tensor-pipe time of the step for every BN.
+long kstep_cycles(int bn, bool x3) {
+  const long bytes = x3 ? 98304 + 768L * bn : 32768 + 256L * bn;
+  return bytes / 128;
+}
+
+struct TilePlan {
+  int bn = 256;
+  int ks = 1;
+};
+
+// Tile width and K-split count with the shortest modelled makespan:
+//   ceil(units / SMs) x (k-steps per unit x step cost) + pipeline fill + one epilogue drain,
+// plus, per extra split, the atomic reduction of the M x N output.  `max_ks` is 1 when the
+// epilogue cannot accumulate partial sums.
+TilePlan plan_tiles(int M, int N, int K, int batch, bool x3, int max_ks, int force_bn) {
+  const int sms = num_sms();
+  const long k32 = (K + 31) / 32;
+  TilePlan best;
+  double best_cost = -1;
+  const int widths[4] = {256, 192, 128, 64};
+  for (int bn : widths) {
+    if (force_bn && bn != force_bn) continue;
+    if (!force_bn && bn > 64 && N <= bn / 2) continue;  // most of the tile would be empty
+    const long tiles = (long)ceil_div(M, BM) * ceil_div(N, bn) * batch;
+    for (int ks = 1; ks <= max_ks; ks++) {
+      if (ks > 1 && tiles * (ks - 1) >= sms) break;  // already a full wave without this split
+      const long units = tiles * ks;
+      const long rounds = (units + sms - 1) / sms;
+      const double steps = (double)((k32 + ks - 1) / ks);
+      double cost = rounds * steps * kstep_cycles(bn, x3) + 2000.0 + 16.0 * bn;
+      if (ks > 1) cost += (double)M * N * batch * ks / (sms * 8.0);  // float4 atomics
+      if (best_cost < 0 || cost < best_cost) {
+        best_cost = cost;
+        best.bn = bn;
+        best.ks = ks;
+      }
+    }
+  }
+  return best;
+}
+
+std::atomic<int> g_tile_override{0};
+
 }  // namespace
+
+void gemm_set_tile_override(int bn) { g_tile_override.store(bn); }
 
 bool gemm_tf32_supported(const GemmOperand& A, const GemmOperand& B) {
   auto ok = [](const GemmOperand& o) {
@@ -537,58 +723,54 @@ int gemm_tf32(cudaStream_t stream, int M, int N, int K, int batch, const GemmOpe
               const GemmEpi& epi_in, int* flags, int precision, int force_splits) {
   TURT_REQUIRE(M > 0 && N > 0 && batch > 0, "gemm: empty problem");
   TURT_REQUIRE(gemm_tf32_supported(A, B), "gemm: operand pitch/base not 16-byte aligned");
-  GemmEpi epi = epi_in;
   if (K == 0) {
     set_error("gemm: K == 0");
     return ERR_INVALID;
   }
-  // Tile width: the fused gate|up epilogue needs whole (gate, up) chunk pairs.
-  int BN = 128;
-  if (N <= 64) BN = 64;
-  const int tiles = ceil_div(M, BM) * ceil_div(N, BN) * batch;
+  const bool x3 = precision == GEMM_TF32X3;
+  const int BK = x3 ? 16 : 32;
+  int force_bn = g_tile_override.load();
+  if (force_bn != 64 && force_bn != 128 && force_bn != 192 && force_bn != 256) force_bn = 0;
+  LaunchArgs la;
+  la.st = stream;
+  la.epi = epi_in;
+  la.M = M;
+  la.N = N;
+  la.K = K;
+  la.batch = batch;
+  la.flags = flags;
+  // K is split (partial sums reduced with atomics) only when the output alone gives too few
+  // units to fill the GPU (weight gradients), with at least 256 of K per split.
+  const bool can_split = la.epi.kind == EPI_ACCUM || la.epi.kind == EPI_STORE || la.epi.kind == EPI_RED;
+  const int max_ks = force_splits > 0 ? 1 : (can_split ? std::max(1, K / 256) : 1);
+  const TilePlan plan = plan_tiles(M, N, K, batch, x3, std::min(max_ks, 64), force_bn);
+  const int BN = plan.bn;
   const int kt_total = ceil_div(K, BK);
-  int ks = 1;
-  if (force_splits > 0) {
-    ks = force_splits;
-  } else if ((epi.kind == EPI_ACCUM || epi.kind == EPI_STORE || epi.kind == EPI_RED) && tiles < num_sms() &&
-             kt_total >= 16) {
-    ks = num_sms() / tiles;
-    if (ks > kt_total / 8) ks = kt_total / 8;
-    if (ks < 1) ks = 1;
-  }
-  int kt_per = ceil_div(kt_total, ks);
-  ks = ceil_div(kt_total, kt_per);
-  if (ks > 1) {
+  const int ks = force_splits > 0 ? force_splits : plan.ks;
+  la.kt_per = ceil_div(kt_total, ks);
+  la.ks = ceil_div(kt_total, la.kt_per);
+  if (la.ks > 1) {
+    GemmEpi& epi = la.epi;
+    TURT_REQUIRE(can_split, "gemm: split-K needs an accumulating epilogue");
     if (epi.kind == EPI_STORE) {
-      TURT_CHECK_CUDA(cudaMemset2DAsync(epi.C, epi.ldc * 4, 0, (size_t)N * 4, (size_t)M, stream));
-      for (int b = 1; b < batch; b++)
+      for (int b = 0; b < batch; b++)
         TURT_CHECK_CUDA(
             cudaMemset2DAsync(epi.C + (long)b * epi.strideC, epi.ldc * 4, 0, (size_t)N * 4, (size_t)M, stream));
     }
-    TURT_REQUIRE(epi.kind == EPI_STORE || epi.kind == EPI_ACCUM || epi.kind == EPI_RED,
-                 "gemm: split-K needs an accumulating epilogue");
     epi.kind = EPI_RED;
   }
-  CUtensorMap ma, mb;
   int rc;
   if (!A.mn_major)
-    rc = make_map(&ma, A.ptr, K, M, batch, A.ld, A.stride, 32, BM, false);
+    rc = make_map(&la.ma, A.ptr, K, M, batch, A.ld, A.stride, BK, BM, false);
   else
-    rc = make_map(&ma, A.ptr, M, K, batch, A.ld, A.stride, 32, 32, true);
+    rc = make_map(&la.ma, A.ptr, M, K, batch, A.ld, A.stride, 32, BK, true);
   if (rc) return rc;
   if (!B.mn_major)
-    rc = make_map(&mb, B.ptr, K, N, batch, B.ld, B.stride, 32, BN, false);
+    rc = make_map(&la.mb, B.ptr, K, N, batch, B.ld, B.stride, BK, BN, false);
   else
-    rc = make_map(&mb, B.ptr, N, K, batch, B.ld, B.stride, 32, 32, true);
+    rc = make_map(&la.mb, B.ptr, N, K, batch, B.ld, B.stride, 32, BK, true);
   if (rc) return rc;
-  if (precision == GEMM_TF32X3) {
-    if (BN == 64)
-      return dispatch_major<64, 4, true>(stream, A.mn_major, B.mn_major, ma, mb, epi, M, N, K, batch, ks, kt_per, flags);
-    return dispatch_major<128, 3, true>(stream, A.mn_major, B.mn_major, ma, mb, epi, M, N, K, batch, ks, kt_per, flags);
-  }
-  if (BN == 64)
-    return dispatch_major<64, 8, false>(stream, A.mn_major, B.mn_major, ma, mb, epi, M, N, K, batch, ks, kt_per, flags);
-  return dispatch_major<128, 6, false>(stream, A.mn_major, B.mn_major, ma, mb, epi, M, N, K, batch, ks, kt_per, flags);
+  return x3 ? dispatch_bn<true>(BN, A.mn_major, B.mn_major, la) : dispatch_bn<false>(BN, A.mn_major, B.mn_major, la);
 }
 
 int gemm_simt(cudaStream_t stream, const float* A, const float* B, float* C, int M, int K, int N, int batch,

@@ -56,6 +56,9 @@ int gemm_tf32(cudaStream_t stream, int M, int N, int K, int batch, const GemmOpe
 // True when gemm_tf32 can take these operands (TMA needs 16-byte pitches and bases).
 bool gemm_tf32_supported(const GemmOperand& A, const GemmOperand& B);
 
+// Forces the output-tile width of every later gemm_tf32 call (64/128/192/256; 0 = automatic).
+void gemm_set_tile_override(int bn);
+
 // CUDA-core fp32 GEMM for shapes the TMA path cannot address (odd pitches): same
 // flags as the reference's MATMUL kernel (src/infer/webgpu/autograd.ts:33-75).
 int gemm_simt(cudaStream_t stream, const float* A, const float* B, float* C, int M, int K, int N, int batch,
