@@ -160,6 +160,17 @@ typedef struct turt_config {
 
 int turt_model_create(turt_ctx* ctx, const turt_config* cfg, turt_model** out);
 int turt_model_destroy(turt_model* model);
+/* Attention implementation of the model's fused train step.  No reference counterpart (the
+ * reference always materialises scores per head):
+ * TURT_ATTN_AUTO (default) = TURT_ATTN_TENSOR when the per-layer [B*H][T][T] probabilities
+ * of all layers fit a 16 GiB budget and the head dim is a multiple of 16, else TURT_ATTN_FLASH;
+ * TURT_ATTN_TENSOR = score / probability GEMMs on the tensor cores, probabilities kept for
+ * the backward pass; TURT_ATTN_FLASH = fused online-softmax kernels on the CUDA cores, no
+ * [T][T] buffers (head dim 16, 32 or 64). */
+#define TURT_ATTN_AUTO 0
+#define TURT_ATTN_TENSOR 1
+#define TURT_ATTN_FLASH 2
+int turt_model_set_attention(turt_model* model, int mode);
 /* parameters() order, gpu-gpt.ts:118-132: count, total scalars, per-tensor name and shape. */
 int turt_param_count(turt_model* model, int* count);
 int turt_num_params(turt_model* model, size_t* total);

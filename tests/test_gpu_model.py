@@ -36,7 +36,7 @@ def _tokens(orc, n, vocab, seed=99):
     return ids, tgt
 
 
-def _run_parity(ctx, orc, V, T, L, H, E, arch, b, t, hidden=0):
+def _run_parity(ctx, orc, V, T, L, H, E, arch, b, t, hidden=0, attn=0):
     from turt_b200.runtime import Model, make_config
     cfg = orc.cfg(V, T, L, H, E, arch, hidden)
     params = orc.init(cfg, 7)
@@ -44,6 +44,7 @@ def _run_parity(ctx, orc, V, T, L, H, E, arch, b, t, hidden=0):
     ref_loss, ref_g = orc.loss_grad(cfg, params, ids, tgt, b, t)
     model = Model(ctx, make_config(V, T, L, H, E, arch, hidden))
     try:
+        model.set_attention(attn)
         assert model.num_params() == orc.num_params(cfg)
         assert model.shapes == orc.param_shapes(cfg)
         model.load_flat(params)
@@ -64,25 +65,31 @@ def _run_parity(ctx, orc, V, T, L, H, E, arch, b, t, hidden=0):
     return loss, ref_loss, loss_err, worst, worst_name
 
 
+ATTN = [pytest.param(1, id="tensor-attn"), pytest.param(2, id="flash-attn")]
+
+
+@pytest.mark.parametrize("attn", ATTN)
 @pytest.mark.parametrize("arch", ["gpt2", "modern"])
-def test_validate_config(ctx, orc, arch):
+def test_validate_config(ctx, orc, arch, attn):
     """The reference's own validation config: V 48, block 16, 2 layers, 2 heads, E 32, b 2, t 8."""
-    loss, ref, le, ge, name = _run_parity(ctx, orc, 48, 16, 2, 2, 32, arch, 2, 8)
+    loss, ref, le, ge, name = _run_parity(ctx, orc, 48, 16, 2, 2, 32, arch, 2, 8, attn=attn)
     assert le <= LOSS_TOL, (loss, ref)
     assert ge <= GRAD_TOL, (ge, name)
 
 
+@pytest.mark.parametrize("attn", ATTN)
 @pytest.mark.parametrize("hidden", [320, 352])
-def test_tiny_modern_8x128(ctx, orc, hidden):
+def test_tiny_modern_8x128(ctx, orc, hidden, attn):
     """Tiny modern GPT (4 layers, 4 heads, d 128, vocab 8192, batch 8 x 128), SwiGLU 320 and 352."""
-    loss, ref, le, ge, name = _run_parity(ctx, orc, 8192, 128, 4, 4, 128, "modern", 8, 128, hidden)
+    loss, ref, le, ge, name = _run_parity(ctx, orc, 8192, 128, 4, 4, 128, "modern", 8, 128, hidden, attn)
     assert le <= LOSS_TOL, (loss, ref)
     assert ge <= GRAD_TOL, (ge, name)
 
 
-def test_gpt2_hd64(ctx, orc):
+@pytest.mark.parametrize("attn", ATTN)
+def test_gpt2_hd64(ctx, orc, attn):
     """gpt2 arch with head dim 64 and a ragged sequence length (t not a multiple of 64)."""
-    loss, ref, le, ge, name = _run_parity(ctx, orc, 512, 96, 2, 2, 128, "gpt2", 3, 80)
+    loss, ref, le, ge, name = _run_parity(ctx, orc, 512, 96, 2, 2, 128, "gpt2", 3, 80, attn=attn)
     assert le <= LOSS_TOL, (loss, ref)
     assert ge <= GRAD_TOL, (ge, name)
 
@@ -160,5 +167,15 @@ def test_fused_epilogues_every_tile_width(ctx, orc, arch, bn):
         loss, ref, le, ge, name = _run_parity(ctx, orc, 512, 96, 2, 2, 128, arch, 3, 80, 352 if arch == "modern" else 0)
     finally:
         check(lib().turt_gemm_set_tile(0))
+    assert le <= LOSS_TOL, (loss, ref)
+    assert ge <= GRAD_TOL, (ge, name)
+
+
+@pytest.mark.parametrize("arch", ["gpt2", "modern"])
+@pytest.mark.parametrize("t", [7, 130, 200])
+def test_tensor_attention_ragged(ctx, orc, arch, t):
+    """Tensor-core attention with sequence lengths that are not multiples of 4 (padded score
+    pitch), of the 128-row tile (diagonal tiles split), and above one tile; head dim 16."""
+    loss, ref, le, ge, name = _run_parity(ctx, orc, 256, 256, 2, 4, 64, arch, 2, t, attn=1)
     assert le <= LOSS_TOL, (loss, ref)
     assert ge <= GRAD_TOL, (ge, name)

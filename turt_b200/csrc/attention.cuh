@@ -11,3 +11,28 @@ int attention_fwd(cudaStream_t st, const float* qkv, const float2* rope_cs, floa
 int attention_bwd(cudaStream_t st, const float* qkv, const float2* rope_cs, const float* out, const float* dout,
                   const float* lse, float* D, float* dqkv, int B, int T, int H, int hd, int rope);
 }  // namespace turt
+
+// ------------------------------------------------------------------------------------------
+// Tensor-core attention: the reference's materialised chain (scores -> scale -> causal mask
+// -> softmax -> P*V) as batched 3xTF32 tcgen05 GEMMs over the B*H heads plus row kernels.
+// P stays resident from the forward to the backward pass.  Score rows have pitch
+// attn_pitch(T) (T rounded up to 4 floats, the TMA row-pitch granule).
+namespace turt {
+struct AttnTensors {
+  float* P = nullptr;   // [B*H][T][pitch] scores, then probabilities (kept for backward)
+  float* qr = nullptr;  // [B*H][T][hd] rotated q (RoPE models; null otherwise)
+  float* kr = nullptr;  // [B*H][T][hd] rotated k
+};
+struct AttnScratch {
+  float* dS = nullptr;  // [B*H][T][pitch]
+  float* dq = nullptr;  // [B*H][T][hd] (RoPE models)
+  float* dk = nullptr;
+};
+inline long attn_pitch(int T) { return ((long)T + 3) & ~3L; }
+bool attention_tc_supported(int hd);
+int attention_tc_fwd(cudaStream_t st, const float* qkv, const float2* rope_cs, float* out, const AttnTensors& at, int B,
+                     int T, int H, int hd, int rope, int* flags, int precision);
+int attention_tc_bwd(cudaStream_t st, const float* qkv, const float2* rope_cs, const float* dout,
+                     const AttnTensors& at, const AttnScratch& sc, float* dqkv, int B, int T, int H, int hd, int rope,
+                     int* flags, int precision);
+}  // namespace turt

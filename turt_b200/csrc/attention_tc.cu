@@ -1,0 +1,356 @@
+// attention_tc.cu -- causal self-attention on the tensor cores, materialised per head.
+//
+// The reference computes attention per layer as (src/models/gpu-gpt.ts:143-168)
+//   split heads -> ROPE(q), ROPE(k) -> S = bmmBT(q, k) -> S *= 1/sqrt(hd)
+//   -> maskedFillCausal(S, -1e9) -> P = softmax(S) -> O = bmm(P, v) -> merge heads
+// and its autograd tape runs the matching backward ops.  This file keeps that dataflow and
+// puts every contraction on the batched tcgen05 GEMM (3xTF32) with the B*H heads as a
+// two-level (sequence, head) batch, so q, k, v, dO and the merged outputs are addressed in
+// place inside the fused [N][3E] / [N][E] activations:
+//   forward : [RoPE q,k -> head-major copies]  S = q k^T (upper tiles skipped)
+//             softmax rows (scale, causal mask, P kept)  O = P v (K-range cut at the diagonal)
+//   backward: dP = dO v^T  dS = P (dP - rowsum(P dP)) * scale  dV = P^T dO  dQ = dS k
+//             dK = dS^T q  [inverse RoPE on dQ, dK]
+// Masked probabilities are exact zeros, so the causal tile / K-range skips change no result.
+#include "attention.cuh"
+#include "gemm.cuh"
+
+namespace turt {
+namespace {
+
+// q, k of [N][3E] (token n = b*T + t, head h at columns h*hd) -> rotated head-major
+// copies [B*H][T][hd].  RoPE rotates interleaved pairs (src/math/tensor.ts:650-700):
+// (x0, x1) -> (x0 c - x1 s, x0 s + x1 c) with (c, s) = rope_cs[t][pair].
+__global__ void k_rope_heads(const float* __restrict__ qkv, const float2* __restrict__ cs, float* __restrict__ qr,
+                             float* __restrict__ kr, int B, int T, int H, int hd) {
+  const int E = H * hd, q4 = hd / 4;
+  const long total = (long)B * T * H * q4;
+  const int which = blockIdx.y;  // 0 = q, 1 = k
+  const float* src = qkv + which * E;
+  float* dst = which ? kr : qr;
+  for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (long)gridDim.x * blockDim.x) {
+    const int f = (int)(e % q4);
+    const long r = e / q4;  // (n, h)
+    const int h = (int)(r % H);
+    const long n = r / H;
+    const int t = (int)(n % T), b = (int)(n / T);
+    const float4 x = *reinterpret_cast<const float4*>(src + n * 3 * E + h * hd + 4 * f);
+    const float2 c0 = cs[(long)t * (hd / 2) + 2 * f], c1 = cs[(long)t * (hd / 2) + 2 * f + 1];
+    float4 y;
+    y.x = x.x * c0.x - x.y * c0.y;
+    y.y = x.x * c0.y + x.y * c0.x;
+    y.z = x.z * c1.x - x.w * c1.y;
+    y.w = x.z * c1.y + x.w * c1.x;
+    *reinterpret_cast<float4*>(dst + (((long)b * H + h) * T + t) * hd + 4 * f) = y;
+  }
+}
+
+// Head-major dq, dk [B*H][T][hd] -> dqkv[N][3E] columns [0, E) and [E, 2E), rotated back by -theta.
+__global__ void k_unrope_heads(const float* __restrict__ dq, const float* __restrict__ dk,
+                               const float2* __restrict__ cs, float* __restrict__ dqkv, int B, int T, int H, int hd) {
+  const int E = H * hd, q4 = hd / 4;
+  const long total = (long)B * T * H * q4;
+  const int which = blockIdx.y;
+  const float* src = which ? dk : dq;
+  float* dst = dqkv + which * E;
+  for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (long)gridDim.x * blockDim.x) {
+    const int f = (int)(e % q4);
+    const long r = e / q4;  // (b, h, t) head-major
+    const int t = (int)(r % T);
+    const long bh = r / T;
+    const int h = (int)(bh % H), b = (int)(bh / H);
+    const float4 g = *reinterpret_cast<const float4*>(src + r * hd + 4 * f);
+    const float2 c0 = cs[(long)t * (hd / 2) + 2 * f], c1 = cs[(long)t * (hd / 2) + 2 * f + 1];
+    float4 y;
+    y.x = g.x * c0.x + g.y * c0.y;
+    y.y = -g.x * c0.y + g.y * c0.x;
+    y.z = g.z * c1.x + g.w * c1.y;
+    y.w = -g.z * c1.y + g.w * c1.x;
+    *reinterpret_cast<float4*>(dst + ((long)b * T + t) * 3 * E + h * hd + 4 * f) = y;
+  }
+}
+
+constexpr int kRowWarps = 8;  // rows (one warp each) per 256-thread block
+constexpr int kMaxRegChunks = 8;  // rows up to 32 * 4 * 8 = 1024 keys stay in registers
+
+// Causal softmax of one score row in place: P[j] = exp(s_j*scale - max) / sum for j <= i,
+// 0 for i < j < pitch.  Lane `lane` owns the float4 chunks starting at 4*(32c + lane); rows
+// longer than the register budget take the three-pass loop.  Entries right of the diagonal
+// may be unwritten (skipped score tiles): they are read only into masked lanes.
+template <bool REG>
+__global__ void __launch_bounds__(256) k_softmax_causal(float* __restrict__ S, long rows, int T, long pitch,
+                                                        float scale) {
+  const long row = (long)blockIdx.x * kRowWarps + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int i = (int)(row % T);
+  float* p = S + (row / T) * T * pitch + (long)i * pitch;
+  const int n = i + 1;  // valid keys
+  float mx = -INFINITY;
+  if (REG) {
+    float v[kMaxRegChunks * 4];
+#pragma unroll
+    for (int c = 0; c < kMaxRegChunks; c++) {
+      const int j0 = (c * 32 + lane) * 4;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (j0 < n) x = *reinterpret_cast<const float4*>(p + j0);
+      v[c * 4 + 0] = j0 + 0 < n ? x.x * scale : -INFINITY;
+      v[c * 4 + 1] = j0 + 1 < n ? x.y * scale : -INFINITY;
+      v[c * 4 + 2] = j0 + 2 < n ? x.z * scale : -INFINITY;
+      v[c * 4 + 3] = j0 + 3 < n ? x.w * scale : -INFINITY;
+#pragma unroll
+      for (int u = 0; u < 4; u++) mx = fmaxf(mx, v[c * 4 + u]);
+    }
+    mx = warp_max(mx);
+    float sum = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxRegChunks * 4; c++) {
+      v[c] = expf(v[c] - mx);  // exp(-inf) = 0 for masked keys
+      sum += v[c];
+    }
+    sum = warp_sum(sum);
+    const float inv = 1.0f / sum;
+#pragma unroll
+    for (int c = 0; c < kMaxRegChunks; c++) {
+      const int j0 = (c * 32 + lane) * 4;
+      if (j0 < pitch)
+        *reinterpret_cast<float4*>(p + j0) =
+            make_float4(v[c * 4] * inv, v[c * 4 + 1] * inv, v[c * 4 + 2] * inv, v[c * 4 + 3] * inv);
+    }
+  } else {
+    for (int j = lane; j < n; j += 32) mx = fmaxf(mx, p[j] * scale);
+    mx = warp_max(mx);
+    float sum = 0.f;
+    for (int j = lane; j < n; j += 32) sum += expf(p[j] * scale - mx);
+    sum = warp_sum(sum);
+    const float inv = 1.0f / sum;
+    for (int j = lane; j < pitch; j += 32) p[j] = j < n ? expf(p[j] * scale - mx) * inv : 0.f;
+  }
+}
+
+// Softmax + scale backward of one row, in place over dP: dS_j = P_j (dP_j - sum_k P_k dP_k) * scale
+// for j <= i, 0 right of the diagonal (masked scores get no gradient).
+template <bool REG>
+__global__ void __launch_bounds__(256) k_softmax_causal_bwd(const float* __restrict__ P, float* __restrict__ dP,
+                                                            long rows, int T, long pitch, float scale) {
+  const long row = (long)blockIdx.x * kRowWarps + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int i = (int)(row % T);
+  const long off = (row / T) * T * pitch + (long)i * pitch;
+  const float* p = P + off;
+  float* g = dP + off;
+  const int n = i + 1;
+  float dot = 0.f;
+  if (REG) {
+    float pv[kMaxRegChunks * 4], gv[kMaxRegChunks * 4];
+#pragma unroll
+    for (int c = 0; c < kMaxRegChunks; c++) {
+      const int j0 = (c * 32 + lane) * 4;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), d = a;
+      if (j0 < n) {
+        a = *reinterpret_cast<const float4*>(p + j0);
+        d = *reinterpret_cast<const float4*>(g + j0);
+      }
+      pv[c * 4 + 0] = j0 + 0 < n ? a.x : 0.f;
+      pv[c * 4 + 1] = j0 + 1 < n ? a.y : 0.f;
+      pv[c * 4 + 2] = j0 + 2 < n ? a.z : 0.f;
+      pv[c * 4 + 3] = j0 + 3 < n ? a.w : 0.f;
+      gv[c * 4 + 0] = j0 + 0 < n ? d.x : 0.f;
+      gv[c * 4 + 1] = j0 + 1 < n ? d.y : 0.f;
+      gv[c * 4 + 2] = j0 + 2 < n ? d.z : 0.f;
+      gv[c * 4 + 3] = j0 + 3 < n ? d.w : 0.f;
+#pragma unroll
+      for (int u = 0; u < 4; u++) dot += pv[c * 4 + u] * gv[c * 4 + u];
+    }
+    dot = warp_sum(dot);
+#pragma unroll
+    for (int c = 0; c < kMaxRegChunks; c++) {
+      const int j0 = (c * 32 + lane) * 4;
+      if (j0 < pitch) {
+        float4 r;
+        r.x = pv[c * 4 + 0] * (gv[c * 4 + 0] - dot) * scale;
+        r.y = pv[c * 4 + 1] * (gv[c * 4 + 1] - dot) * scale;
+        r.z = pv[c * 4 + 2] * (gv[c * 4 + 2] - dot) * scale;
+        r.w = pv[c * 4 + 3] * (gv[c * 4 + 3] - dot) * scale;
+        *reinterpret_cast<float4*>(g + j0) = r;
+      }
+    }
+  } else {
+    for (int j = lane; j < n; j += 32) dot += p[j] * g[j];
+    dot = warp_sum(dot);
+    for (int j = lane; j < pitch; j += 32) g[j] = j < n ? p[j] * (g[j] - dot) * scale : 0.f;
+  }
+}
+
+int rows_launch(cudaStream_t st, long rows, int T, long pitch, float scale, float* S, const float* P, bool bwd) {
+  const int blocks = (int)((rows + kRowWarps - 1) / kRowWarps);
+  const bool reg = pitch <= 32 * 4 * kMaxRegChunks;
+  if (!bwd) {
+    if (reg)
+      k_softmax_causal<true><<<blocks, 256, 0, st>>>(S, rows, T, pitch, scale);
+    else
+      k_softmax_causal<false><<<blocks, 256, 0, st>>>(S, rows, T, pitch, scale);
+  } else {
+    if (reg)
+      k_softmax_causal_bwd<true><<<blocks, 256, 0, st>>>(P, S, rows, T, pitch, scale);
+    else
+      k_softmax_causal_bwd<false><<<blocks, 256, 0, st>>>(P, S, rows, T, pitch, scale);
+  }
+  TURT_LAUNCH_CHECK();
+  return OK;
+}
+
+int grid_for(long total) {
+  long b = (total + 255) / 256;
+  if (b > 148 * 16) b = 148 * 16;
+  return (int)(b < 1 ? 1 : b);
+}
+
+// Operand views.  Batch index = b * H + h (inner level = head).
+struct Views {
+  GemmOperand q, k, v, dout, P, PT;
+  long pitch;
+};
+
+Views views(const float* qkv, const float* dout, const AttnTensors& at, const float* P, int T, int H, int hd,
+            bool rope) {
+  const int E = H * hd;
+  Views w;
+  w.pitch = attn_pitch(T);
+  auto inplace = [&](const float* base, long ld, long rows_stride) {
+    GemmOperand o;
+    o.ptr = base;
+    o.ld = ld;
+    o.stride = hd;
+    o.stride_hi = rows_stride;
+    return o;
+  };
+  auto headmajor = [&](const float* base) {
+    GemmOperand o;
+    o.ptr = base;
+    o.ld = hd;
+    o.stride = (long)T * hd;
+    o.stride_hi = (long)H * T * hd;
+    return o;
+  };
+  w.q = rope ? headmajor(at.qr) : inplace(qkv, 3L * E, (long)T * 3 * E);
+  w.k = rope ? headmajor(at.kr) : inplace(qkv + E, 3L * E, (long)T * 3 * E);
+  w.v = inplace(qkv + 2 * E, 3L * E, (long)T * 3 * E);
+  if (dout) w.dout = inplace(dout, E, (long)T * E);
+  w.P.ptr = P;
+  w.P.ld = w.pitch;
+  w.P.stride = (long)T * w.pitch;
+  w.P.stride_hi = (long)H * T * w.pitch;
+  w.PT = w.P;
+  w.PT.mn_major = true;
+  return w;
+}
+
+GemmOperand mn(GemmOperand o) {
+  o.mn_major = true;
+  return o;
+}
+
+GemmEpi scores_epi(float* S, int T, int H, long pitch) {
+  GemmEpi e;
+  e.kind = EPI_STORE;
+  e.C = S;
+  e.ldc = pitch;
+  e.strideC = (long)T * pitch;
+  e.strideC_hi = (long)H * T * pitch;
+  e.bdiv = H;
+  e.causal = CAUSAL_SKIP_UPPER;
+  return e;
+}
+
+// [T][hd] per-head output written into a merged [N][ld] activation at column `col`.
+GemmEpi merged_epi(float* base, long ld, int T, int hd, int causal) {
+  GemmEpi e;
+  e.kind = EPI_STORE;
+  e.C = base;
+  e.ldc = ld;
+  e.strideC = hd;
+  e.strideC_hi = (long)T * ld;
+  e.causal = causal;
+  return e;
+}
+
+GemmEpi headmajor_epi(float* base, int T, int H, int hd, int causal) {
+  GemmEpi e;
+  e.kind = EPI_STORE;
+  e.C = base;
+  e.ldc = hd;
+  e.strideC = (long)T * hd;
+  e.strideC_hi = (long)H * T * hd;
+  e.causal = causal;
+  return e;
+}
+
+}  // namespace
+
+bool attention_tc_supported(int hd) { return hd >= 16 && hd <= 256 && hd % 16 == 0; }
+
+int attention_tc_fwd(cudaStream_t st, const float* qkv, const float2* rope_cs, float* out, const AttnTensors& at, int B,
+                     int T, int H, int hd, int rope, int* flags, int precision) {
+  TURT_REQUIRE(attention_tc_supported(hd), "attention: head dim must be a multiple of 16 in [16, 256]");
+  TURT_REQUIRE(at.P && (!rope || (at.qr && at.kr)), "attention: buffers missing");
+  const int E = H * hd, BH = B * H;
+  const float scale = 1.0f / sqrtf((float)hd);
+  if (rope) {
+    k_rope_heads<<<dim3(grid_for((long)B * T * H * hd / 4), 2), 256, 0, st>>>(qkv, rope_cs, at.qr, at.kr, B, T, H, hd);
+    TURT_LAUNCH_CHECK();
+  }
+  const Views w = views(qkv, nullptr, at, at.P, T, H, hd, rope != 0);
+  // S = q k^T  (k [T][hd] is the K-major B operand)
+  RC(gemm_tf32(st, T, T, hd, BH, w.q, w.k, scores_epi(at.P, T, H, w.pitch), flags, precision));
+  RC(rows_launch(st, (long)BH * T, T, w.pitch, scale, at.P, nullptr, false));
+  // O = P v  (v [T][hd] is the MN-major B operand), merged into out[N][E]
+  GemmEpi e = merged_epi(out, E, T, hd, CAUSAL_K_LOWER);
+  e.bdiv = H;
+  RC(gemm_tf32(st, T, hd, T, BH, w.P, mn(w.v), e, flags, precision));
+  return OK;
+}
+
+int attention_tc_bwd(cudaStream_t st, const float* qkv, const float2* rope_cs, const float* dout,
+                     const AttnTensors& at, const AttnScratch& sc, float* dqkv, int B, int T, int H, int hd, int rope,
+                     int* flags, int precision) {
+  TURT_REQUIRE(attention_tc_supported(hd), "attention: head dim must be a multiple of 16 in [16, 256]");
+  TURT_REQUIRE(at.P && sc.dS && (!rope || (at.qr && at.kr && sc.dq && sc.dk)), "attention: buffers missing");
+  const int E = H * hd, BH = B * H;
+  const float scale = 1.0f / sqrtf((float)hd);
+  const Views w = views(qkv, dout, at, at.P, T, H, hd, rope != 0);
+  // dP = dO v^T
+  RC(gemm_tf32(st, T, T, hd, BH, w.dout, w.v, scores_epi(sc.dS, T, H, w.pitch), flags, precision));
+  // dS = P (dP - rowsum(P dP)) * scale, in place
+  RC(rows_launch(st, (long)BH * T, T, w.pitch, scale, sc.dS, at.P, true));
+  GemmOperand dS = w.P, dST = w.PT;
+  dS.ptr = sc.dS;
+  dST.ptr = sc.dS;
+  // dV = P^T dO  -> dqkv[:, 2E:3E)
+  GemmEpi e = merged_epi(dqkv + 2 * E, 3L * E, T, hd, CAUSAL_K_UPPER);
+  e.bdiv = H;
+  RC(gemm_tf32(st, T, hd, T, BH, w.PT, mn(w.dout), e, flags, precision));
+  // dQ = dS k, dK = dS^T q  (rotated frame when RoPE is on)
+  if (rope) {
+    e = headmajor_epi(sc.dq, T, H, hd, CAUSAL_K_LOWER);
+    e.bdiv = H;
+    RC(gemm_tf32(st, T, hd, T, BH, dS, mn(w.k), e, flags, precision));
+    e = headmajor_epi(sc.dk, T, H, hd, CAUSAL_K_UPPER);
+    e.bdiv = H;
+    RC(gemm_tf32(st, T, hd, T, BH, dST, mn(w.q), e, flags, precision));
+    k_unrope_heads<<<dim3(grid_for((long)B * T * H * hd / 4), 2), 256, 0, st>>>(sc.dq, sc.dk, rope_cs, dqkv, B, T, H,
+                                                                                hd);
+    TURT_LAUNCH_CHECK();
+  } else {
+    e = merged_epi(dqkv, 3L * E, T, hd, CAUSAL_K_LOWER);
+    e.bdiv = H;
+    RC(gemm_tf32(st, T, hd, T, BH, dS, mn(w.k), e, flags, precision));
+    e = merged_epi(dqkv + E, 3L * E, T, hd, CAUSAL_K_UPPER);
+    e.bdiv = H;
+    RC(gemm_tf32(st, T, hd, T, BH, dST, mn(w.q), e, flags, precision));
+  }
+  return OK;
+}
+
+}  // namespace turt

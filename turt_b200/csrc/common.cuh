@@ -46,6 +46,13 @@ void note_launch(int n = 1);
     }                                                                           \
   } while (0)
 
+// Propagates a non-zero status code.
+#define RC(x)              \
+  do {                     \
+    int rc__ = (x);        \
+    if (rc__) return rc__; \
+  } while (0)
+
 #define TURT_REQUIRE(cond, msg)             \
   do {                                      \
     if (!(cond)) {                          \
@@ -116,6 +123,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* f
       return false;
     }
   }
+}
+
+// Warp-wide bounded wait in which only lane 0 polls the barrier (a poll by every lane costs
+// shared-memory bandwidth); the __syncwarp orders the other lanes after lane 0's observation
+// of the completed phase.  The result is the same on every lane.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* flags, int site) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, flags, site) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -24,12 +24,12 @@ namespace {
 constexpr int BM = 128;
 
 // ------------------------------------------------------------ PTX wrappers
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
                                             uint64_t* bar) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
       "[%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
 
@@ -124,7 +124,7 @@ struct EpiVec {
 
 // Columns [col0, col0 + 32) of one output row (every kind except the fused SwiGLU forward).
 __device__ __forceinline__ void epi_chunk(const GemmEpi& epi, const EpiVec& vec, float* v, float* Cb, long row,
-                                          int col0, int n, int batch) {
+                                          int col0, int n, long cboff) {
   float* dst = Cb + row * epi.ldc + col0;
   switch (epi.kind) {
     case EPI_STORE:
@@ -150,7 +150,7 @@ __device__ __forceinline__ void epi_chunk(const GemmEpi& epi, const EpiVec& vec,
       break;
     case EPI_ADD_RES: {
       float o[32];
-      ld32(epi.R + (long)batch * epi.strideC + row * epi.ldr + col0, o, n, vec.R);
+      ld32(epi.R + cboff + row * epi.ldr + col0, o, n, vec.R);
 #pragma unroll
       for (int j = 0; j < 32; j++) v[j] += o[j];
       if (epi.bias) {
@@ -251,7 +251,7 @@ struct GemmShape {
 template <int BN, int BK, bool A_MN, bool B_MN, bool X3>
 __global__ void __launch_bounds__(GemmShape<BN, BK, X3>::THREADS, 1)
     k_gemm_tf32(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmEpi epi,
-                int M, int N, int K, int batches, int ksplits, int kt_per_split, int* flags) {
+                int M, int N, int K, int batches, int bdiv, int causal, int ksplits, int kt_per_split, int* flags) {
   using S = GemmShape<BN, BK, X3>;
   constexpr int STAGES = S::STAGES;
   static_assert(BK == 16 || BK == 32, "BK");
@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(GemmShape<BN, BK, X3>::THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // unit -> (m0, n0, batch, first k-tile, k-tile count)
+  // unit -> (m0, n0, batch, first k-tile, k-tile count); false = nothing to compute (causal skip)
   auto decode = [&](int u, int& m0, int& n0, int& b, int& kt0, int& nkt) {
     m0 = (u % mt) * BM;
     u /= mt;
@@ -306,7 +306,12 @@ __global__ void __launch_bounds__(GemmShape<BN, BK, X3>::THREADS, 1)
     const int split = u % ksplits;
     b = u / ksplits;
     kt0 = split * kt_per_split;
-    nkt = min(kt_total, kt0 + kt_per_split) - kt0;
+    int kt1 = min(kt_total, kt0 + kt_per_split);
+    if (causal == CAUSAL_SKIP_UPPER && n0 >= m0 + BM) return false;
+    if (causal == CAUSAL_K_LOWER) kt1 = min(kt1, (m0 + BM + BK - 1) / BK);
+    if (causal == CAUSAL_K_UPPER) kt0 = max(kt0, m0 / BK);
+    nkt = kt1 - kt0;
+    return nkt > 0;
   };
 
   if (warp == 0) {
@@ -315,7 +320,7 @@ __global__ void __launch_bounds__(GemmShape<BN, BK, X3>::THREADS, 1)
       uint32_t it = 0;
       for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
         int m0, n0, b, kt0, nkt;
-        decode(u, m0, n0, b, kt0, nkt);
+        if (!decode(u, m0, n0, b, kt0, nkt)) continue;
         // Boxes that start beyond M (or N) only feed output rows (columns) that are never
         // written, so they are skipped and not counted.
         int na = 1, nb = 1;
@@ -328,6 +333,7 @@ __global__ void __launch_bounds__(GemmShape<BN, BK, X3>::THREADS, 1)
           for (int j = 0; j < BN / 32; j++) nb += (n0 + 32 * j < N);
         }
         const uint32_t bytes = (A_MN ? na * S::MN_BOX : S::A_BYTES) + (B_MN ? nb * S::MN_BOX : S::B_BYTES);
+        const int bi = b % bdiv, bo = b / bdiv;
         for (int i = 0; i < nkt; i++, it++) {
           const int s = it % STAGES;
           if (!mbar_wait(&empty[s], ((it / STAGES) + 1) & 1, flags, 101)) {
@@ -339,16 +345,16 @@ __global__ void __launch_bounds__(GemmShape<BN, BK, X3>::THREADS, 1)
           const uint32_t sb = sa + S::A_BYTES;
           mbar_arrive_expect_tx(&full[s], bytes);
           if (!A_MN) {
-            tma_load_3d(sa, &tmA, kc, m0, b, &full[s]);
+            tma_load_4d(sa, &tmA, kc, m0, bi, bo, &full[s]);
           } else {
             for (int j = 0; j < BM / 32; j++)
-              if (m0 + 32 * j < M) tma_load_3d(sa + j * S::MN_BOX, &tmA, m0 + 32 * j, kc, b, &full[s]);
+              if (m0 + 32 * j < M) tma_load_4d(sa + j * S::MN_BOX, &tmA, m0 + 32 * j, kc, bi, bo, &full[s]);
           }
           if (!B_MN) {
-            tma_load_3d(sb, &tmB, kc, n0, b, &full[s]);
+            tma_load_4d(sb, &tmB, kc, n0, bi, bo, &full[s]);
           } else {
             for (int j = 0; j < BN / 32; j++)
-              if (n0 + 32 * j < N) tma_load_3d(sb + j * S::MN_BOX, &tmB, n0 + 32 * j, kc, b, &full[s]);
+              if (n0 + 32 * j < N) tma_load_4d(sb + j * S::MN_BOX, &tmB, n0 + 32 * j, kc, bi, bo, &full[s]);
           }
         }
       }
@@ -362,11 +368,12 @@ __global__ void __launch_bounds__(GemmShape<BN, BK, X3>::THREADS, 1)
       constexpr uint32_t kKSbo = BK == 32 ? 1024 : 512;
       uint32_t it = 0;
       int t = 0;
-      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x, t++) {
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
         int m0, n0, b, kt0, nkt;
-        decode(u, m0, n0, b, kt0, nkt);
-        const int acc = t & 1;
-        if (!mbar_wait(&tempty[acc], ((t >> 1) + 1) & 1, flags, 105)) {
+        if (!decode(u, m0, n0, b, kt0, nkt)) continue;
+        const int acc = t & 1, use = t >> 1;
+        t++;  // counts computed units only (causal skips do not use an accumulator)
+        if (!mbar_wait(&tempty[acc], (use + 1) & 1, flags, 105)) {
           *abort_flag = 1;
           break;
         }
@@ -420,11 +427,11 @@ __global__ void __launch_bounds__(GemmShape<BN, BK, X3>::THREADS, 1)
     uint32_t it = 0;
     for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
       int m0, n0, b, kt0, nkt;
-      decode(u, m0, n0, b, kt0, nkt);
+      if (!decode(u, m0, n0, b, kt0, nkt)) continue;
       bool ok = true;
       for (int i = 0; i < nkt; i++, it++) {
         const int s = it % STAGES;
-        if (!mbar_wait(&full[s], (it / STAGES) & 1, flags, 104)) {
+        if (!mbar_wait_warp(&full[s], (it / STAGES) & 1, flags, 104)) {
           ok = false;
           break;
         }
@@ -453,22 +460,25 @@ __global__ void __launch_bounds__(GemmShape<BN, BK, X3>::THREADS, 1)
   } else {
     // -------------------------------------------------- epilogue warps (2..5)
     const int q = warp & 3;
-    const EpiVec vec{(epi.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(epi.C) & 15) == 0) && (epi.strideC % 4 == 0),
+    const EpiVec vec{(epi.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(epi.C) & 15) == 0) && (epi.strideC % 4 == 0) &&
+                         (epi.strideC_hi % 4 == 0),
                      epi.R && (epi.ldr % 4 == 0) && ((reinterpret_cast<uintptr_t>(epi.R) & 15) == 0),
                      epi.C2 && (epi.ldc2 % 4 == 0) && ((reinterpret_cast<uintptr_t>(epi.C2) & 15) == 0)};
     int t = 0;
-    for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x, t++) {
+    for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
       int m0, n0, b, kt0, nkt;
-      decode(u, m0, n0, b, kt0, nkt);
-      const int acc = t & 1;
-      if (!mbar_wait(&tfull[acc], (t >> 1) & 1, flags, 103)) {
+      if (!decode(u, m0, n0, b, kt0, nkt)) continue;
+      const int acc = t & 1, use = t >> 1;
+      t++;
+      if (!mbar_wait_warp(&tfull[acc], use & 1, flags, 103)) {
         *abort_flag = 1;
         break;
       }
       tc_fence_after();
       const long row = m0 + q * 32 + lane;
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      float* Cb = epi.C + (long)b * epi.strideC;
+      const long cboff = (long)(b % bdiv) * epi.strideC + (long)(b / bdiv) * epi.strideC_hi;
+      float* Cb = epi.C + cboff;
       if (epi.kind == EPI_SWIGLU_FWD) {
         // Chunk pairs (gate, up): C keeps both pre-activations, C2 gets silu(gate) * up.
 #pragma unroll 1
@@ -492,7 +502,7 @@ __global__ void __launch_bounds__(GemmShape<BN, BK, X3>::THREADS, 1)
           if (col0 >= N) break;  // warp-uniform
           float v[32];
           tmem_ld32(tbase + c * 32, v);
-          if (row < M) epi_chunk(epi, vec, v, Cb, row, col0, min(32, N - col0), b);
+          if (row < M) epi_chunk(epi, vec, v, Cb, row, col0, min(32, N - col0), cboff);
         }
       }
       // hand the accumulator back to the MMA issuer
@@ -574,25 +584,29 @@ EncodeTiledFn get_encode() {
   return fn;
 }
 
-// 3-D tensor map over a row-major [batch][rows][inner] view with `ld` elements per row.
+// 4-D tensor map over a row-major [outer][inner batch][rows][inner] view with `ld` elements per
+// row, `s_in` / `s_out` elements between inner / outer batch entries (one level: n_out = 1).
 // K-major operands take a box_inner-float-wide swizzle (128 B for 32 floats, 64 B for 16);
 // MN-major ones the 128-byte swizzle with 32-byte atomicity.
-int make_map(CUtensorMap* map, const float* base, long inner, long rows, long batch, long ld, long bstride,
-             int box_inner, int box_rows, bool mn_major) {
+int make_map(CUtensorMap* map, const float* base, long inner, long rows, long n_in, long n_out, long ld, long s_in,
+             long s_out, int box_inner, int box_rows, bool mn_major) {
   EncodeTiledFn enc = get_encode();
   if (!enc) {
     set_error("cuTensorMapEncodeTiled entry point unavailable");
     return ERR_CUDA;
   }
-  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)batch};
-  long bs = batch > 1 ? bstride : ld * rows;
-  if (bs % 4 != 0) bs = ((bs + 3) / 4) * 4;  // unused for batch == 1
-  cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)bs * 4};
-  cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
+  // Strides of size-1 dimensions are never used; give them a legal value.
+  if (n_in <= 1) s_in = ld * rows;
+  if (n_out <= 1) s_out = s_in * n_in;
+  if (s_in % 4 != 0) s_in = ((s_in + 3) / 4) * 4;
+  if (s_out % 4 != 0) s_out = ((s_out + 3) / 4) * 4;
+  cuuint64_t dims[4] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)n_in, (cuuint64_t)n_out};
+  cuuint64_t strides[3] = {(cuuint64_t)ld * 4, (cuuint64_t)s_in * 4, (cuuint64_t)s_out * 4};
+  cuuint32_t box[4] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUtensorMapSwizzle sw = mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
                                          : (box_inner == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -617,7 +631,7 @@ struct LaunchArgs {
   cudaStream_t st;
   CUtensorMap ma, mb;
   GemmEpi epi;
-  int M, N, K, batch, ks, kt_per;
+  int M, N, K, batch, bdiv, causal, ks, kt_per;
   int* flags;
 };
 
@@ -634,7 +648,8 @@ int launch(const LaunchArgs& a) {
   }
   const long units = (long)ceil_div(a.M, BM) * ceil_div(a.N, BN) * a.batch * a.ks;
   const int grid = (int)(units < num_sms() ? units : num_sms());
-  kfn<<<grid, S::THREADS, S::SMEM, a.st>>>(a.ma, a.mb, a.epi, a.M, a.N, a.K, a.batch, a.ks, a.kt_per, a.flags);
+  kfn<<<grid, S::THREADS, S::SMEM, a.st>>>(a.ma, a.mb, a.epi, a.M, a.N, a.K, a.batch, a.bdiv, a.causal, a.ks, a.kt_per,
+                                           a.flags);
   TURT_LAUNCH_CHECK();
   return OK;
 }
@@ -714,7 +729,8 @@ void gemm_set_tile_override(int bn) { g_tile_override.store(bn); }
 
 bool gemm_tf32_supported(const GemmOperand& A, const GemmOperand& B) {
   auto ok = [](const GemmOperand& o) {
-    return (reinterpret_cast<uintptr_t>(o.ptr) & 15) == 0 && o.ld % 4 == 0 && o.stride % 4 == 0;
+    return (reinterpret_cast<uintptr_t>(o.ptr) & 15) == 0 && o.ld % 4 == 0 && o.stride % 4 == 0 &&
+           o.stride_hi % 4 == 0;
   };
   return ok(A) && ok(B);
 }
@@ -739,9 +755,15 @@ int gemm_tf32(cudaStream_t stream, int M, int N, int K, int batch, const GemmOpe
   la.K = K;
   la.batch = batch;
   la.flags = flags;
+  const int bdiv = epi_in.bdiv > 0 ? epi_in.bdiv : batch;
+  TURT_REQUIRE(batch % bdiv == 0, "gemm: batch is not a multiple of the inner batch count");
+  la.bdiv = bdiv;
+  la.causal = epi_in.causal;
+  if (la.causal != CAUSAL_NONE) TURT_REQUIRE(M == N || la.causal != CAUSAL_SKIP_UPPER, "gemm: causal skip needs M == N");
   // K is split (partial sums reduced with atomics) only when the output alone gives too few
   // units to fill the GPU (weight gradients), with at least 256 of K per split.
-  const bool can_split = la.epi.kind == EPI_ACCUM || la.epi.kind == EPI_STORE || la.epi.kind == EPI_RED;
+  const bool can_split = (la.epi.kind == EPI_ACCUM || la.epi.kind == EPI_STORE || la.epi.kind == EPI_RED) &&
+                         la.causal == CAUSAL_NONE;
   const int max_ks = force_splits > 0 ? 1 : (can_split ? std::max(1, K / 256) : 1);
   const TilePlan plan = plan_tiles(M, N, K, batch, x3, std::min(max_ks, 64), force_bn);
   const int BN = plan.bn;
@@ -754,21 +776,21 @@ int gemm_tf32(cudaStream_t stream, int M, int N, int K, int batch, const GemmOpe
     TURT_REQUIRE(can_split, "gemm: split-K needs an accumulating epilogue");
     if (epi.kind == EPI_STORE) {
       for (int b = 0; b < batch; b++)
-        TURT_CHECK_CUDA(
-            cudaMemset2DAsync(epi.C + (long)b * epi.strideC, epi.ldc * 4, 0, (size_t)N * 4, (size_t)M, stream));
+        TURT_CHECK_CUDA(cudaMemset2DAsync(epi.C + (long)(b % bdiv) * epi.strideC + (long)(b / bdiv) * epi.strideC_hi,
+                                          epi.ldc * 4, 0, (size_t)N * 4, (size_t)M, stream));
     }
     epi.kind = EPI_RED;
   }
   int rc;
   if (!A.mn_major)
-    rc = make_map(&la.ma, A.ptr, K, M, batch, A.ld, A.stride, BK, BM, false);
+    rc = make_map(&la.ma, A.ptr, K, M, bdiv, batch / bdiv, A.ld, A.stride, A.stride_hi, BK, BM, false);
   else
-    rc = make_map(&la.ma, A.ptr, M, K, batch, A.ld, A.stride, 32, BK, true);
+    rc = make_map(&la.ma, A.ptr, M, K, bdiv, batch / bdiv, A.ld, A.stride, A.stride_hi, 32, BK, true);
   if (rc) return rc;
   if (!B.mn_major)
-    rc = make_map(&la.mb, B.ptr, K, N, batch, B.ld, B.stride, BK, BN, false);
+    rc = make_map(&la.mb, B.ptr, K, N, bdiv, batch / bdiv, B.ld, B.stride, B.stride_hi, BK, BN, false);
   else
-    rc = make_map(&la.mb, B.ptr, N, K, batch, B.ld, B.stride, 32, BK, true);
+    rc = make_map(&la.mb, B.ptr, N, K, bdiv, batch / bdiv, B.ld, B.stride, B.stride_hi, 32, BK, true);
   if (rc) return rc;
   return x3 ? dispatch_bn<true>(BN, A.mn_major, B.mn_major, la) : dispatch_bn<false>(BN, A.mn_major, B.mn_major, la);
 }

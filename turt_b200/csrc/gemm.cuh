@@ -22,16 +22,31 @@ enum EpiKind : int {
 // [64j, 64j+32) hold gate units [32j, 32j+32), columns [64j+32, 64j+64) the matching up units.
 constexpr int kGluBlock = 32;
 
+// Causal structure of a batched attention GEMM over [T x T] score / probability tiles
+// (row index = query, column index = key, lower triangle kept).  Work that only touches the
+// masked upper triangle is skipped; the skipped products are exact zeros.
+enum GemmCausal : int {
+  CAUSAL_NONE = 0,
+  CAUSAL_SKIP_UPPER = 1,  // output [T x T] scores: tiles entirely above the diagonal are not computed
+  CAUSAL_K_LOWER = 2,     // A = lower-triangular [rows x K]: K-range of a row tile ends at its last row
+  CAUSAL_K_UPPER = 3,     // A = upper-triangular (a transposed lower one): K-range starts at the first row
+};
+
 struct GemmEpi {
   int kind = EPI_STORE;
   float* C = nullptr;
   long ldc = 0;
-  long strideC = 0;  // per batch
+  long strideC = 0;  // per batch (per inner batch index when bdiv > 0)
   const float* R = nullptr;
   long ldr = 0;
   const float* bias = nullptr;
   float* C2 = nullptr;
   long ldc2 = 0;
+  // Two-level batch: batch index b = outer * bdiv + inner addresses C + inner * strideC +
+  // outer * strideC_hi (bdiv = 0: one level).  Operands use GemmOperand::stride_hi likewise.
+  int bdiv = 0;
+  long strideC_hi = 0;
+  int causal = CAUSAL_NONE;
 };
 
 // Operand description.  `mn_major` = the operand's contiguous dimension is M (for A) or N
@@ -39,8 +54,9 @@ struct GemmEpi {
 struct GemmOperand {
   const float* ptr = nullptr;
   long ld = 0;      // row pitch in elements
-  long stride = 0;  // batch stride in elements
+  long stride = 0;  // batch stride in elements (inner batch index when GemmEpi::bdiv > 0)
   bool mn_major = false;
+  long stride_hi = 0;  // outer batch stride (GemmEpi::bdiv > 0)
 };
 
 // Tensor-core precision: plain TF32 (10 mantissa bits per operand) or error-compensated

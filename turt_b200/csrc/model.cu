@@ -135,13 +135,32 @@ void free_workspace(turt_model* m) {
   if (m->ws) cudaFree(m->ws);
   m->ws = nullptr;
   m->capN = 0;
+  m->capS = 0;
   m->act.clear();
+}
+
+// Attention path for B x T tokens: tensor-core (materialised scores) when allowed and the
+// probabilities of every layer fit the budget, else the fused CUDA-core kernels.
+constexpr size_t kAttnScoreBudget = (size_t)16 << 30;  // bytes
+
+bool use_tensor_attention(const turt_model* m, int B, int T) {
+  const int hd = m->cfg.n_embd / m->cfg.n_head;
+  if (m->attn_mode == TURT_ATTN_FLASH || !attention_tc_supported(hd)) return false;
+  if (m->attn_mode == TURT_ATTN_TENSOR) return true;
+  const size_t bytes = (size_t)m->cfg.n_layer * B * m->cfg.n_head * T * attn_pitch(T) * 4;
+  return bytes <= kAttnScoreBudget;
 }
 
 // Carves every activation / scratch buffer for N = B*T tokens out of one allocation.
 int ensure_workspace(turt_model* m, int B, int T) {
   const int N = B * T;
-  if (N <= m->capN && B * m->cfg.n_head * T <= m->capB) return OK;
+  const bool tc = use_tensor_attention(m, B, T);
+  const long S_need = tc ? (long)B * m->cfg.n_head * T * attn_pitch(T) : 0;
+  if (N <= m->capN && B * m->cfg.n_head * T <= m->capB && tc == m->attn_tc && S_need <= m->capS) return OK;
+  if (!tc && !attention_supported_hd(m->cfg.n_embd / m->cfg.n_head)) {
+    set_error("fused CUDA-core attention supports head dim 16, 32 or 64; the tensor-core path is off or over budget");
+    return ERR_UNSUPPORTED;
+  }
   free_workspace(m);
   const int E = m->cfg.n_embd, H = m->cfg.n_head, V = m->cfg.vocab_size, h = m->hid, Lc = m->cfg.n_layer;
   const int W1 = m->modern ? 2 * h : h;
@@ -153,8 +172,9 @@ int ensure_workspace(turt_model* m, int B, int T) {
     return o;
   };
   struct LA {
-    size_t x, y1, rs1, mu1, qkv, att, lse, h, y2, rs2, mu2, pre, act;
+    size_t x, y1, rs1, mu1, qkv, att, lse, h, y2, rs2, mu2, pre, act, P, qr, kr;
   };
+  const bool rope = m->modern;
   std::vector<LA> la(Lc);
   const size_t NE = (size_t)N * E, BHT = (size_t)B * H * T;
   for (int l = 0; l < Lc; l++) {
@@ -172,11 +192,15 @@ int ensure_workspace(turt_model* m, int B, int T) {
     a.mu2 = m->modern ? 0 : take(N);
     a.pre = take((size_t)N * W1);
     a.act = take((size_t)N * h);
+    a.P = tc ? take((size_t)S_need) : 0;
+    a.qr = tc && rope ? take(NE) : 0;
+    a.kr = tc && rope ? take(NE) : 0;
   }
   size_t xL = take(NE), yf = take(NE), rsf = take(N), muf = take(N);
   size_t logits = take((size_t)N * V), loss_rows = take(N);
   size_t dx = take(NE), dy = take(NE), datt = take(NE), dqkv = take(3 * NE), dpre = take((size_t)N * W1);
   size_t Dsc = take(BHT);
+  size_t dS = tc ? take((size_t)S_need) : 0, dqh = tc && rope ? take(NE) : 0, dkh = tc && rope ? take(NE) : 0;
   const int C = 3 * E > W1 ? 3 * E : W1;
   size_t part = take((size_t)2 * norm_parts(N) * (C > E ? C : E));
   size_t ids = take(N), tgt = take(N);
@@ -202,6 +226,9 @@ int ensure_workspace(turt_model* m, int B, int T) {
     A.mu2 = m->modern ? nullptr : F(a.mu2);
     A.pre = F(a.pre);
     A.act = F(a.act);
+    A.P = tc ? F(a.P) : nullptr;
+    A.qr = tc && rope ? F(a.qr) : nullptr;
+    A.kr = tc && rope ? F(a.kr) : nullptr;
   }
   m->xL = F(xL);
   m->yf = F(yf);
@@ -215,6 +242,9 @@ int ensure_workspace(turt_model* m, int B, int T) {
   m->dqkv = F(dqkv);
   m->dpre = F(dpre);
   m->Dsc = F(Dsc);
+  m->dS = tc ? F(dS) : nullptr;
+  m->dqh = tc && rope ? F(dqh) : nullptr;
+  m->dkh = tc && rope ? F(dkh) : nullptr;
   m->part = F(part);
   m->d_ids = reinterpret_cast<uint32_t*>(base + ids);
   m->d_tgt = reinterpret_cast<uint32_t*>(base + tgt);
@@ -224,6 +254,8 @@ int ensure_workspace(turt_model* m, int B, int T) {
   TURT_CHECK_CUDA(cudaMallocHost(&m->h_tgt, (size_t)N * 4));
   m->capN = N;
   m->capB = B * H * T;
+  m->capS = S_need;
+  m->attn_tc = tc;
   return OK;
 }
 
@@ -240,12 +272,6 @@ inline GemmEpi epi(int kind, float* C, long ldc) {
 
 // Model GEMMs run on the tensor cores: FP32 (CUDA-core) precision applies to op-level calls only.
 inline int mp(const turt_model* m) { return m->ctx->precision == 0 ? GEMM_TF32X3 : m->ctx->precision; }
-
-#define RC(x)          \
-  do {                 \
-    int rc__ = (x);    \
-    if (rc__) return rc__; \
-  } while (0)
 
 int stage_tokens(turt_model* m, const uint32_t* ids, const uint32_t* tgt, int N) {
   cudaStream_t st = m->ctx->stream;
@@ -276,7 +302,12 @@ int forward(turt_model* m, int B, int T, bool train, float loss_scale) {
     GemmEpi e = epi(m->modern ? EPI_STORE : EPI_BIAS, a.qkv, 3 * E);
     if (!m->modern) e.bias = P + L.bqkv;
     RC(gemm_tf32(st, N, 3 * E, E, 1, opK(a.y1, E), opMN(P + L.wqkv, 3 * E), e, flags, mp(m)));
-    RC(attention_fwd(st, a.qkv, m->rope_cs, a.att, a.lse, B, T, H, hd, m->modern ? 1 : 0));
+    if (m->attn_tc) {
+      AttnTensors at{a.P, a.qr, a.kr};
+      RC(attention_tc_fwd(st, a.qkv, m->rope_cs, a.att, at, B, T, H, hd, m->modern ? 1 : 0, flags, mp(m)));
+    } else {
+      RC(attention_fwd(st, a.qkv, m->rope_cs, a.att, a.lse, B, T, H, hd, m->modern ? 1 : 0));
+    }
     e = epi(EPI_ADD_RES, a.h, E);
     e.R = a.x;
     e.ldr = E;
@@ -362,7 +393,15 @@ int backward(turt_model* m, int B, int T) {
     RC(gemm_tf32(st, N, E, E, 1, opK(m->dx, E), opK(P + L.wproj, E), epi(EPI_STORE, m->datt, E), flags, mp(m)));
     RC(gemm_tf32(st, E, E, N, 1, opMN(a.att, E), opMN(m->dx, E), epi(EPI_ACCUM, G + L.wproj, E), flags, mp(m)));
     if (!m->modern) RC(colsum_accum(st, m->dx, N, E, G + L.bproj, m->part));
-    RC(attention_bwd(st, a.qkv, m->rope_cs, a.att, m->datt, a.lse, m->Dsc, m->dqkv, B, T, H, hd, m->modern ? 1 : 0));
+    if (m->attn_tc) {
+      AttnTensors at{a.P, a.qr, a.kr};
+      AttnScratch sc{m->dS, m->dqh, m->dkh};
+      RC(attention_tc_bwd(st, a.qkv, m->rope_cs, m->datt, at, sc, m->dqkv, B, T, H, hd, m->modern ? 1 : 0, flags,
+                          mp(m)));
+    } else {
+      RC(attention_bwd(st, a.qkv, m->rope_cs, a.att, m->datt, a.lse, m->Dsc, m->dqkv, B, T, H, hd,
+                       m->modern ? 1 : 0));
+    }
     if (!m->modern) RC(colsum_accum(st, m->dqkv, N, 3 * E, G + L.bqkv, m->part));
     RC(gemm_tf32(st, N, E, 3 * E, 1, opK(m->dqkv, 3 * E), opK(P + L.wqkv, 3 * E), epi(EPI_STORE, m->dy, E), flags, mp(m)));
     RC(gemm_tf32(st, E, 3 * E, N, 1, opMN(a.y1, E), opMN(m->dqkv, 3 * E), epi(EPI_ACCUM, G + L.wqkv, 3 * E), flags, mp(m)));
@@ -422,8 +461,8 @@ int turt_model_create(turt_ctx* ctx, const turt_config* cfg, turt_model** out) {
   }
   TURT_REQUIRE(cfg->arch == TURT_ARCH_GPT2 || cfg->arch == TURT_ARCH_MODERN, "arch must be gpt2 (0) or modern (1)");
   const int hd = cfg->n_embd / cfg->n_head;
-  if (!attention_supported_hd(hd)) {
-    set_error("head dim " + std::to_string(hd) + " not supported (16, 32 or 64)");
+  if (!attention_supported_hd(hd) && !attention_tc_supported(hd)) {
+    set_error("head dim " + std::to_string(hd) + " not supported (a multiple of 16 up to 256)");
     return ERR_UNSUPPORTED;
   }
   TURT_REQUIRE(cfg->n_embd % 32 == 0 && cfg->n_embd <= 1024, "nEmbd must be a multiple of 32, at most 1024");
@@ -467,6 +506,17 @@ int turt_model_create(turt_ctx* ctx, const turt_config* cfg, turt_model** out) {
   TURT_CHECK_CUDA(cudaMallocHost(&m->h_loss, 16));
   TURT_CHECK_CUDA(cudaStreamSynchronize(st));
   *out = m;
+  return OK;
+}
+
+int turt_model_set_attention(turt_model* m, int mode) {
+  TURT_REQUIRE(m, "null model");
+  TURT_REQUIRE(mode == TURT_ATTN_AUTO || mode == TURT_ATTN_TENSOR || mode == TURT_ATTN_FLASH,
+               "attention mode must be 0 (auto), 1 (tensor) or 2 (flash)");
+  const int hd = m->cfg.n_embd / m->cfg.n_head;
+  if (mode == TURT_ATTN_TENSOR) TURT_REQUIRE(attention_tc_supported(hd), "tensor-core attention needs hd % 16 == 0");
+  if (mode == TURT_ATTN_FLASH) TURT_REQUIRE(attention_supported_hd(hd), "flash attention needs hd of 16, 32 or 64");
+  m->attn_mode = mode;
   return OK;
 }
 

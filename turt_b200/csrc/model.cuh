@@ -28,6 +28,7 @@ struct LayerOff {
 
 struct LayerAct {
   float *x, *y1, *rs1, *mu1, *qkv, *att, *lse, *h, *y2, *rs2, *mu2, *pre, *act;
+  float *P, *qr, *kr;  // tensor-core attention: probabilities, rotated q / k (kept for backward)
 };
 
 struct DpState;
@@ -49,11 +50,15 @@ struct turt_model {
   float2* rope_cs = nullptr;
   // workspace for the current token capacity
   int capN = 0, capB = 0;
+  long capS = 0;       // B*H*T*pitch floats per layer of score storage in the workspace
+  int attn_mode = 0;   // TURT_ATTN_*
+  bool attn_tc = false;  // the current workspace uses tensor-core attention
   void* ws = nullptr;
   std::vector<turt::LayerAct> act;
   float *xL = nullptr, *yf = nullptr, *rsf = nullptr, *muf = nullptr, *logits = nullptr, *loss_rows = nullptr;
   float *dx = nullptr, *dy = nullptr, *datt = nullptr, *dqkv = nullptr, *dpre = nullptr, *Dsc = nullptr,
         *part = nullptr;
+  float *dS = nullptr, *dqh = nullptr, *dkh = nullptr;  // tensor-core attention backward scratch
   uint32_t *d_ids = nullptr, *d_tgt = nullptr;
   uint32_t *h_ids = nullptr, *h_tgt = nullptr;  // pinned staging
   float* loss_dev = nullptr;

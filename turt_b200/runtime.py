@@ -104,6 +104,13 @@ class Model:
     def handle(self):
         return self._h
 
+    ATTN_AUTO, ATTN_TENSOR, ATTN_FLASH = 0, 1, 2
+
+    def set_attention(self, mode: int) -> None:
+        """Attention implementation: ATTN_AUTO, ATTN_TENSOR (tensor-core, materialised
+        probabilities) or ATTN_FLASH (fused CUDA-core online softmax)."""
+        check(lib().turt_model_set_attention(self._h, mode))
+
     def num_params(self) -> int:
         t = C.c_size_t()
         check(lib().turt_num_params(self._h, C.byref(t)))
