@@ -157,16 +157,18 @@ def test_sequence_longer_than_block_rejected(ctx):
         model.close()
 
 
+@pytest.mark.parametrize("pair", [0, 1])
 @pytest.mark.parametrize("bn", [64, 128, 192, 256])
 @pytest.mark.parametrize("arch", ["gpt2", "modern"])
-def test_fused_epilogues_every_tile_width(ctx, orc, arch, bn):
-    """Bias / GELU / SwiGLU / residual epilogues under each forced GEMM tile width."""
+def test_fused_epilogues_every_tile_width(ctx, orc, arch, bn, pair):
+    """Bias / GELU / SwiGLU / residual epilogues and the attention GEMMs (two-level batch,
+    causal skips) under each forced GEMM tile width and kernel (single CTA / CTA pair)."""
     from turt_b200._lib import check, lib
-    check(lib().turt_gemm_set_tile(bn))
+    check(lib().turt_gemm_set_tile(bn, pair))
     try:
         loss, ref, le, ge, name = _run_parity(ctx, orc, 512, 96, 2, 2, 128, arch, 3, 80, 352 if arch == "modern" else 0)
     finally:
-        check(lib().turt_gemm_set_tile(0))
+        check(lib().turt_gemm_set_tile(0, -1))
     assert le <= LOSS_TOL, (loss, ref)
     assert ge <= GRAD_TOL, (ge, name)
 

@@ -128,9 +128,10 @@ int turt_get_precision(turt_ctx* ctx, int* precision) {
   return OK;
 }
 
-int turt_gemm_set_tile(int bn) {
+int turt_gemm_set_tile(int bn, int pair) {
   TURT_REQUIRE(bn == 0 || bn == 64 || bn == 128 || bn == 192 || bn == 256, "tile width must be 0, 64, 128, 192 or 256");
-  gemm_set_tile_override(bn);
+  TURT_REQUIRE(pair >= -1 && pair <= 1, "pair must be -1 (automatic), 0 (single CTA) or 1 (CTA pair)");
+  gemm_set_tile_override(bn, pair);
   return OK;
 }
 

@@ -125,17 +125,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* f
   }
 }
 
-// Warp-wide bounded wait in which only lane 0 polls the barrier (a poll by every lane costs
-// shared-memory bandwidth); the __syncwarp orders the other lanes after lane 0's observation
-// of the completed phase.  The result is the same on every lane.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* flags, int site) {
-  int ok = 1;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, flags, site) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  __syncwarp();
-  return ok != 0;
-}
-
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -431,7 +431,7 @@ __global__ void __launch_bounds__(GemmShape<BN, BK, X3>::THREADS, 1)
       bool ok = true;
       for (int i = 0; i < nkt; i++, it++) {
         const int s = it % STAGES;
-        if (!mbar_wait_warp(&full[s], (it / STAGES) & 1, flags, 104)) {
+        if (!mbar_wait(&full[s], (it / STAGES) & 1, flags, 104)) {
           ok = false;
           break;
         }
@@ -470,7 +470,7 @@ __global__ void __launch_bounds__(GemmShape<BN, BK, X3>::THREADS, 1)
       if (!decode(u, m0, n0, b, kt0, nkt)) continue;
       const int acc = t & 1, use = t >> 1;
       t++;
-      if (!mbar_wait_warp(&tfull[acc], use & 1, flags, 103)) {
+      if (!mbar_wait(&tfull[acc], use & 1, flags, 103)) {
         *abort_flag = 1;
         break;
       }
@@ -516,6 +516,408 @@ __global__ void __launch_bounds__(GemmShape<BN, BK, X3>::THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S::TMEM_COLS) : "memory");
+  }
+}
+
+// ------------------------------------------------------------ CTA-pair kernel (3xTF32)
+// Two CTAs of a cluster compute one 256 x BN tile with tcgen05.mma.cta_group::2: each CTA
+// stages its own 128 rows of A and its own BN/2 rows of B (plus their lo parts), and the MMA
+// issued by the even CTA reads both CTAs' tiles.  Per SM this halves the B operand traffic
+// (shared-memory reads, TMA writes and lo-part conversion), which is what bounds the
+// single-CTA kernel.  Both accumulators (128 lanes x BN columns, double-buffered) live in each
+// CTA's own TMEM, so each CTA drains its own rows.
+//
+// Cross-CTA signalling, all without multicast:
+//   full[s]    (each CTA)  its own TMA bytes landed              -> its converter warps
+//   conv[s]    (each CTA)  its 4 converter warps done            -> MMA issuer / odd relay
+//   pconv[s]   (even CTA)  odd CTA's conv[s] completed (relayed) -> MMA issuer
+//   empty[s]   (each CTA)  MMA retired (two commits, one per CTA) -> its producer
+//   tfull[a]   (each CTA)  accumulator a ready (two commits)      -> its epilogue warps
+//   tempty[a]  (each CTA)  its 4 epilogue warps drained a         -> MMA issuer / odd relay
+//   ptempty[a] (even CTA)  odd CTA's tempty[a] completed (relayed) -> MMA issuer
+// Workers arrive on their own CTA's barriers (CTA-scope release, no wait on their earlier
+// stores); two otherwise idle threads of the odd CTA (warp 1 for conv, warp 10 for tempty)
+// forward each completed phase with one cluster-scope arrive.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t peer_addr(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Bounded wait with cluster-scope acquire, for barriers that the other CTA arrives on.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* flags, int site) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      if (flags) atomicExch(&flags[FLAG_TIMEOUT], site);
+      return false;
+    }
+  }
+}
+// Arrive on an mbarrier given by its shared::cluster address (this CTA's or the peer's).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+__device__ __forceinline__ void mma_tf32_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster_addr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster_addr)
+               : "memory");
+}
+
+template <int BN>
+struct PairShape {
+  static constexpr int BK = 16;
+  static constexpr int BH = BN / 2;  // B rows staged by each CTA
+  static constexpr int A_BYTES = BM * BK * 4;
+  static constexpr int B_BYTES = BH * BK * 4;
+  static constexpr int HI_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGE_BYTES = HI_BYTES * 2;
+  static constexpr int MN_BOX = 32 * BK * 4;
+  static constexpr int THREADS = 352;
+  static constexpr uint32_t TMEM_COLS = 2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512);
+  static constexpr int STAGES_FIT = (232448 - 1024 - 512) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 512;
+};
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(352, 1)
+    k_gemm_tf32_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmEpi epi,
+                     int M, int N, int K, int batches, int bdiv, int causal, int* flags) {
+  using S = PairShape<BN>;
+  constexpr int STAGES = S::STAGES, BK = S::BK;
+  static_assert(BN % 64 == 0 && BN <= 256, "BN");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * S::STAGE_BYTES);
+  uint64_t* conv = full + STAGES;
+  uint64_t* pconv = conv + STAGES;
+  uint64_t* empty = pconv + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* ptempty = tempty + 2;
+  uint64_t* done = ptempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int mt = (M + 2 * BM - 1) / (2 * BM), nt = (N + BN - 1) / BN;
+  const int units = mt * nt * batches;
+  const int kt_total = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], 4);
+      mbar_init(&pconv[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+      mbar_init(&ptempty[b], 1);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(S::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any cross-CTA use
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // shared::cluster addresses of the even CTA's relay targets
+  const uint32_t lead_pconv = peer_addr(smem_u32(pconv), 0);
+  const uint32_t lead_ptempty = peer_addr(smem_u32(ptempty), 0);
+
+  // unit -> (m0 of the 256-row pair tile, n0, batch, k-tile range); false = causal skip
+  auto decode = [&](int u, int& m0, int& n0, int& b, int& kt0, int& nkt) {
+    m0 = (u % mt) * 2 * BM;
+    u /= mt;
+    n0 = (u % nt) * BN;
+    b = u / nt;
+    kt0 = 0;
+    int kt1 = kt_total;
+    if (causal == CAUSAL_SKIP_UPPER && n0 >= m0 + 2 * BM) return false;
+    if (causal == CAUSAL_K_LOWER) kt1 = min(kt1, (m0 + 2 * BM + BK - 1) / BK);
+    if (causal == CAUSAL_K_UPPER) kt0 = m0 / BK;
+    nkt = kt1 - kt0;
+    return nkt > 0;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer (both CTAs)
+      uint32_t it = 0;
+      for (int u = pair; u < units && !*abort_flag; u += npairs) {
+        int m0, n0, b, kt0, nkt;
+        if (!decode(u, m0, n0, b, kt0, nkt)) continue;
+        const int ma0 = m0 + (int)rank * BM;       // this CTA's A rows
+        const int nb0 = n0 + (int)rank * S::BH;    // this CTA's B rows (output columns)
+        // Rows beyond M (columns beyond N) only feed accumulator rows (columns) that are
+        // never written: their boxes are not loaded and their stale tiles are harmless.
+        int na = 0, nbx = 0;
+        if (A_MN) {
+          for (int j = 0; j < BM / 32; j++) na += (ma0 + 32 * j < M);
+        } else {
+          na = ma0 < M;
+        }
+        if (B_MN) {
+          for (int j = 0; j < S::BH / 32; j++) nbx += (nb0 + 32 * j < N);
+        } else {
+          nbx = nb0 < N;
+        }
+        const uint32_t bytes =
+            (A_MN ? na * S::MN_BOX : na * S::A_BYTES) + (B_MN ? nbx * S::MN_BOX : nbx * S::B_BYTES);
+        const int bi = b % bdiv, bo = b / bdiv;
+        for (int i = 0; i < nkt; i++, it++) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&empty[s], ((it / STAGES) + 1) & 1, flags, 111)) {
+            *abort_flag = 1;
+            break;
+          }
+          const int kc = (kt0 + i) * BK;
+          const uint32_t sa = smem_u32(smem + s * S::STAGE_BYTES);
+          const uint32_t sb = sa + S::A_BYTES;
+          mbar_arrive_expect_tx(&full[s], bytes);
+          if (!A_MN) {
+            if (na) tma_load_4d(sa, &tmA, kc, ma0, bi, bo, &full[s]);
+          } else {
+            for (int j = 0; j < BM / 32; j++)
+              if (ma0 + 32 * j < M) tma_load_4d(sa + j * S::MN_BOX, &tmA, ma0 + 32 * j, kc, bi, bo, &full[s]);
+          }
+          if (!B_MN) {
+            if (nbx) tma_load_4d(sb, &tmB, kc, nb0, bi, bo, &full[s]);
+          } else {
+            for (int j = 0; j < S::BH / 32; j++)
+              if (nb0 + 32 * j < N) tma_load_4d(sb + j * S::MN_BOX, &tmB, nb0 + 32 * j, kc, bi, bo, &full[s]);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ------------------------------------------------ MMA issuer (even CTA)
+      constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((A_MN ? 1u : 0u) << 15) |
+                                 ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
+                                 ((uint32_t)((2 * BM) >> 4) << 24);
+      const uint32_t empty_peer = peer_addr(smem_u32(empty), 1);
+      const uint32_t tfull_peer = peer_addr(smem_u32(tfull), 1);
+      uint32_t it = 0;
+      int t = 0;
+      for (int u = pair; u < units && !*abort_flag; u += npairs) {
+        int m0, n0, b, kt0, nkt;
+        if (!decode(u, m0, n0, b, kt0, nkt)) continue;
+        const int acc = t & 1, use = t >> 1;
+        t++;
+        if (!mbar_wait(&tempty[acc], (use + 1) & 1, flags, 115) ||
+            !mbar_wait_cluster(&ptempty[acc], (use + 1) & 1, flags, 117)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int i = 0; i < nkt; i++, it++) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&conv[s], (it / STAGES) & 1, flags, 112) ||
+              !mbar_wait_cluster(&pconv[s], (it / STAGES) & 1, flags, 118)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * S::STAGE_BYTES);
+          const uint32_t sb = sa + S::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; kk++) {
+            const uint32_t oa = A_MN ? kk * 1024 : kk * 32, ob = B_MN ? kk * 1024 : kk * 32;
+            const uint64_t da = A_MN ? smem_desc(sa + oa, S::MN_BOX, 512, kLayoutSW128Atom32)
+                                     : smem_desc(sa + oa, 16, 512, kLayoutSW64);
+            const uint64_t db = B_MN ? smem_desc(sb + ob, S::MN_BOX, 512, kLayoutSW128Atom32)
+                                     : smem_desc(sb + ob, 16, 512, kLayoutSW64);
+            const uint32_t first = (i > 0 || kk > 0) ? 1u : 0u;
+            const uint64_t lo = (uint64_t)(S::HI_BYTES >> 4);
+            mma_tf32_pair(d, da + lo, db, idesc, first);
+            mma_tf32_pair(d, da, db + lo, idesc, 1u);
+            mma_tf32_pair(d, da, db, idesc, 1u);
+          }
+          mma_commit_pair(smem_u32(&empty[s]));
+          mma_commit_pair(empty_peer + (uint32_t)(s * 8));
+        }
+        if (!ok) {
+          *abort_flag = 1;
+          break;
+        }
+        mma_commit_pair(smem_u32(&tfull[acc]));
+        mma_commit_pair(tfull_peer + (uint32_t)(acc * 8));
+      }
+      mma_commit_pair(smem_u32(done));
+      if (!mbar_wait(done, 0, flags, 116)) *abort_flag = 1;
+    } else if (lane == 0 && rank == 1) {
+      // ------------------------------------------------ conv relay (odd CTA)
+      uint32_t it = 0;
+      for (int u = pair; u < units && !*abort_flag; u += npairs) {
+        int m0, n0, b, kt0, nkt;
+        if (!decode(u, m0, n0, b, kt0, nkt)) continue;
+        bool ok = true;
+        for (int i = 0; i < nkt; i++, it++) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&conv[s], (it / STAGES) & 1, flags, 119)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_cluster(lead_pconv + (uint32_t)(s * 8));
+        }
+        if (!ok) {
+          *abort_flag = 1;
+          break;
+        }
+      }
+    }
+  } else if (warp == 10) {
+    if (lane == 0 && rank == 1) {
+      // ------------------------------------------------ tempty relay (odd CTA)
+      int t = 0;
+      for (int u = pair; u < units && !*abort_flag; u += npairs) {
+        int m0, n0, b, kt0, nkt;
+        if (!decode(u, m0, n0, b, kt0, nkt)) continue;
+        const int acc = t & 1, use = t >> 1;
+        t++;
+        if (!mbar_wait(&tempty[acc], use & 1, flags, 120)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_cluster(lead_ptempty + (uint32_t)(acc * 8));
+      }
+    }
+  } else if (warp >= 6) {
+    // -------------------------------------------------- lo-part converters (both CTAs)
+    const int ct = threadIdx.x - 192;
+    uint32_t it = 0;
+    for (int u = pair; u < units && !*abort_flag; u += npairs) {
+      int m0, n0, b, kt0, nkt;
+      if (!decode(u, m0, n0, b, kt0, nkt)) continue;
+      bool ok = true;
+      for (int i = 0; i < nkt; i++, it++) {
+        const int s = it % STAGES;
+        if (!mbar_wait(&full[s], (it / STAGES) & 1, flags, 114)) {
+          ok = false;
+          break;
+        }
+        const float4* hi = reinterpret_cast<const float4*>(smem + s * S::STAGE_BYTES);
+        float4* lo = reinterpret_cast<float4*>(smem + s * S::STAGE_BYTES + S::HI_BYTES);
+#pragma unroll 4
+        for (int e = ct; e < S::HI_BYTES / 16; e += 128) {
+          const float4 v = hi[e];
+          float4 r;
+          r.x = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+          r.y = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+          r.z = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+          r.w = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+          lo[e] = r;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[s]);
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        break;
+      }
+    }
+  } else {
+    // -------------------------------------------------- epilogue warps (2..5, both CTAs)
+    const int q = warp & 3;
+    const EpiVec vec{(epi.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(epi.C) & 15) == 0) && (epi.strideC % 4 == 0) &&
+                         (epi.strideC_hi % 4 == 0),
+                     epi.R && (epi.ldr % 4 == 0) && ((reinterpret_cast<uintptr_t>(epi.R) & 15) == 0),
+                     epi.C2 && (epi.ldc2 % 4 == 0) && ((reinterpret_cast<uintptr_t>(epi.C2) & 15) == 0)};
+    int t = 0;
+    for (int u = pair; u < units && !*abort_flag; u += npairs) {
+      int m0, n0, b, kt0, nkt;
+      if (!decode(u, m0, n0, b, kt0, nkt)) continue;
+      const int acc = t & 1, use = t >> 1;
+      t++;
+      if (!mbar_wait(&tfull[acc], use & 1, flags, 113)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const long row = m0 + (int)rank * BM + q * 32 + lane;
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      const long cboff = (long)(b % bdiv) * epi.strideC + (long)(b / bdiv) * epi.strideC_hi;
+      float* Cb = epi.C + cboff;
+      if (epi.kind == EPI_SWIGLU_FWD) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; c += 2) {
+          const int col0 = n0 + c * 32;
+          float g[32], v[32];
+          tmem_ld32(tbase + c * 32, g);
+          tmem_ld32(tbase + (c + 1) * 32, v);
+          if (row < M && col0 < N) {
+            st32(Cb + row * epi.ldc + col0, g, min(32, N - col0), vec.C);
+            st32(Cb + row * epi.ldc + col0 + 32, v, min(32, N - col0 - 32), vec.C);
+#pragma unroll
+            for (int j = 0; j < 32; j++) v[j] *= g[j] * sigmoid_f(g[j]);
+            st32(epi.C2 + row * epi.ldc2 + col0 / 2, v, min(32, N - col0 - 32), vec.C2);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; c++) {
+          const int col0 = n0 + c * 32;
+          if (col0 >= N) break;
+          float v[32];
+          tmem_ld32(tbase + c * 32, v);
+          if (row < M) epi_chunk(epi, vec, v, Cb, row, col0, min(32, N - col0), cboff);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // every MMA retired (the even CTA waited on `done`) before TMEM is released
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S::TMEM_COLS) : "memory");
   }
 }
 
@@ -677,44 +1079,123 @@ int dispatch_bn(int bn, bool amn, bool bmn, const LaunchArgs& a) {
   }
 }
 
-// Cost of one 32-deep k-step of a 128 x BN tile, in SM cycles, from the shared-memory
-// traffic it needs (TMA writes, tensor-core operand reads, 3xTF32 lo-part conversion) at
-// 128 B/cycle; it is above the tensor-pipe time of the step for every BN.
-long kstep_cycles(int bn, bool x3) {
-  const long bytes = x3 ? 98304 + 768L * bn : 32768 + 256L * bn;
-  return bytes / 128;
+template <int BN, bool A_MN, bool B_MN>
+int launch_pair(const LaunchArgs& a) {
+  using S = PairShape<BN>;
+  static_assert(S::SMEM <= 232448, "gemm: shared memory budget exceeded");
+  static_assert(S::STAGES >= 3, "gemm: fewer than three pipeline stages fit");
+  auto kfn = k_gemm_tf32_pair<BN, A_MN, B_MN>;
+  static int max_pairs = 0;
+  if (!max_pairs) {
+    TURT_CHECK_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM));
+    cudaLaunchConfig_t q = {};
+    cudaLaunchAttribute qa[1];
+    qa[0].id = cudaLaunchAttributeClusterDimension;
+    qa[0].val.clusterDim.x = 2;
+    qa[0].val.clusterDim.y = 1;
+    qa[0].val.clusterDim.z = 1;
+    q.gridDim = dim3(2 * 74);
+    q.blockDim = dim3(S::THREADS);
+    q.dynamicSmemBytes = S::SMEM;
+    q.attrs = qa;
+    q.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kfn, &q) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = num_sms() / 2;
+    }
+    max_pairs = n;
+  }
+  const long units = (long)ceil_div(a.M, 2 * BM) * ceil_div(a.N, BN) * a.batch;
+  const int pairs = (int)(units < max_pairs ? units : max_pairs);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(S::THREADS);
+  cfg.dynamicSmemBytes = S::SMEM;
+  cfg.stream = a.st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  TURT_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kfn, a.ma, a.mb, a.epi, a.M, a.N, a.K, a.batch, a.bdiv, a.causal, a.flags));
+  note_launch();
+  return OK;
+}
+
+int dispatch_pair(int bn, bool amn, bool bmn, const LaunchArgs& a) {
+#define TURT_PAIR_BN(BNV)                                            \
+  if (!amn && !bmn) return launch_pair<BNV, false, false>(a);        \
+  if (!amn && bmn) return launch_pair<BNV, false, true>(a);          \
+  if (amn && !bmn) return launch_pair<BNV, true, false>(a);          \
+  return launch_pair<BNV, true, true>(a);
+  switch (bn) {
+    case 64: {
+      TURT_PAIR_BN(64)
+    }
+    case 128: {
+      TURT_PAIR_BN(128)
+    }
+    case 192: {
+      TURT_PAIR_BN(192)
+    }
+    default: {
+      TURT_PAIR_BN(256)
+    }
+  }
+#undef TURT_PAIR_BN
+}
+
+// Per-SM cycles of one 32-deep k-step for a 128-row slice of a BN-wide tile: the larger of
+// the tensor-pipe time (3 or 1 MMAs of 128 x BN x 8 per 8 of K at ~1890 MAC/cycle) and the
+// shared-memory time at 128 B/cycle (TMA writes, operand reads by the MMAs, 3xTF32 lo-part
+// conversion).  A CTA pair stages and converts only half of B per SM.
+long kstep_cycles(int bn, bool x3, bool pair) {
+  const long mma = (x3 ? 13L : 13L / 3) * bn / 2;
+  const long smem = x3 ? (pair ? 768 + 3L * bn : 768 + 6L * bn) : 256 + 2L * bn;
+  return mma > smem ? mma : smem;
 }
 
 struct TilePlan {
   int bn = 256;
   int ks = 1;
+  bool pair = false;
 };
 
-// Tile width and K-split count with the shortest modelled makespan:
-//   ceil(units / SMs) x (k-steps per unit x step cost) + pipeline fill + one epilogue drain,
-// plus, per extra split, the atomic reduction of the M x N output.  `max_ks` is 1 when the
-// epilogue cannot accumulate partial sums.
-TilePlan plan_tiles(int M, int N, int K, int batch, bool x3, int max_ks, int force_bn) {
+// Tile width, K-split count and single-CTA / CTA-pair kernel with the shortest modelled
+// makespan: ceil(units / concurrent units) x (k-steps per unit x step cost) + pipeline fill
+// + one epilogue drain, plus, per extra split, the atomic reduction of the M x N output.
+// `max_ks` is 1 when the epilogue cannot accumulate partial sums.  Pairs run 3xTF32 only,
+// without K splits.
+TilePlan plan_tiles(int M, int N, int K, int batch, bool x3, int max_ks, int force_bn, int force_pair) {
   const int sms = num_sms();
   const long k32 = (K + 31) / 32;
   TilePlan best;
   double best_cost = -1;
   const int widths[4] = {256, 192, 128, 64};
-  for (int bn : widths) {
-    if (force_bn && bn != force_bn) continue;
-    if (!force_bn && bn > 64 && N <= bn / 2) continue;  // most of the tile would be empty
-    const long tiles = (long)ceil_div(M, BM) * ceil_div(N, bn) * batch;
-    for (int ks = 1; ks <= max_ks; ks++) {
-      if (ks > 1 && tiles * (ks - 1) >= sms) break;  // already a full wave without this split
-      const long units = tiles * ks;
-      const long rounds = (units + sms - 1) / sms;
-      const double steps = (double)((k32 + ks - 1) / ks);
-      double cost = rounds * steps * kstep_cycles(bn, x3) + 2000.0 + 16.0 * bn;
-      if (ks > 1) cost += (double)M * N * batch * ks / (sms * 8.0);  // float4 atomics
-      if (best_cost < 0 || cost < best_cost) {
-        best_cost = cost;
-        best.bn = bn;
-        best.ks = ks;
+  for (int pair = 0; pair <= (x3 ? 1 : 0); pair++) {
+    if (force_pair >= 0 && pair != force_pair) continue;
+    for (int bn : widths) {
+      if (force_bn && bn != force_bn) continue;
+      if (!force_bn && bn > 64 && N <= bn / 2) continue;  // most of the tile would be empty
+      const int rows = pair ? 2 * BM : BM;
+      const long tiles = (long)ceil_div(M, rows) * ceil_div(N, bn) * batch;
+      const long slots = pair ? sms / 2 : sms;
+      for (int ks = 1; ks <= (pair ? 1 : max_ks); ks++) {
+        if (ks > 1 && tiles * (ks - 1) >= slots) break;  // already a full wave without this split
+        const long units = tiles * ks;
+        const long rounds = (units + slots - 1) / slots;
+        const double steps = (double)((k32 + ks - 1) / ks);
+        double cost = rounds * steps * kstep_cycles(bn, x3, pair) + 2000.0 + 16.0 * bn;
+        if (ks > 1) cost += (double)M * N * batch * ks / (sms * 8.0);  // float4 atomics
+        if (best_cost < 0 || cost < best_cost) {
+          best_cost = cost;
+          best.bn = bn;
+          best.ks = ks;
+          best.pair = pair != 0;
+        }
       }
     }
   }
@@ -722,10 +1203,14 @@ TilePlan plan_tiles(int M, int N, int K, int batch, bool x3, int max_ks, int for
 }
 
 std::atomic<int> g_tile_override{0};
+std::atomic<int> g_pair_override{-1};
 
 }  // namespace
 
-void gemm_set_tile_override(int bn) { g_tile_override.store(bn); }
+void gemm_set_tile_override(int bn, int pair) {
+  g_tile_override.store(bn);
+  g_pair_override.store(pair);
+}
 
 bool gemm_tf32_supported(const GemmOperand& A, const GemmOperand& B) {
   auto ok = [](const GemmOperand& o) {
@@ -765,7 +1250,11 @@ int gemm_tf32(cudaStream_t stream, int M, int N, int K, int batch, const GemmOpe
   const bool can_split = (la.epi.kind == EPI_ACCUM || la.epi.kind == EPI_STORE || la.epi.kind == EPI_RED) &&
                          la.causal == CAUSAL_NONE;
   const int max_ks = force_splits > 0 ? 1 : (can_split ? std::max(1, K / 256) : 1);
-  const TilePlan plan = plan_tiles(M, N, K, batch, x3, std::min(max_ks, 64), force_bn);
+  // The CTA-pair kernel is exact but measured no faster than the single-CTA kernel on the
+  // train-step shapes (its cross-CTA handshakes leave the tensor pipe idle), so it runs only
+  // when forced.
+  const int force_pair = x3 ? (g_pair_override.load() == 1 ? 1 : 0) : 0;
+  const TilePlan plan = plan_tiles(M, N, K, batch, x3, std::min(max_ks, 64), force_bn, force_splits > 0 ? 0 : force_pair);
   const int BN = plan.bn;
   const int kt_total = ceil_div(K, BK);
   const int ks = force_splits > 0 ? force_splits : plan.ks;
@@ -788,10 +1277,12 @@ int gemm_tf32(cudaStream_t stream, int M, int N, int K, int batch, const GemmOpe
     rc = make_map(&la.ma, A.ptr, M, K, bdiv, batch / bdiv, A.ld, A.stride, A.stride_hi, 32, BK, true);
   if (rc) return rc;
   if (!B.mn_major)
-    rc = make_map(&la.mb, B.ptr, K, N, bdiv, batch / bdiv, B.ld, B.stride, B.stride_hi, BK, BN, false);
+    rc = make_map(&la.mb, B.ptr, K, N, bdiv, batch / bdiv, B.ld, B.stride, B.stride_hi, BK, plan.pair ? BN / 2 : BN,
+                  false);
   else
     rc = make_map(&la.mb, B.ptr, N, K, bdiv, batch / bdiv, B.ld, B.stride, B.stride_hi, 32, BK, true);
   if (rc) return rc;
+  if (plan.pair) return dispatch_pair(BN, A.mn_major, B.mn_major, la);
   return x3 ? dispatch_bn<true>(BN, A.mn_major, B.mn_major, la) : dispatch_bn<false>(BN, A.mn_major, B.mn_major, la);
 }
 

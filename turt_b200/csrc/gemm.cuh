@@ -72,8 +72,9 @@ int gemm_tf32(cudaStream_t stream, int M, int N, int K, int batch, const GemmOpe
 // True when gemm_tf32 can take these operands (TMA needs 16-byte pitches and bases).
 bool gemm_tf32_supported(const GemmOperand& A, const GemmOperand& B);
 
-// Forces the output-tile width of every later gemm_tf32 call (64/128/192/256; 0 = automatic).
-void gemm_set_tile_override(int bn);
+// Forces the output-tile width (64/128/192/256; 0 = automatic) and the kernel (pair = 1: CTA
+// pair, 0: single CTA, -1: automatic) of every later gemm_tf32 call.
+void gemm_set_tile_override(int bn, int pair);
 
 // CUDA-core fp32 GEMM for shapes the TMA path cannot address (odd pitches): same
 // flags as the reference's MATMUL kernel (src/infer/webgpu/autograd.ts:33-75).
