@@ -70,133 +70,186 @@ __global__ void k_unrope_heads(const float* __restrict__ dq, const float* __rest
   }
 }
 
-constexpr int kRowWarps = 8;  // rows (one warp each) per 256-thread block
-constexpr int kMaxRegChunks = 8;  // rows up to 32 * 4 * 8 = 1024 keys stay in registers
+constexpr int kRowWarps = 8;       // warps per 256-thread block
 
-// Causal softmax of one score row in place: P[j] = exp(s_j*scale - max) / sum for j <= i,
-// 0 for i < j < pitch.  Lane `lane` owns the float4 chunks starting at 4*(32c + lane); rows
-// longer than the register budget take the three-pass loop.  Entries right of the diagonal
-// may be unwritten (skipped score tiles): they are read only into masked lanes.
-template <bool REG>
+// Causal softmax of score rows in place: P[j] = exp(s_j*scale - max) / sum for j <= i, 0 for
+// i < j < pitch.  A warp handles R consecutive rows at once (more loads in flight); lane `lane`
+// owns the float4 chunks starting at 4*(32c + lane), c < C = ceil(pitch / 128).  Entries
+// right of the diagonal may be unwritten (skipped score tiles): they are read only into
+// masked lanes.
+template <int C, int R>
 __global__ void __launch_bounds__(256) k_softmax_causal(float* __restrict__ S, long rows, int T, long pitch,
                                                         float scale) {
-  const long row = (long)blockIdx.x * kRowWarps + threadIdx.x / 32;
+  const long row0 = ((long)blockIdx.x * kRowWarps + threadIdx.x / 32) * R;
   const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const int i = (int)(row % T);
-  float* p = S + (row / T) * T * pitch + (long)i * pitch;
-  const int n = i + 1;  // valid keys
-  float mx = -INFINITY;
-  if (REG) {
-    float v[kMaxRegChunks * 4];
+  if (row0 >= rows) return;
+  float v[R][C * 4];
+  float mx[R];
 #pragma unroll
-    for (int c = 0; c < kMaxRegChunks; c++) {
+  for (int r = 0; r < R; r++) {
+    const long row = row0 + r;
+    const int n = row < rows ? (int)(row % T) + 1 : 0;  // valid keys
+    const float* p = S + (row / T) * T * pitch + (row % T) * pitch;
+    mx[r] = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < C; c++) {
       const int j0 = (c * 32 + lane) * 4;
       float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
       if (j0 < n) x = *reinterpret_cast<const float4*>(p + j0);
-      v[c * 4 + 0] = j0 + 0 < n ? x.x * scale : -INFINITY;
-      v[c * 4 + 1] = j0 + 1 < n ? x.y * scale : -INFINITY;
-      v[c * 4 + 2] = j0 + 2 < n ? x.z * scale : -INFINITY;
-      v[c * 4 + 3] = j0 + 3 < n ? x.w * scale : -INFINITY;
-#pragma unroll
-      for (int u = 0; u < 4; u++) mx = fmaxf(mx, v[c * 4 + u]);
+      v[r][c * 4 + 0] = j0 + 0 < n ? x.x * scale : -INFINITY;
+      v[r][c * 4 + 1] = j0 + 1 < n ? x.y * scale : -INFINITY;
+      v[r][c * 4 + 2] = j0 + 2 < n ? x.z * scale : -INFINITY;
+      v[r][c * 4 + 3] = j0 + 3 < n ? x.w * scale : -INFINITY;
     }
-    mx = warp_max(mx);
+  }
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+#pragma unroll
+    for (int c = 0; c < C * 4; c++) mx[r] = fmaxf(mx[r], v[r][c]);
+    mx[r] = warp_max(mx[r]);
+  }
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+    const long row = row0 + r;
+    if (row >= rows) break;
     float sum = 0.f;
 #pragma unroll
-    for (int c = 0; c < kMaxRegChunks * 4; c++) {
-      v[c] = expf(v[c] - mx);  // exp(-inf) = 0 for masked keys
-      sum += v[c];
+    for (int c = 0; c < C * 4; c++) {
+      v[r][c] = expf(v[r][c] - mx[r]);  // exp(-inf) = 0 for masked keys
+      sum += v[r][c];
     }
     sum = warp_sum(sum);
     const float inv = 1.0f / sum;
+    float* p = S + (row / T) * T * pitch + (row % T) * pitch;
 #pragma unroll
-    for (int c = 0; c < kMaxRegChunks; c++) {
+    for (int c = 0; c < C; c++) {
       const int j0 = (c * 32 + lane) * 4;
       if (j0 < pitch)
         *reinterpret_cast<float4*>(p + j0) =
-            make_float4(v[c * 4] * inv, v[c * 4 + 1] * inv, v[c * 4 + 2] * inv, v[c * 4 + 3] * inv);
+            make_float4(v[r][c * 4] * inv, v[r][c * 4 + 1] * inv, v[r][c * 4 + 2] * inv, v[r][c * 4 + 3] * inv);
     }
-  } else {
-    for (int j = lane; j < n; j += 32) mx = fmaxf(mx, p[j] * scale);
-    mx = warp_max(mx);
-    float sum = 0.f;
-    for (int j = lane; j < n; j += 32) sum += expf(p[j] * scale - mx);
-    sum = warp_sum(sum);
-    const float inv = 1.0f / sum;
-    for (int j = lane; j < pitch; j += 32) p[j] = j < n ? expf(p[j] * scale - mx) * inv : 0.f;
   }
 }
 
-// Softmax + scale backward of one row, in place over dP: dS_j = P_j (dP_j - sum_k P_k dP_k) * scale
-// for j <= i, 0 right of the diagonal (masked scores get no gradient).
-template <bool REG>
-__global__ void __launch_bounds__(256) k_softmax_causal_bwd(const float* __restrict__ P, float* __restrict__ dP,
-                                                            long rows, int T, long pitch, float scale) {
+// Rows longer than the register budget: three passes over memory, one warp per row.
+__global__ void __launch_bounds__(256) k_softmax_causal_long(float* __restrict__ S, long rows, int T, long pitch,
+                                                             float scale) {
   const long row = (long)blockIdx.x * kRowWarps + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
-  const int i = (int)(row % T);
-  const long off = (row / T) * T * pitch + (long)i * pitch;
-  const float* p = P + off;
-  float* g = dP + off;
-  const int n = i + 1;
-  float dot = 0.f;
-  if (REG) {
-    float pv[kMaxRegChunks * 4], gv[kMaxRegChunks * 4];
+  float* p = S + (row / T) * T * pitch + (row % T) * pitch;
+  const int n = (int)(row % T) + 1;
+  float mx = -INFINITY;
+  for (int j = lane; j < n; j += 32) mx = fmaxf(mx, p[j] * scale);
+  mx = warp_max(mx);
+  float sum = 0.f;
+  for (int j = lane; j < n; j += 32) sum += expf(p[j] * scale - mx);
+  sum = warp_sum(sum);
+  const float inv = 1.0f / sum;
+  for (int j = lane; j < pitch; j += 32) p[j] = j < n ? expf(p[j] * scale - mx) * inv : 0.f;
+}
+
+// Softmax + scale backward, in place over dP: dS_j = P_j (dP_j - sum_k P_k dP_k) * scale for
+// j <= i, 0 right of the diagonal (masked scores get no gradient).  Same row mapping as above.
+template <int C, int R>
+__global__ void __launch_bounds__(256) k_softmax_causal_bwd(const float* __restrict__ P, float* __restrict__ dP,
+                                                            long rows, int T, long pitch, float scale) {
+  const long row0 = ((long)blockIdx.x * kRowWarps + threadIdx.x / 32) * R;
+  const int lane = threadIdx.x & 31;
+  if (row0 >= rows) return;
+  float pv[R][C * 4], gv[R][C * 4], dot[R];
 #pragma unroll
-    for (int c = 0; c < kMaxRegChunks; c++) {
+  for (int r = 0; r < R; r++) {
+    const long row = row0 + r;
+    const int n = row < rows ? (int)(row % T) + 1 : 0;
+    const long off = (row / T) * T * pitch + (row % T) * pitch;
+    dot[r] = 0.f;
+#pragma unroll
+    for (int c = 0; c < C; c++) {
       const int j0 = (c * 32 + lane) * 4;
       float4 a = make_float4(0.f, 0.f, 0.f, 0.f), d = a;
       if (j0 < n) {
-        a = *reinterpret_cast<const float4*>(p + j0);
-        d = *reinterpret_cast<const float4*>(g + j0);
+        a = *reinterpret_cast<const float4*>(P + off + j0);
+        d = *reinterpret_cast<const float4*>(dP + off + j0);
       }
-      pv[c * 4 + 0] = j0 + 0 < n ? a.x : 0.f;
-      pv[c * 4 + 1] = j0 + 1 < n ? a.y : 0.f;
-      pv[c * 4 + 2] = j0 + 2 < n ? a.z : 0.f;
-      pv[c * 4 + 3] = j0 + 3 < n ? a.w : 0.f;
-      gv[c * 4 + 0] = j0 + 0 < n ? d.x : 0.f;
-      gv[c * 4 + 1] = j0 + 1 < n ? d.y : 0.f;
-      gv[c * 4 + 2] = j0 + 2 < n ? d.z : 0.f;
-      gv[c * 4 + 3] = j0 + 3 < n ? d.w : 0.f;
-#pragma unroll
-      for (int u = 0; u < 4; u++) dot += pv[c * 4 + u] * gv[c * 4 + u];
+      pv[r][c * 4 + 0] = j0 + 0 < n ? a.x : 0.f;
+      pv[r][c * 4 + 1] = j0 + 1 < n ? a.y : 0.f;
+      pv[r][c * 4 + 2] = j0 + 2 < n ? a.z : 0.f;
+      pv[r][c * 4 + 3] = j0 + 3 < n ? a.w : 0.f;
+      gv[r][c * 4 + 0] = j0 + 0 < n ? d.x : 0.f;
+      gv[r][c * 4 + 1] = j0 + 1 < n ? d.y : 0.f;
+      gv[r][c * 4 + 2] = j0 + 2 < n ? d.z : 0.f;
+      gv[r][c * 4 + 3] = j0 + 3 < n ? d.w : 0.f;
     }
-    dot = warp_sum(dot);
+  }
 #pragma unroll
-    for (int c = 0; c < kMaxRegChunks; c++) {
+  for (int r = 0; r < R; r++) {
+#pragma unroll
+    for (int c = 0; c < C * 4; c++) dot[r] += pv[r][c] * gv[r][c];
+    dot[r] = warp_sum(dot[r]);
+  }
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+    const long row = row0 + r;
+    if (row >= rows) break;
+    float* g = dP + (row / T) * T * pitch + (row % T) * pitch;
+#pragma unroll
+    for (int c = 0; c < C; c++) {
       const int j0 = (c * 32 + lane) * 4;
       if (j0 < pitch) {
-        float4 r;
-        r.x = pv[c * 4 + 0] * (gv[c * 4 + 0] - dot) * scale;
-        r.y = pv[c * 4 + 1] * (gv[c * 4 + 1] - dot) * scale;
-        r.z = pv[c * 4 + 2] * (gv[c * 4 + 2] - dot) * scale;
-        r.w = pv[c * 4 + 3] * (gv[c * 4 + 3] - dot) * scale;
-        *reinterpret_cast<float4*>(g + j0) = r;
+        float4 o;
+        o.x = pv[r][c * 4 + 0] * (gv[r][c * 4 + 0] - dot[r]) * scale;
+        o.y = pv[r][c * 4 + 1] * (gv[r][c * 4 + 1] - dot[r]) * scale;
+        o.z = pv[r][c * 4 + 2] * (gv[r][c * 4 + 2] - dot[r]) * scale;
+        o.w = pv[r][c * 4 + 3] * (gv[r][c * 4 + 3] - dot[r]) * scale;
+        *reinterpret_cast<float4*>(g + j0) = o;
       }
     }
-  } else {
-    for (int j = lane; j < n; j += 32) dot += p[j] * g[j];
-    dot = warp_sum(dot);
-    for (int j = lane; j < pitch; j += 32) g[j] = j < n ? p[j] * (g[j] - dot) * scale : 0.f;
   }
 }
 
+__global__ void __launch_bounds__(256) k_softmax_causal_bwd_long(const float* __restrict__ P, float* __restrict__ dP,
+                                                                 long rows, int T, long pitch, float scale) {
+  const long row = (long)blockIdx.x * kRowWarps + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const long off = (row / T) * T * pitch + (row % T) * pitch;
+  const float* p = P + off;
+  float* g = dP + off;
+  const int n = (int)(row % T) + 1;
+  float dot = 0.f;
+  for (int j = lane; j < n; j += 32) dot += p[j] * g[j];
+  dot = warp_sum(dot);
+  for (int j = lane; j < pitch; j += 32) g[j] = j < n ? p[j] * (g[j] - dot) * scale : 0.f;
+}
+
+template <int C>
+int rows_launch_c(cudaStream_t st, long rows, int T, long pitch, float scale, float* S, const float* P, bool bwd) {
+  constexpr int R = C <= 2 ? 4 : (C <= 4 ? 2 : 1);  // rows per warp: ~8 float4 loads in flight per array
+  const int blocks = (int)((rows + kRowWarps * R - 1) / (kRowWarps * R));
+  if (!bwd)
+    k_softmax_causal<C, R><<<blocks, 256, 0, st>>>(S, rows, T, pitch, scale);
+  else
+    k_softmax_causal_bwd<C, R><<<blocks, 256, 0, st>>>(P, S, rows, T, pitch, scale);
+  TURT_LAUNCH_CHECK();
+  return OK;
+}
+
 int rows_launch(cudaStream_t st, long rows, int T, long pitch, float scale, float* S, const float* P, bool bwd) {
-  const int blocks = (int)((rows + kRowWarps - 1) / kRowWarps);
-  const bool reg = pitch <= 32 * 4 * kMaxRegChunks;
-  if (!bwd) {
-    if (reg)
-      k_softmax_causal<true><<<blocks, 256, 0, st>>>(S, rows, T, pitch, scale);
-    else
-      k_softmax_causal<false><<<blocks, 256, 0, st>>>(S, rows, T, pitch, scale);
-  } else {
-    if (reg)
-      k_softmax_causal_bwd<true><<<blocks, 256, 0, st>>>(P, S, rows, T, pitch, scale);
-    else
-      k_softmax_causal_bwd<false><<<blocks, 256, 0, st>>>(P, S, rows, T, pitch, scale);
+  switch ((pitch + 127) / 128) {
+    case 1: return rows_launch_c<1>(st, rows, T, pitch, scale, S, P, bwd);
+    case 2: return rows_launch_c<2>(st, rows, T, pitch, scale, S, P, bwd);
+    case 3: return rows_launch_c<3>(st, rows, T, pitch, scale, S, P, bwd);
+    case 4: return rows_launch_c<4>(st, rows, T, pitch, scale, S, P, bwd);
+    case 5: case 6: return rows_launch_c<6>(st, rows, T, pitch, scale, S, P, bwd);
+    case 7: case 8: return rows_launch_c<8>(st, rows, T, pitch, scale, S, P, bwd);
+    default: break;
   }
+  const int blocks = (int)((rows + kRowWarps - 1) / kRowWarps);
+  if (!bwd)
+    k_softmax_causal_long<<<blocks, 256, 0, st>>>(S, rows, T, pitch, scale);
+  else
+    k_softmax_causal_bwd_long<<<blocks, 256, 0, st>>>(P, S, rows, T, pitch, scale);
   TURT_LAUNCH_CHECK();
   return OK;
 }

@@ -48,190 +48,276 @@ __global__ void k_embed_bwd(const float* __restrict__ dx, const uint32_t* __rest
 }
 
 // ------------------------------------------------------------------ norms
-// One warp per row; E/32 values per lane kept in registers (E <= 32*MAXV).
-constexpr int MAXV = 32;  // E <= 1024
+// One warp per row.  Lane `lane` owns the float4 chunks lane + 32j (j < NJ = ceil(E/128)) of
+// the row, so every load and store is a coalesced 16-byte access.  E is a multiple of 32 and at
+// most 1024 (NJ <= 8).
+constexpr int MAXV = 32;  // E <= 32 * MAXV
+constexpr int kNormWarps = 8;
+
+__device__ __forceinline__ float4 ld4(const float* p, int i) { return reinterpret_cast<const float4*>(p)[i]; }
+__device__ __forceinline__ void st4(float* p, int i, float4 v) { reinterpret_cast<float4*>(p)[i] = v; }
+__device__ __forceinline__ float dot4(float4 a, float4 b) { return a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w; }
 
 // RMSNorm forward: y = x * rs * g, rs = (mean(x^2) + eps)^-1/2 (autograd.ts:315-330).
-__global__ void k_rms_fwd(const float* __restrict__ x, const float* __restrict__ g, float* __restrict__ y,
-                          float* __restrict__ rstd, int rows, int E, float eps) {
-  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
+template <int NJ>
+__global__ void __launch_bounds__(256) k_rms_fwd(const float* __restrict__ x, const float* __restrict__ g,
+                                                 float* __restrict__ y, float* __restrict__ rstd, int rows, int E,
+                                                 float eps) {
+  const int row = blockIdx.x * kNormWarps + threadIdx.x / 32, lane = threadIdx.x & 31;
   if (row >= rows) return;
+  const int n4 = E / 4;
   const float* xr = x + (size_t)row * E;
-  float v[MAXV];
+  float4 v[NJ];
   float ss = 0.f;
-  const int nv = E / 32;
 #pragma unroll
-  for (int k = 0; k < MAXV; k++)
-    if (k < nv) {
-      v[k] = xr[k * 32 + lane];
-      ss += v[k] * v[k];
-    }
+  for (int j = 0; j < NJ; j++) {
+    const int i = lane + 32 * j;
+    v[j] = i < n4 ? ld4(xr, i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    ss += dot4(v[j], v[j]);
+  }
   ss = warp_sum(ss);
   const float rs = rsqrtf(ss / E + eps);
   if (lane == 0) rstd[row] = rs;
   float* yr = y + (size_t)row * E;
 #pragma unroll
-  for (int k = 0; k < MAXV; k++)
-    if (k < nv) yr[k * 32 + lane] = v[k] * rs * g[k * 32 + lane];
+  for (int j = 0; j < NJ; j++) {
+    const int i = lane + 32 * j;
+    if (i < n4) {
+      const float4 gg = ld4(g, i);
+      st4(yr, i, make_float4(v[j].x * rs * gg.x, v[j].y * rs * gg.y, v[j].z * rs * gg.z, v[j].w * rs * gg.w));
+    }
+  }
+}
+
+// Block partial of a per-column sum: the 8 warps' register partials (lane chunks) are combined
+// in shared memory in fixed order and written as row blockIdx.x of part[gridDim.x][E].
+template <int NJ>
+__device__ __forceinline__ void block_partial(const float4 (&acc)[NJ], float* sm, float* __restrict__ part, int E) {
+  const int w = threadIdx.x / 32, lane = threadIdx.x & 31, n4 = E / 4;
+#pragma unroll
+  for (int j = 0; j < NJ; j++) {
+    const int i = lane + 32 * j;
+    if (i < n4) st4(sm + (size_t)w * E, i, acc[j]);
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < E; c += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int q = 0; q < kNormWarps; q++) t += sm[q * E + c];
+    part[(size_t)blockIdx.x * E + c] = t;
+  }
 }
 
 // RMSNorm backward with the residual gradient fused in:
 //   dx = dres + rs*g*dy - (rs^3/E) * (sum_j dy_j g_j x_j) * x      (RMS_DX, autograd.ts:331-351)
 // and per-block partial dgamma = sum_rows dy * x * rs              (RMS_DG, :352-365).
-// dx may alias dres.  Block = 8 warps, ROWS_PER_BLOCK rows.
-constexpr int NORM_ROWS = 16;  // rows per block: 8192 rows -> 512 blocks (~3.5 per SM)
-__global__ void k_rms_bwd(const float* __restrict__ x, const float* __restrict__ dy, const float* __restrict__ g,
-                          const float* __restrict__ rstd, const float* dres, float* dx, float* __restrict__ dg_part,
-                          int rows, int E) {
-  __shared__ float acc[8][MAXV * 32];
-  const int w = threadIdx.x / 32, lane = threadIdx.x & 31;
-  const int nv = E / 32;
-  float dgl[MAXV];
+// dx may alias dres.  Rows are dealt to warps grid-stride, two rows per iteration so that each
+// warp keeps 6*NJ independent 16-byte loads in flight.
+template <int NJ>
+__global__ void __launch_bounds__(256) k_rms_bwd(const float* __restrict__ x, const float* __restrict__ dy,
+                                                 const float* __restrict__ g, const float* __restrict__ rstd,
+                                                 const float* dres, float* dx, float* __restrict__ dg_part, int rows,
+                                                 int E) {
+  extern __shared__ float sm[];
+  const int lane = threadIdx.x & 31, n4 = E / 4;
+  const int stride = gridDim.x * kNormWarps;
+  float4 gv[NJ], dgl[NJ];
 #pragma unroll
-  for (int k = 0; k < MAXV; k++) dgl[k] = 0.f;
-  const int r0 = blockIdx.x * NORM_ROWS;
-  for (int r = r0 + w; r < min(rows, r0 + NORM_ROWS); r += 8) {
-    const float* xr = x + (size_t)r * E;
-    const float* dyr = dy + (size_t)r * E;
-    const float rs = rstd[r];
-    float xv[MAXV], dv[MAXV];
-    float s = 0.f;
-#pragma unroll
-    for (int k = 0; k < MAXV; k++)
-      if (k < nv) {
-        xv[k] = xr[k * 32 + lane];
-        dv[k] = dyr[k * 32 + lane];
-        s += dv[k] * g[k * 32 + lane] * xv[k];
-        dgl[k] += dv[k] * xv[k] * rs;
-      }
-    s = warp_sum(s);
-    const float kf = rs * rs * rs * s / E;
-    const float* dr = dres ? dres + (size_t)r * E : nullptr;
-    float* dxr = dx + (size_t)r * E;
-#pragma unroll
-    for (int k = 0; k < MAXV; k++)
-      if (k < nv) {
-        float o = rs * dv[k] * g[k * 32 + lane] - kf * xv[k];
-        if (dr) o += dr[k * 32 + lane];
-        dxr[k * 32 + lane] = o;
-      }
+  for (int j = 0; j < NJ; j++) {
+    const int i = lane + 32 * j;
+    gv[j] = i < n4 ? ld4(g, i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    dgl[j] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
+  for (int r0 = blockIdx.x * kNormWarps + threadIdx.x / 32; r0 < rows; r0 += 2 * stride) {
+    const int rr[2] = {r0, r0 + stride};
+    float4 xv[2][NJ], dv[2][NJ];
+    float s[2] = {0.f, 0.f}, rs[2];
 #pragma unroll
-  for (int k = 0; k < MAXV; k++)
-    if (k < nv) acc[w][k * 32 + lane] = dgl[k];
-  __syncthreads();
-  for (int c = threadIdx.x; c < E; c += blockDim.x) {
-    float s = 0.f;
+    for (int q = 0; q < 2; q++) {
+      const bool ok = rr[q] < rows;
+      rs[q] = ok ? rstd[rr[q]] : 0.f;
 #pragma unroll
-    for (int q = 0; q < 8; q++) s += acc[q][c];
-    dg_part[(size_t)blockIdx.x * E + c] = s;
+      for (int j = 0; j < NJ; j++) {
+        const int i = lane + 32 * j;
+        const bool in = ok && i < n4;
+        xv[q][j] = in ? ld4(x + (size_t)rr[q] * E, i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        dv[q][j] = in ? ld4(dy + (size_t)rr[q] * E, i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 2; q++)
+#pragma unroll
+      for (int j = 0; j < NJ; j++) {
+        const float4 a = xv[q][j], d = dv[q][j], gg = gv[j];
+        s[q] += d.x * gg.x * a.x + d.y * gg.y * a.y + d.z * gg.z * a.z + d.w * gg.w * a.w;
+        dgl[j].x += d.x * a.x * rs[q];
+        dgl[j].y += d.y * a.y * rs[q];
+        dgl[j].z += d.z * a.z * rs[q];
+        dgl[j].w += d.w * a.w * rs[q];
+      }
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+      if (rr[q] >= rows) continue;  // warp-uniform
+      const float sum = warp_sum(s[q]);
+      const float kf = rs[q] * rs[q] * rs[q] * sum / E;
+      const float* dr = dres ? dres + (size_t)rr[q] * E : nullptr;
+      float* dxr = dx + (size_t)rr[q] * E;
+#pragma unroll
+      for (int j = 0; j < NJ; j++) {
+        const int i = lane + 32 * j;
+        if (i >= n4) continue;
+        const float4 a = xv[q][j], d = dv[q][j], gg = gv[j];
+        float4 o = make_float4(rs[q] * d.x * gg.x - kf * a.x, rs[q] * d.y * gg.y - kf * a.y,
+                               rs[q] * d.z * gg.z - kf * a.z, rs[q] * d.w * gg.w - kf * a.w);
+        if (dr) {
+          const float4 t = ld4(dr, i);
+          o.x += t.x;
+          o.y += t.y;
+          o.z += t.z;
+          o.w += t.w;
+        }
+        st4(dxr, i, o);
+      }
+    }
   }
+  block_partial<NJ>(dgl, sm, dg_part, E);
 }
 
 // LayerNorm forward (biased variance), autograd.ts:256-274.
-__global__ void k_ln_fwd(const float* __restrict__ x, const float* __restrict__ g, const float* __restrict__ b,
-                         float* __restrict__ y, float* __restrict__ mean, float* __restrict__ rstd, int rows, int E,
-                         float eps) {
-  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
+template <int NJ>
+__global__ void __launch_bounds__(256) k_ln_fwd(const float* __restrict__ x, const float* __restrict__ g,
+                                                const float* __restrict__ b, float* __restrict__ y,
+                                                float* __restrict__ mean, float* __restrict__ rstd, int rows, int E,
+                                                float eps) {
+  const int row = blockIdx.x * kNormWarps + threadIdx.x / 32, lane = threadIdx.x & 31;
   if (row >= rows) return;
+  const int n4 = E / 4;
   const float* xr = x + (size_t)row * E;
-  const int nv = E / 32;
-  float v[MAXV];
+  float4 v[NJ];
   float s = 0.f;
 #pragma unroll
-  for (int k = 0; k < MAXV; k++)
-    if (k < nv) {
-      v[k] = xr[k * 32 + lane];
-      s += v[k];
-    }
+  for (int j = 0; j < NJ; j++) {
+    const int i = lane + 32 * j;
+    v[j] = i < n4 ? ld4(xr, i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    s += v[j].x + v[j].y + v[j].z + v[j].w;
+  }
   const float mu = warp_sum(s) / E;
-  float q = 0.f;
+  float qv = 0.f;
 #pragma unroll
-  for (int k = 0; k < MAXV; k++)
-    if (k < nv) q += (v[k] - mu) * (v[k] - mu);
-  const float rs = rsqrtf(warp_sum(q) / E + eps);
+  for (int j = 0; j < NJ; j++) {
+    const int i = lane + 32 * j;
+    if (i < n4) {
+      const float4 d = make_float4(v[j].x - mu, v[j].y - mu, v[j].z - mu, v[j].w - mu);
+      qv += dot4(d, d);
+    }
+  }
+  const float rs = rsqrtf(warp_sum(qv) / E + eps);
   if (lane == 0) {
     mean[row] = mu;
     rstd[row] = rs;
   }
   float* yr = y + (size_t)row * E;
 #pragma unroll
-  for (int k = 0; k < MAXV; k++)
-    if (k < nv) yr[k * 32 + lane] = (v[k] - mu) * rs * g[k * 32 + lane] + b[k * 32 + lane];
+  for (int j = 0; j < NJ; j++) {
+    const int i = lane + 32 * j;
+    if (i < n4) {
+      const float4 gg = ld4(g, i), bb = ld4(b, i);
+      st4(yr, i,
+          make_float4((v[j].x - mu) * rs * gg.x + bb.x, (v[j].y - mu) * rs * gg.y + bb.y,
+                      (v[j].z - mu) * rs * gg.z + bb.z, (v[j].w - mu) * rs * gg.w + bb.w));
+    }
+  }
 }
 
-// LayerNorm backward (LN_DX + LN_DGB, autograd.ts:275-308) with the residual gradient fused.
-__global__ void k_ln_bwd(const float* __restrict__ x, const float* __restrict__ dy, const float* __restrict__ g,
-                         const float* __restrict__ mean, const float* __restrict__ rstd, const float* dres, float* dx,
-                         float* __restrict__ dg_part, float* __restrict__ db_part, int rows, int E) {
-  __shared__ float accg[8][MAXV * 32];
-  const int w = threadIdx.x / 32, lane = threadIdx.x & 31;
-  const int nv = E / 32;
-  float dgl[MAXV], dbl[MAXV];
+// LayerNorm backward (LN_DX + LN_DGB, autograd.ts:275-308) with the residual gradient fused;
+// partial dgamma / dbeta per block.  One row per warp iteration, grid-stride.
+template <int NJ>
+__global__ void __launch_bounds__(256) k_ln_bwd(const float* __restrict__ x, const float* __restrict__ dy,
+                                                const float* __restrict__ g, const float* __restrict__ mean,
+                                                const float* __restrict__ rstd, const float* dres, float* dx,
+                                                float* __restrict__ dg_part, float* __restrict__ db_part, int rows,
+                                                int E) {
+  extern __shared__ float sm[];
+  const int lane = threadIdx.x & 31, n4 = E / 4;
+  const int stride = gridDim.x * kNormWarps;
+  float4 gv[NJ], dgl[NJ], dbl[NJ];
 #pragma unroll
-  for (int k = 0; k < MAXV; k++) dgl[k] = dbl[k] = 0.f;
-  const int r0 = blockIdx.x * NORM_ROWS;
-  for (int r = r0 + w; r < min(rows, r0 + NORM_ROWS); r += 8) {
-    const float* xr = x + (size_t)r * E;
-    const float* dyr = dy + (size_t)r * E;
+  for (int j = 0; j < NJ; j++) {
+    const int i = lane + 32 * j;
+    gv[j] = i < n4 ? ld4(g, i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    dgl[j] = dbl[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int r = blockIdx.x * kNormWarps + threadIdx.x / 32; r < rows; r += stride) {
     const float mu = mean[r], rs = rstd[r];
-    float xh[MAXV], dv[MAXV];
+    float4 xh[NJ], dv[NJ];
     float sdy = 0.f, sdyx = 0.f;
 #pragma unroll
-    for (int k = 0; k < MAXV; k++)
-      if (k < nv) {
-        xh[k] = (xr[k * 32 + lane] - mu) * rs;
-        const float gy = dyr[k * 32 + lane];
-        dgl[k] += gy * xh[k];
-        dbl[k] += gy;
-        dv[k] = gy * g[k * 32 + lane];
-        sdy += dv[k];
-        sdyx += dv[k] * xh[k];
+    for (int j = 0; j < NJ; j++) {
+      const int i = lane + 32 * j;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), gy = a;
+      if (i < n4) {
+        a = ld4(x + (size_t)r * E, i);
+        gy = ld4(dy + (size_t)r * E, i);
       }
+      xh[j] = make_float4((a.x - mu) * rs, (a.y - mu) * rs, (a.z - mu) * rs, (a.w - mu) * rs);
+      if (i >= n4) xh[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      dgl[j].x += gy.x * xh[j].x;
+      dgl[j].y += gy.y * xh[j].y;
+      dgl[j].z += gy.z * xh[j].z;
+      dgl[j].w += gy.w * xh[j].w;
+      dbl[j].x += gy.x;
+      dbl[j].y += gy.y;
+      dbl[j].z += gy.z;
+      dbl[j].w += gy.w;
+      dv[j] = make_float4(gy.x * gv[j].x, gy.y * gv[j].y, gy.z * gv[j].z, gy.w * gv[j].w);
+      sdy += dv[j].x + dv[j].y + dv[j].z + dv[j].w;
+      sdyx += dot4(dv[j], xh[j]);
+    }
     sdy = warp_sum(sdy) / E;
     sdyx = warp_sum(sdyx) / E;
     const float* dr = dres ? dres + (size_t)r * E : nullptr;
     float* dxr = dx + (size_t)r * E;
 #pragma unroll
-    for (int k = 0; k < MAXV; k++)
-      if (k < nv) {
-        float o = rs * (dv[k] - sdy - xh[k] * sdyx);
-        if (dr) o += dr[k * 32 + lane];
-        dxr[k * 32 + lane] = o;
+    for (int j = 0; j < NJ; j++) {
+      const int i = lane + 32 * j;
+      if (i >= n4) continue;
+      float4 o = make_float4(rs * (dv[j].x - sdy - xh[j].x * sdyx), rs * (dv[j].y - sdy - xh[j].y * sdyx),
+                             rs * (dv[j].z - sdy - xh[j].z * sdyx), rs * (dv[j].w - sdy - xh[j].w * sdyx));
+      if (dr) {
+        const float4 t = ld4(dr, i);
+        o.x += t.x;
+        o.y += t.y;
+        o.z += t.z;
+        o.w += t.w;
       }
+      st4(dxr, i, o);
+    }
   }
-#pragma unroll
-  for (int k = 0; k < MAXV; k++)
-    if (k < nv) accg[w][k * 32 + lane] = dgl[k];
+  block_partial<NJ>(dgl, sm, dg_part, E);
   __syncthreads();
-  for (int c = threadIdx.x; c < E; c += blockDim.x) {
-    float s = 0.f;
-#pragma unroll
-    for (int q = 0; q < 8; q++) s += accg[q][c];
-    dg_part[(size_t)blockIdx.x * E + c] = s;
-  }
-  __syncthreads();
-#pragma unroll
-  for (int k = 0; k < MAXV; k++)
-    if (k < nv) accg[w][k * 32 + lane] = dbl[k];
-  __syncthreads();
-  for (int c = threadIdx.x; c < E; c += blockDim.x) {
-    float s = 0.f;
-#pragma unroll
-    for (int q = 0; q < 8; q++) s += accg[q][c];
-    db_part[(size_t)blockIdx.x * E + c] = s;
-  }
+  block_partial<NJ>(dbl, sm, db_part, E);
 }
 
 // out[c] += sum_b part[b][c] (fixed order: deterministic).  One block per 32 columns; warp w
-// sums partial rows w, w+8, ... with coalesced 128-byte loads, then the 8 warp sums combine.
+// sums partial rows w, w+8, ... (coalesced 128-byte rows, four loads in flight), then the 8
+// warp sums combine in order.
 __global__ void k_reduce_parts(const float* __restrict__ part, int nparts, int C, float* __restrict__ out) {
   __shared__ float red[8][33];
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = blockIdx.x * 32 + lane;
   float s = 0.f;
-  if (c < C)
-    for (int b = w; b < nparts; b += 8) s += part[(size_t)b * C + c];
+  if (c < C) {
+    int b = w;
+    for (; b + 24 < nparts; b += 32) {
+      const float a0 = part[(size_t)b * C + c], a1 = part[(size_t)(b + 8) * C + c];
+      const float a2 = part[(size_t)(b + 16) * C + c], a3 = part[(size_t)(b + 24) * C + c];
+      s += a0;
+      s += a1;
+      s += a2;
+      s += a3;
+    }
+    for (; b < nparts; b += 8) s += part[(size_t)b * C + c];
+  }
   red[w][lane] = s;
   __syncthreads();
   if (w == 0 && c < C) {
@@ -242,13 +328,13 @@ __global__ void k_reduce_parts(const float* __restrict__ part, int nparts, int C
   }
 }
 
-// Column sums of g[rows][C] into partials (bias gradients; SEGSUM, autograd.ts:122-135).
+// Column sums of g[rows][C] into partials (bias gradients; SEGSUM, autograd.ts:122-135):
+// partial row p sums rows p, p + P, p + 2P, ... (P = gridDim.y).
 __global__ void k_colsum_parts(const float* __restrict__ g, int rows, int C, float* __restrict__ part) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
-  const int r0 = blockIdx.y * NORM_ROWS;
   float s = 0.f;
-  for (int r = r0; r < min(rows, r0 + NORM_ROWS); r++) s += g[(size_t)r * C + c];
+  for (int r = blockIdx.y; r < rows; r += gridDim.y) s += g[(size_t)r * C + c];
   part[(size_t)blockIdx.y * C + c] = s;
 }
 
@@ -537,18 +623,52 @@ int embed_bwd(cudaStream_t st, const float* dx, const uint32_t* ids, float* dwte
   TURT_LAUNCH_CHECK();
   return OK;
 }
+namespace {
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+// Dispatch on NJ = ceil(E / 128) float4 chunks per lane.
+#define TURT_NJ_SWITCH(E, CALL) \
+  switch (((E) + 127) / 128) {  \
+    case 1: CALL(1); break;     \
+    case 2: CALL(2); break;     \
+    case 3: CALL(3); break;     \
+    case 4: CALL(4); break;     \
+    case 5: CALL(5); break;     \
+    case 6: CALL(6); break;     \
+    case 7: CALL(7); break;     \
+    default: CALL(8); break;    \
+  }
+}  // namespace
+
 int rms_fwd(cudaStream_t st, const float* x, const float* g, float* y, float* rstd, int rows, int E, float eps) {
   TURT_REQUIRE(E % 32 == 0 && E <= 32 * MAXV, "norm width must be a multiple of 32, at most 1024");
-  k_rms_fwd<<<ceil_div(rows, 8), 256, 0, st>>>(x, g, y, rstd, rows, E, eps);
+#define CALL(NJ) k_rms_fwd<NJ><<<ceil_div(rows, kNormWarps), 256, 0, st>>>(x, g, y, rstd, rows, E, eps)
+  TURT_NJ_SWITCH(E, CALL)
+#undef CALL
   TURT_LAUNCH_CHECK();
   return OK;
 }
-int norm_parts(int rows) { return ceil_div(rows, NORM_ROWS); }
+// Partial-sum rows a norm backward writes: one per block, at most one block per SM.
+int norm_parts(int rows) {
+  const int b = ceil_div(rows, kNormWarps);
+  return b < sm_count() ? b : sm_count();
+}
 int rms_bwd(cudaStream_t st, const float* x, const float* dy, const float* g, const float* rstd, const float* dres,
             float* dx, float* dg_accum, float* part, int rows, int E) {
   TURT_REQUIRE(E % 32 == 0 && E <= 32 * MAXV, "norm width must be a multiple of 32, at most 1024");
   const int nb = norm_parts(rows);
-  k_rms_bwd<<<nb, 256, 0, st>>>(x, dy, g, rstd, dres, dx, part, rows, E);
+  const size_t smem = (size_t)kNormWarps * E * 4;
+#define CALL(NJ) k_rms_bwd<NJ><<<nb, 256, smem, st>>>(x, dy, g, rstd, dres, dx, part, rows, E)
+  TURT_NJ_SWITCH(E, CALL)
+#undef CALL
   TURT_LAUNCH_CHECK();
   k_reduce_parts<<<ceil_div(E, 32), 256, 0, st>>>(part, nb, E, dg_accum);
   TURT_LAUNCH_CHECK();
@@ -557,7 +677,9 @@ int rms_bwd(cudaStream_t st, const float* x, const float* dy, const float* g, co
 int ln_fwd(cudaStream_t st, const float* x, const float* g, const float* b, float* y, float* mean, float* rstd, int rows,
            int E, float eps) {
   TURT_REQUIRE(E % 32 == 0 && E <= 32 * MAXV, "norm width must be a multiple of 32, at most 1024");
-  k_ln_fwd<<<ceil_div(rows, 8), 256, 0, st>>>(x, g, b, y, mean, rstd, rows, E, eps);
+#define CALL(NJ) k_ln_fwd<NJ><<<ceil_div(rows, kNormWarps), 256, 0, st>>>(x, g, b, y, mean, rstd, rows, E, eps)
+  TURT_NJ_SWITCH(E, CALL)
+#undef CALL
   TURT_LAUNCH_CHECK();
   return OK;
 }
@@ -565,7 +687,11 @@ int ln_bwd(cudaStream_t st, const float* x, const float* dy, const float* g, con
            const float* dres, float* dx, float* dg_accum, float* db_accum, float* part, int rows, int E) {
   TURT_REQUIRE(E % 32 == 0 && E <= 32 * MAXV, "norm width must be a multiple of 32, at most 1024");
   const int nb = norm_parts(rows);
-  k_ln_bwd<<<nb, 256, 0, st>>>(x, dy, g, mean, rstd, dres, dx, part, part + (size_t)nb * E, rows, E);
+  const size_t smem = (size_t)kNormWarps * E * 4;
+#define CALL(NJ) \
+  k_ln_bwd<NJ><<<nb, 256, smem, st>>>(x, dy, g, mean, rstd, dres, dx, part, part + (size_t)nb * E, rows, E)
+  TURT_NJ_SWITCH(E, CALL)
+#undef CALL
   TURT_LAUNCH_CHECK();
   k_reduce_parts<<<ceil_div(E, 32), 256, 0, st>>>(part, nb, E, dg_accum);
   TURT_LAUNCH_CHECK();
