@@ -332,9 +332,11 @@ def run_gpu(args, w, rank: int, world: int, local_rank: int) -> None:
                        "last_loss": last_loss},
             "roofline": {"bound": "tensor", "kernel": "k_gemm_tf32 (head projection %dx%dx%d)" % (N_tok, V, E),
                          "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s", "frac": achieved / tf32_peak,
-                         "traffic": None, "peak_source": f"{peaks['source']} bf16 dense / 2",
+                         "traffic": read_profile_traffic("gemm_pair_head_fwd_8192x8192x384.md"),
+                         "peak_source": f"{peaks['source']} bf16 dense / 2",
                          "launch_ms": gemm_ms,
-                         "mma_issue_factor": 3 if args.precision == 3 else 1},
+                         "mma_issue_factor": 3 if args.precision == 3 else 1,
+                         "frac_of_precision_peak": achieved * (3 if args.precision == 3 else 1) / tf32_peak},
             "step_roofline": {"flops_per_token": f_tok, "achieved_tflops_per_gpu": step_tflops,
                               "peak_tflops": tf32_peak_sust, "frac": step_tflops / tf32_peak_sust,
                               "peak_source": f"{peaks['source']} bf16 sustained / 2"},
@@ -360,13 +362,224 @@ def run_gpu(args, w, rank: int, world: int, local_rank: int) -> None:
         print(json.dumps(out), flush=True)
 
 
+# ----------------------------------------------------------------------------- backward-op workload
+OP_ROWS = 8192
+
+
+def op_bytes():
+    """Algorithmic HBM bytes of the standalone backward kernels (each element read or written once)."""
+    N, E, h, V, n_adam = OP_ROWS, 384, 1024, 8192, 10_000_000
+    return {
+        "rms_bwd [8192,384]": 3 * N * E * 4 + 4 * N + 8 * E,
+        "swiglu_bwd [8192,1024]": 5 * N * h * 4,
+        "softmax_ce_grad [8192,8192]": 2 * N * V * 4 + 2 * N * 4,
+        "adamw_clip 10M": 8 * n_adam * 4,
+    }
+
+
+def read_profile_traffic(name: str, key: str = "traffic_bytes_per_launch"):
+    """Per-launch DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) recorded by an ncu
+    capture summarised under profiles/ (a line `<key>: N`), or None."""
+    import re
+    path = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(path):
+        return None
+    m = re.search(re.escape(key) + r":\s*([0-9]+)", open(path).read())
+    return int(m.group(1)) if m else None
+
+
+def run_backward_ops(args, rank: int) -> None:
+    """Standalone timing of the train step's fused memory-bound backward kernels on seeded
+    N(0, 1) inputs with 8192 rows; each launch timed alone with CUDA events after an L2 flush."""
+    if rank != 0:
+        return
+    import ctypes as C
+
+    import numpy as np
+    import torch
+
+    from turt_b200._lib import check, lib
+    from turt_b200.runtime import Context
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx = Context(0)
+    ctx.set_stream(stream.cuda_stream)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    dev = "cuda"
+
+    def randn(*shape):
+        return torch.randn(*shape, generator=g, device=dev, dtype=torch.float32)
+
+    N, E, h, V, n_adam = OP_ROWS, 384, 1024, 8192, 10_000_000
+    x, dy, gam = randn(N, E), randn(N, E), randn(E)
+    rstd = torch.rsqrt((x * x).mean(dim=1) + 1e-5)
+    dx, dg = torch.empty_like(x), torch.zeros(E, device=dev)
+    ga, up, dact = randn(N, h), randn(N, h), randn(N, h)
+    dga, dup = torch.empty_like(ga), torch.empty_like(up)
+    logits = randn(N, V)
+    tgt = torch.randint(0, V, (N,), generator=g, device=dev, dtype=torch.int32)
+    loss_rows = torch.empty(N, device=dev)
+    p, gr, m = randn(n_adam), randn(n_adam), randn(n_adam)
+    v = randn(n_adam).abs()
+    flush = torch.empty(64 * 1024 * 1024, device=dev)  # 256 MB > L2
+    flush_rd = torch.ones(64 * 1024 * 1024, device=dev)
+    P = lambda t: t.data_ptr()
+    h_ = ctx.handle
+    calls = {
+        "rms_bwd [8192,384]": lambda: check(lib().turt_fused_rms_bwd(h_, P(x), P(dy), P(gam), P(rstd), None, P(dx),
+                                                                     P(dg), N, E)),
+        "swiglu_bwd [8192,1024]": lambda: check(lib().turt_fused_swiglu_bwd(h_, P(ga), P(up), P(dact), P(dga), P(dup),
+                                                                            N * h)),
+        "softmax_ce_grad [8192,8192]": lambda: check(lib().turt_fused_ce(h_, P(logits), P(tgt), P(loss_rows), N, V,
+                                                                          1.0 / N)),
+        "adamw_clip 10M": lambda: check(lib().turt_fused_adamw_clip(h_, P(p), P(gr), P(m), P(v), n_adam, 3e-4, 0.9,
+                                                                    0.95, 1e-8, 0.1, 0.1, 0.0975, 1.0, None)),
+    }
+    nbytes = op_bytes()
+    peaks = measured_peaks()
+    kernels = {}
+    launches0 = Context.launch_count()
+    with ClockSampler(0) as clk:
+        for name, fn in calls.items():
+            for _ in range(args.warmup):
+                fn()
+            times = []
+            for _ in range(args.steps):
+                flush.fill_(1.0)  # evict: 256 MB of writes
+                flush_rd.sum()    # ... then 256 MB of reads, so no dirty line is written back inside the launch
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                fn()
+                e1.record(stream)
+                e1.synchronize()
+                times.append(e0.elapsed_time(e1))
+            ms = statistics.median(times)
+            gbs = nbytes[name] / (ms / 1000.0) / 1e9
+            kernels[name] = {"ms": ms, "bytes": nbytes[name], "gbs": gbs, "frac": gbs / peaks["hbm_gbs"]}
+    launches = Context.launch_count() - launches0
+    total_ms = sum(k["ms"] for k in kernels.values())
+    total_bytes = sum(nbytes.values())
+    value = total_bytes / (total_ms / 1000.0) / 1e9
+    top = "softmax_ce_grad [8192,8192]"
+    out = {
+        "metric": "standalone backward-op kernels: algorithmic HBM bytes / time", "value": value, "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "backward-ops", "rows": N, "inputs": "seeded N(0,1), uniform int targets",
+                   "l2": "flushed before every timed launch (256 MB write, then 256 MB read of another buffer); "
+                         "ms = median launch"},
+        "kernels": kernels,
+        "roofline": {"bound": "hbm", "kernel": "k_ce_fused " + top, "achieved": kernels[top]["gbs"],
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": kernels[top]["frac"],
+                     "traffic": read_profile_traffic("backward_ops_8192rows.md", "k_ce_fused_traffic_bytes_per_launch"),
+                     "peak_source": f"{peaks['source']} HBM copy"},
+        "gpu_launches": launches,
+        "clocks": clk.summary(),
+    }
+    ctx.close()
+    if not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_ops_baseline()
+    out["e2e"] = {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0,
+                  "note": "device-resident kernels: no host copies belong to this workload"}
+    print(json.dumps(out), flush=True)
+
+
+def run_gemm(args, rank: int) -> None:
+    """One tensor-core GEMM C[M,N] = A[M,K] B[N,K]^T (both K-major, the head-projection
+    layout) repeated: algorithmic 2MNK FLOPs over the median CUDA-event launch time."""
+    if rank != 0:
+        return
+    import torch
+
+    from turt_b200._lib import check, lib
+    from turt_b200.runtime import Context
+    M, N, K = (int(t) for t in args.gemm.split(","))
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx = Context(0)
+    ctx.set_stream(stream.cuda_stream)
+    ctx.set_precision(args.precision)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    a = torch.randn(M, K, generator=g, device="cuda")
+    b = torch.randn(N, K, generator=g, device="cuda")
+    c = torch.empty(M, N, device="cuda")
+    flush = torch.empty(64 * 1024 * 1024, device="cuda")
+    flush_rd = torch.ones(64 * 1024 * 1024, device="cuda")
+
+    def fn():
+        check(lib().turt_matmul_into(ctx.handle, a.data_ptr(), b.data_ptr(), c.data_ptr(), M, K, N, 1, 0, 1, 0))
+
+    for _ in range(args.warmup):
+        fn()
+    times = []
+    launches0 = Context.launch_count()
+    with ClockSampler(0) as clk:
+        for _ in range(args.steps):
+            flush.fill_(1.0)
+            flush_rd.sum()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+    launches = Context.launch_count() - launches0
+    ms = statistics.median(times)
+    peaks = measured_peaks()
+    tf32 = peaks["bf16_tflops"] / 2.0
+    achieved = 2.0 * M * N * K / (ms / 1000.0) / 1e12
+    issue = 3 if args.precision == 3 else 1
+    out = {"metric": "tensor-core GEMM throughput (algorithmic 2MNK FLOPs)", "value": achieved, "unit": "TFLOP/s",
+           "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "tf32x3" if issue == 3 else "tf32", "data": "synthetic",
+           "config": {"workload": "gemm", "M": M, "N": N, "K": K, "layout": "A [M,K], B [N,K], both K-major",
+                      "l2": "flushed before every timed launch (256 MB write, then 256 MB read of another "
+                            "buffer); ms = median launch"},
+           "roofline": {"bound": "tensor", "kernel": "k_gemm_tf32 / k_gemm_tf32_pair", "achieved": achieved,
+                        "peak": tf32, "unit": "TFLOP/s", "frac": achieved / tf32,
+                        "frac_of_precision_peak": achieved * issue / tf32, "mma_issue_factor": issue,
+                        "traffic": None, "peak_source": f"{peaks['source']} bf16 dense / 2"},
+           "e2e": {"value": achieved, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0,
+                   "note": "device-resident operands"},
+           "gpu_launches": launches, "clocks": clk.summary()}
+    ctx.close()
+    print(json.dumps(out), flush=True)
+
+
+def cpu_ops_baseline():
+    """The oracle's restatement of the same four ops (single thread) on 1/8 of each workload."""
+    import numpy as np
+
+    from oracle.oracle import Oracle
+    orc = Oracle()
+    rng = np.random.default_rng(7)
+    N, E, h, V, n = OP_ROWS // 8, 384, 1024, 8192, 10_000_000 // 8
+    x, dy = rng.standard_normal((N, E)).astype(np.float32), rng.standard_normal((N, E)).astype(np.float32)
+    gam = rng.standard_normal(E).astype(np.float32)
+    a, u, d = (rng.standard_normal(N * h).astype(np.float32) for _ in range(3))
+    logits = rng.standard_normal((N, V)).astype(np.float32)
+    tgt = rng.integers(0, V, N).astype(np.int32)
+    p, g, m = (rng.standard_normal(n).astype(np.float32) for _ in range(3))
+    v = np.abs(rng.standard_normal(n)).astype(np.float32)
+    t0 = time.perf_counter()
+    orc.rmsnorm(x, gam, dy)
+    orc.silu_bwd(a, d * u)
+    orc.cross_entropy(logits, tgt)
+    orc.clip(g, 1.0)
+    orc.adamw_bc(p, g, m, v, 3e-4, 0.9, 0.95, 1e-8, 0.1, 0.1, 0.0975)
+    secs = time.perf_counter() - t0
+    return {"value": sum(op_bytes().values()) / 8 / secs / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": "the four ops on 1/8 of each size (1024 rows, 1.25M AdamW elements), oracle C restatement"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="turt", choices=["turt", "reference"])
-    ap.add_argument("--workload", default="gpt-6L-384d", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="gpt-6L-384d", choices=sorted(WORKLOADS) + ["backward-ops", "gemm"])
+    ap.add_argument("--gemm", default="8192,8192,384", help="M,N,K of the gemm workload")
     ap.add_argument("--precision", type=int, default=3, choices=[1, 3])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -375,6 +588,27 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.workload == "gemm":
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the gemm workload is a kernel microbenchmark "
+                                  "with no reference counterpart"}), flush=True)
+            return
+        run_gemm(args, rank)
+        return
+    if args.workload == "backward-ops":
+        if args.impl == "reference":
+            if rank == 0:
+                line = cpu_ops_baseline()
+                print(json.dumps({"impl": "reference", "metric": "standalone backward-op kernels: algorithmic HBM "
+                                  "bytes / time", "value": line["value"], "unit": "GB/s", "n_gpus": args.gpus,
+                                  "steps": 1, "warmup": 0, "higher_is_better": True, "dtype": "f32",
+                                  "data": "synthetic", "config": {"workload": "backward-ops"}, "cpu_baseline": line,
+                                  "e2e": {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
+                                          "d2h_bytes_per_step": 0}}), flush=True)
+            return
+        run_backward_ops(args, rank)
+        return
     w = WORKLOADS[args.workload]
     if args.impl == "reference":
         run_reference(args, w, rank)

@@ -68,6 +68,25 @@ int turt_get_precision(turt_ctx* ctx, int* precision);
  * 16x16 workgroup tile. */
 int turt_gemm_set_tile(int bn, int pair);
 
+/* ------------------------------------------------------------------ fused kernels
+ * The memory-bound kernels of the fused train step, on raw device buffers, so that each can
+ * be validated and timed on its own (standalone backward-op workload).  No reference
+ * counterpart: the reference runs these as chains of GpuEngine ops (rmsDx + rmsDg; siluBwd +
+ * ewise; ceFwd + ceBwd; adamw per tensor after a CPU-side clip).
+ * turt_fused_rms_bwd: dx = dres + RMS_DX(x, dy, g, rstd) (dres may be NULL), dg += RMS_DG.
+ * turt_fused_swiglu_bwd: with s = sigmoid(a): dgate = dact*u*(s + a*s*(1-s)), dup = dact*a*s.
+ * turt_fused_ce: per-row CE loss of logits[N][V] and, in place, gscale*(softmax - onehot).
+ * turt_fused_adamw_clip: global-norm clip of g to `clip` (<= 0: none; norm_out, host, may be
+ * NULL) fused into one AdamW update of p, m, v (adam.ts:31-54 algebra, bias corrections given). */
+int turt_fused_rms_bwd(turt_ctx* ctx, const float* x, const float* dy, const float* g, const float* rstd,
+                       const float* dres, float* dx, float* dg, int rows, int E);
+int turt_fused_swiglu_bwd(turt_ctx* ctx, const float* gate, const float* up, const float* dact, float* dgate,
+                          float* dup, size_t n);
+int turt_fused_ce(turt_ctx* ctx, float* logits, const uint32_t* targets, float* loss_rows, int N, int V,
+                  float gscale);
+int turt_fused_adamw_clip(turt_ctx* ctx, float* p, const float* g, float* m, float* v, size_t n, float lr, float b1,
+                          float b2, float eps, float wd, float bc1, float bc2, float clip, double* norm_out);
+
 /* ------------------------------------------------------------------ buffers
  * GpuEngine.buffer / free / reclaim / read / fill / tensor / indexBuffer,
  * src/infer/webgpu/autograd.ts:589-595, 641-662, 701-709, 790-814.  Buffers are

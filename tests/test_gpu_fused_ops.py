@@ -1,0 +1,126 @@
+"""The train step's fused memory-bound kernels, standalone (turt_fused_*), against the oracle.
+
+RMSNorm backward (RMS_DX + RMS_DG, autograd.ts:331-365, with the residual gradient added),
+SwiGLU backward (SILU_BWD and the gate*up product rule), fused softmax cross-entropy
+(CE_FWD + CE_BWD, autograd.ts:441-471) and AdamW with global-norm clipping (adam.ts:31-54,
+clip.ts:7-24).  The kernels compute in fp32; the oracle, like the reference's JavaScript, in
+doubles.  Two bounds: max|got - ref| / max|ref| <= 1e-5 (fp32 rounding of the tensor's scale)
+and the reference validator's maxRelErr (denominator max(1e-3, |a|, |b|)) <= 1e-3, which is
+what fp32 rounding of O(1) terms leaves on entries that cancel to ~1e-3 (an fp32 emulation of
+AdamW's m update gives 1e-4 there); the model's gradient bar is 2e-3.
+"""
+import numpy as np
+import pytest
+
+from oracle.oracle import Oracle, max_rel_err
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3     # maxRelErr
+NORM_TOL = 1e-5
+
+
+def _ok(got, ref):
+    got, ref = np.asarray(got, np.float64), np.asarray(ref, np.float64)
+    norm = float(np.max(np.abs(got - ref)) / max(1e-30, np.max(np.abs(ref))))
+    return max_rel_err(got, ref) < TOL and norm < NORM_TOL
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    from turt_b200.runtime import Context
+    c = Context(0)
+    yield c
+    c.close()
+
+
+@pytest.fixture(scope="module")
+def orc():
+    return Oracle()
+
+
+def _dev(ctx, a):
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    p = ctx.buffer(a.size)
+    ctx.upload(p, a)
+    return p
+
+
+@pytest.mark.parametrize("rows,E", [(1024, 384), (100, 32), (37, 768)])
+@pytest.mark.parametrize("with_res", [False, True])
+def test_rms_bwd(ctx, orc, rows, E, with_res):
+    from turt_b200._lib import check, lib
+    rng = np.random.default_rng(rows + E)
+    x = rng.standard_normal((rows, E)).astype(np.float32)
+    gam = (1 + 0.1 * rng.standard_normal(E)).astype(np.float32)
+    dy = rng.standard_normal((rows, E)).astype(np.float32)
+    dres = rng.standard_normal((rows, E)).astype(np.float32) if with_res else None
+    rstd = (1.0 / np.sqrt((x.astype(np.float64) ** 2).mean(axis=1) + 1e-5)).astype(np.float32)
+    _, ref_dx, ref_dg = orc.rmsnorm(x, gam, dy)
+    if with_res:
+        ref_dx = ref_dx + dres
+    dg0 = rng.standard_normal(E).astype(np.float32)  # dg accumulates
+    bufs = [_dev(ctx, a) for a in (x, dy, gam, rstd, dg0)]
+    dx = ctx.buffer(rows * E)
+    dr = _dev(ctx, dres) if with_res else None
+    check(lib().turt_fused_rms_bwd(ctx.handle, bufs[0], bufs[1], bufs[2], bufs[3], dr, dx, bufs[4], rows, E))
+    got_dx = ctx.download(dx, rows * E).reshape(rows, E)
+    got_dg = ctx.download(bufs[4], E)
+    assert _ok(got_dx, ref_dx)
+    assert _ok(got_dg, ref_dg + dg0)
+
+
+@pytest.mark.parametrize("n", [8192 * 1024 // 64, 1003])
+def test_swiglu_bwd(ctx, orc, n):
+    from turt_b200._lib import check, lib
+    rng = np.random.default_rng(n)
+    a, u, d = (rng.standard_normal(n).astype(np.float32) for _ in range(3))
+    ref_du = d * orc.silu(a)
+    ref_da = orc.silu_bwd(a, d * u)
+    pa, pu, pd = (_dev(ctx, t) for t in (a, u, d))
+    da, du = ctx.buffer(n), ctx.buffer(n)
+    check(lib().turt_fused_swiglu_bwd(ctx.handle, pa, pu, pd, da, du, n))
+    assert _ok(ctx.download(da, n), ref_da)
+    assert _ok(ctx.download(du, n), ref_du)
+
+
+@pytest.mark.parametrize("N,V", [(256, 8192), (33, 48)])
+def test_ce_fused(ctx, orc, N, V):
+    from turt_b200._lib import check, lib, u32
+    rng = np.random.default_rng(N + V)
+    logits = (3 * rng.standard_normal((N, V))).astype(np.float32)
+    tgt = rng.integers(0, V, N).astype(np.uint32)
+    ref_loss, ref_g = orc.cross_entropy(logits, tgt)
+    pl = _dev(ctx, logits)
+    pt = ctx.index_buffer(u32(tgt))
+    rows = ctx.buffer(N)
+    check(lib().turt_fused_ce(ctx.handle, pl, pt, rows, N, V, 1.0 / N))
+    got_g = ctx.download(pl, N * V).reshape(N, V)
+    got_loss = float(ctx.download(rows, N).astype(np.float64).mean())
+    assert abs(got_loss - ref_loss) / abs(ref_loss) < 1e-6
+    assert _ok(got_g, ref_g)
+
+
+@pytest.mark.parametrize("clip", [0.0, 1.0])
+def test_adamw_clip(ctx, orc, clip):
+    from turt_b200._lib import check, lib
+    import ctypes as C
+    n = 100_003
+    rng = np.random.default_rng(5)
+    p, g, m = (rng.standard_normal(n).astype(np.float32) for _ in range(3))
+    v = np.abs(rng.standard_normal(n)).astype(np.float32)
+    lr, b1, b2, eps, wd, k = 3e-4, 0.9, 0.95, 1e-8, 0.1, 3
+    bc1, bc2 = 1 - b1 ** k, 1 - b2 ** k
+    rp, rg, rm, rv = p.copy(), g.copy(), m.copy(), v.copy()
+    ref_norm = float(np.sqrt((g.astype(np.float64) ** 2).sum()))
+    if clip > 0:
+        orc.clip(rg, clip)
+    orc.adamw_bc(rp, rg, rm, rv, lr, b1, b2, eps, wd, bc1, bc2)
+    bufs = [_dev(ctx, t) for t in (p, g, m, v)]
+    norm = C.c_double()
+    check(lib().turt_fused_adamw_clip(ctx.handle, bufs[0], bufs[1], bufs[2], bufs[3], n, lr, b1, b2, eps, wd, bc1,
+                                      bc2, clip, C.byref(norm)))
+    assert abs(norm.value - ref_norm) / ref_norm < 1e-9
+    for buf, ref in zip((bufs[0], bufs[2], bufs[3]), (rp, rm, rv)):
+        assert _ok(ctx.download(buf, n), ref)
+    np.testing.assert_array_equal(ctx.download(bufs[1], n), g)  # the gradient is not modified

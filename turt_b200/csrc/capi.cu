@@ -97,6 +97,7 @@ int turt_ctx_destroy(turt_ctx* ctx) {
   for (void* p : ctx->pending_free) cudaFree(p);
   for (void* p : ctx->live_set) cudaFree(p);
   cudaFree(ctx->flags);
+  if (ctx->scratch) cudaFree(ctx->scratch);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
   return OK;

@@ -17,6 +17,8 @@ struct turt_ctx {
   int live = 0, peak = 0;
   int precision = 3;  // GEMM_TF32X3 (validated default) or GEMM_TF32
   std::map<std::tuple<int, int, float>, float2*> rope_tables;
+  void* scratch = nullptr;  // grow-only device scratch of the standalone fused kernels
+  size_t scratch_bytes = 0;
 };
 
 namespace turt {

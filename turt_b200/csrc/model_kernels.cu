@@ -90,7 +90,8 @@ __global__ void __launch_bounds__(256) k_rms_fwd(const float* __restrict__ x, co
 }
 
 // Block partial of a per-column sum: the 8 warps' register partials (lane chunks) are combined
-// in shared memory in fixed order and written as row blockIdx.x of part[gridDim.x][E].
+// in shared memory in fixed order and written column-major as part[c][blockIdx.x] (nparts =
+// gridDim.x entries per column), so that the final reduction reads each column contiguously.
 template <int NJ>
 __device__ __forceinline__ void block_partial(const float4 (&acc)[NJ], float* sm, float* __restrict__ part, int E) {
   const int w = threadIdx.x / 32, lane = threadIdx.x & 31, n4 = E / 4;
@@ -104,7 +105,7 @@ __device__ __forceinline__ void block_partial(const float4 (&acc)[NJ], float* sm
     float t = 0.f;
 #pragma unroll
     for (int q = 0; q < kNormWarps; q++) t += sm[q * E + c];
-    part[(size_t)blockIdx.x * E + c] = t;
+    part[(size_t)c * gridDim.x + blockIdx.x] = t;
   }
 }
 
@@ -114,7 +115,7 @@ __device__ __forceinline__ void block_partial(const float4 (&acc)[NJ], float* sm
 // dx may alias dres.  Rows are dealt to warps grid-stride, two rows per iteration so that each
 // warp keeps 6*NJ independent 16-byte loads in flight.
 template <int NJ>
-__global__ void __launch_bounds__(256) k_rms_bwd(const float* __restrict__ x, const float* __restrict__ dy,
+__global__ void __launch_bounds__(256, 2) k_rms_bwd(const float* __restrict__ x, const float* __restrict__ dy,
                                                  const float* __restrict__ g, const float* __restrict__ rstd,
                                                  const float* dres, float* dx, float* __restrict__ dg_part, int rows,
                                                  int E) {
@@ -232,7 +233,7 @@ __global__ void __launch_bounds__(256) k_ln_fwd(const float* __restrict__ x, con
 // LayerNorm backward (LN_DX + LN_DGB, autograd.ts:275-308) with the residual gradient fused;
 // partial dgamma / dbeta per block.  One row per warp iteration, grid-stride.
 template <int NJ>
-__global__ void __launch_bounds__(256) k_ln_bwd(const float* __restrict__ x, const float* __restrict__ dy,
+__global__ void __launch_bounds__(256, 2) k_ln_bwd(const float* __restrict__ x, const float* __restrict__ dy,
                                                 const float* __restrict__ g, const float* __restrict__ mean,
                                                 const float* __restrict__ rstd, const float* dres, float* dx,
                                                 float* __restrict__ dg_part, float* __restrict__ db_part, int rows,
@@ -298,44 +299,27 @@ __global__ void __launch_bounds__(256) k_ln_bwd(const float* __restrict__ x, con
   block_partial<NJ>(dbl, sm, db_part, E);
 }
 
-// out[c] += sum_b part[b][c] (fixed order: deterministic).  One block per 32 columns; warp w
-// sums partial rows w, w+8, ... (coalesced 128-byte rows, four loads in flight), then the 8
-// warp sums combine in order.
+// out[c] += sum_b part[c][b] (column-major partials, fixed order: deterministic).  One warp per
+// column: the lanes' strided loads are all independent (one memory round trip for up to a few
+// hundred partials), then a butterfly sum.
 __global__ void k_reduce_parts(const float* __restrict__ part, int nparts, int C, float* __restrict__ out) {
-  __shared__ float red[8][33];
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c = blockIdx.x * 32 + lane;
+  const int c = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
+  if (c >= C) return;
+  const float* col = part + (size_t)c * nparts;
   float s = 0.f;
-  if (c < C) {
-    int b = w;
-    for (; b + 24 < nparts; b += 32) {
-      const float a0 = part[(size_t)b * C + c], a1 = part[(size_t)(b + 8) * C + c];
-      const float a2 = part[(size_t)(b + 16) * C + c], a3 = part[(size_t)(b + 24) * C + c];
-      s += a0;
-      s += a1;
-      s += a2;
-      s += a3;
-    }
-    for (; b < nparts; b += 8) s += part[(size_t)b * C + c];
-  }
-  red[w][lane] = s;
-  __syncthreads();
-  if (w == 0 && c < C) {
-    float t = 0.f;
-#pragma unroll
-    for (int q = 0; q < 8; q++) t += red[q][lane];
-    out[c] += t;
-  }
+  for (int b = lane; b < nparts; b += 32) s += col[b];
+  s = warp_sum(s);
+  if (lane == 0) out[c] += s;
 }
 
-// Column sums of g[rows][C] into partials (bias gradients; SEGSUM, autograd.ts:122-135):
-// partial row p sums rows p, p + P, p + 2P, ... (P = gridDim.y).
+// Column sums of g[rows][C] into column-major partials part[c][p] (bias gradients; SEGSUM,
+// autograd.ts:122-135): partial p sums rows p, p + P, p + 2P, ... (P = gridDim.y).
 __global__ void k_colsum_parts(const float* __restrict__ g, int rows, int C, float* __restrict__ part) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
   float s = 0.f;
   for (int r = blockIdx.y; r < rows; r += gridDim.y) s += g[(size_t)r * C + c];
-  part[(size_t)blockIdx.y * C + c] = s;
+  part[(size_t)c * gridDim.y + blockIdx.y] = s;
 }
 
 // -------------------------------------------------- fused softmax + cross-entropy
@@ -656,10 +640,10 @@ int rms_fwd(cudaStream_t st, const float* x, const float* g, float* y, float* rs
   TURT_LAUNCH_CHECK();
   return OK;
 }
-// Partial-sum rows a norm backward writes: one per block, at most one block per SM.
+// Partial-sum rows a norm backward writes: one per block, at most two blocks per SM.
 int norm_parts(int rows) {
   const int b = ceil_div(rows, kNormWarps);
-  return b < sm_count() ? b : sm_count();
+  return b < 2 * sm_count() ? b : 2 * sm_count();
 }
 int rms_bwd(cudaStream_t st, const float* x, const float* dy, const float* g, const float* rstd, const float* dres,
             float* dx, float* dg_accum, float* part, int rows, int E) {
@@ -670,7 +654,7 @@ int rms_bwd(cudaStream_t st, const float* x, const float* dy, const float* g, co
   TURT_NJ_SWITCH(E, CALL)
 #undef CALL
   TURT_LAUNCH_CHECK();
-  k_reduce_parts<<<ceil_div(E, 32), 256, 0, st>>>(part, nb, E, dg_accum);
+  k_reduce_parts<<<ceil_div(E, 8), 256, 0, st>>>(part, nb, E, dg_accum);
   TURT_LAUNCH_CHECK();
   return OK;
 }
@@ -693,9 +677,9 @@ int ln_bwd(cudaStream_t st, const float* x, const float* dy, const float* g, con
   TURT_NJ_SWITCH(E, CALL)
 #undef CALL
   TURT_LAUNCH_CHECK();
-  k_reduce_parts<<<ceil_div(E, 32), 256, 0, st>>>(part, nb, E, dg_accum);
+  k_reduce_parts<<<ceil_div(E, 8), 256, 0, st>>>(part, nb, E, dg_accum);
   TURT_LAUNCH_CHECK();
-  k_reduce_parts<<<ceil_div(E, 32), 256, 0, st>>>(part + (size_t)nb * E, nb, E, db_accum);
+  k_reduce_parts<<<ceil_div(E, 8), 256, 0, st>>>(part + (size_t)nb * E, nb, E, db_accum);
   TURT_LAUNCH_CHECK();
   return OK;
 }
@@ -704,7 +688,7 @@ int colsum_accum(cudaStream_t st, const float* g, int rows, int C, float* out_ac
   dim3 grid(ceil_div(C, 128), nb);
   k_colsum_parts<<<grid, 128, 0, st>>>(g, rows, C, part);
   TURT_LAUNCH_CHECK();
-  k_reduce_parts<<<ceil_div(C, 32), 256, 0, st>>>(part, nb, C, out_accum);
+  k_reduce_parts<<<ceil_div(C, 8), 256, 0, st>>>(part, nb, C, out_accum);
   TURT_LAUNCH_CHECK();
   return OK;
 }
