@@ -25,13 +25,13 @@ struct AttnTensors {
 };
 struct AttnScratch {
   float* dS = nullptr;  // [B*H][T][pitch]
-  float* dq = nullptr;  // [B*H][T][hd] (RoPE models)
-  float* dk = nullptr;
 };
 inline long attn_pitch(int T) { return ((long)T + 3) & ~3L; }
 bool attention_tc_supported(int hd);
+// rotated != 0: the RoPE-rotated head-major q / k copies in `at` were already written (by the
+// projection GEMM's EPI_QKV_ROPE epilogue); otherwise they are made here from qkv.
 int attention_tc_fwd(cudaStream_t st, const float* qkv, const float2* rope_cs, float* out, const AttnTensors& at, int B,
-                     int T, int H, int hd, int rope, int* flags, int precision);
+                     int T, int H, int hd, int rope, int rotated, int* flags, int precision);
 int attention_tc_bwd(cudaStream_t st, const float* qkv, const float2* rope_cs, const float* dout,
                      const AttnTensors& at, const AttnScratch& sc, float* dqkv, int B, int T, int H, int hd, int rope,
                      int* flags, int precision);

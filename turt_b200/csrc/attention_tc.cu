@@ -7,10 +7,11 @@
 // puts every contraction on the batched tcgen05 GEMM (3xTF32) with the B*H heads as a
 // two-level (sequence, head) batch, so q, k, v, dO and the merged outputs are addressed in
 // place inside the fused [N][3E] / [N][E] activations:
-//   forward : [RoPE q,k -> head-major copies]  S = q k^T (upper tiles skipped)
+//   forward : [RoPE q,k -> head-major copies, normally done by the qkv projection's epilogue]
+//             S = q k^T (upper tiles skipped)
 //             softmax rows (scale, causal mask, P kept)  O = P v (K-range cut at the diagonal)
 //   backward: dP = dO v^T  dS = P (dP - rowsum(P dP)) * scale  dV = P^T dO  dQ = dS k
-//             dK = dS^T q  [inverse RoPE on dQ, dK]
+//             dK = dS^T q  (inverse RoPE in the dQ / dK epilogues)
 // Masked probabilities are exact zeros, so the causal tile / K-range skips change no result.
 #include "attention.cuh"
 #include "gemm.cuh"
@@ -42,31 +43,6 @@ __global__ void k_rope_heads(const float* __restrict__ qkv, const float2* __rest
     y.z = x.z * c1.x - x.w * c1.y;
     y.w = x.z * c1.y + x.w * c1.x;
     *reinterpret_cast<float4*>(dst + (((long)b * H + h) * T + t) * hd + 4 * f) = y;
-  }
-}
-
-// Head-major dq, dk [B*H][T][hd] -> dqkv[N][3E] columns [0, E) and [E, 2E), rotated back by -theta.
-__global__ void k_unrope_heads(const float* __restrict__ dq, const float* __restrict__ dk,
-                               const float2* __restrict__ cs, float* __restrict__ dqkv, int B, int T, int H, int hd) {
-  const int E = H * hd, q4 = hd / 4;
-  const long total = (long)B * T * H * q4;
-  const int which = blockIdx.y;
-  const float* src = which ? dk : dq;
-  float* dst = dqkv + which * E;
-  for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (long)gridDim.x * blockDim.x) {
-    const int f = (int)(e % q4);
-    const long r = e / q4;  // (b, h, t) head-major
-    const int t = (int)(r % T);
-    const long bh = r / T;
-    const int h = (int)(bh % H), b = (int)(bh / H);
-    const float4 g = *reinterpret_cast<const float4*>(src + r * hd + 4 * f);
-    const float2 c0 = cs[(long)t * (hd / 2) + 2 * f], c1 = cs[(long)t * (hd / 2) + 2 * f + 1];
-    float4 y;
-    y.x = g.x * c0.x + g.y * c0.y;
-    y.y = -g.x * c0.y + g.y * c0.x;
-    y.z = g.z * c1.x + g.w * c1.y;
-    y.w = -g.z * c1.y + g.w * c1.x;
-    *reinterpret_cast<float4*>(dst + ((long)b * T + t) * 3 * E + h * hd + 4 * f) = y;
   }
 }
 
@@ -329,28 +305,17 @@ GemmEpi merged_epi(float* base, long ld, int T, int hd, int causal) {
   return e;
 }
 
-GemmEpi headmajor_epi(float* base, int T, int H, int hd, int causal) {
-  GemmEpi e;
-  e.kind = EPI_STORE;
-  e.C = base;
-  e.ldc = hd;
-  e.strideC = (long)T * hd;
-  e.strideC_hi = (long)H * T * hd;
-  e.causal = causal;
-  return e;
-}
-
 }  // namespace
 
 bool attention_tc_supported(int hd) { return hd >= 16 && hd <= 256 && hd % 16 == 0; }
 
 int attention_tc_fwd(cudaStream_t st, const float* qkv, const float2* rope_cs, float* out, const AttnTensors& at, int B,
-                     int T, int H, int hd, int rope, int* flags, int precision) {
+                     int T, int H, int hd, int rope, int rotated, int* flags, int precision) {
   TURT_REQUIRE(attention_tc_supported(hd), "attention: head dim must be a multiple of 16 in [16, 256]");
   TURT_REQUIRE(at.P && (!rope || (at.qr && at.kr)), "attention: buffers missing");
   const int E = H * hd, BH = B * H;
   const float scale = 1.0f / sqrtf((float)hd);
-  if (rope) {
+  if (rope && !rotated) {
     k_rope_heads<<<dim3(grid_for((long)B * T * H * hd / 4), 2), 256, 0, st>>>(qkv, rope_cs, at.qr, at.kr, B, T, H, hd);
     TURT_LAUNCH_CHECK();
   }
@@ -369,7 +334,7 @@ int attention_tc_bwd(cudaStream_t st, const float* qkv, const float2* rope_cs, c
                      const AttnTensors& at, const AttnScratch& sc, float* dqkv, int B, int T, int H, int hd, int rope,
                      int* flags, int precision) {
   TURT_REQUIRE(attention_tc_supported(hd), "attention: head dim must be a multiple of 16 in [16, 256]");
-  TURT_REQUIRE(at.P && sc.dS && (!rope || (at.qr && at.kr && sc.dq && sc.dk)), "attention: buffers missing");
+  TURT_REQUIRE(at.P && sc.dS && (!rope || (at.qr && at.kr)), "attention: buffers missing");
   const int E = H * hd, BH = B * H;
   const float scale = 1.0f / sqrtf((float)hd);
   const Views w = views(qkv, dout, at, at.P, T, H, hd, rope != 0);
@@ -384,25 +349,19 @@ int attention_tc_bwd(cudaStream_t st, const float* qkv, const float2* rope_cs, c
   GemmEpi e = merged_epi(dqkv + 2 * E, 3L * E, T, hd, CAUSAL_K_UPPER);
   e.bdiv = H;
   RC(gemm_tf32(st, T, hd, T, BH, w.PT, mn(w.dout), e, flags, precision));
-  // dQ = dS k, dK = dS^T q  (rotated frame when RoPE is on)
+  // dQ = dS k, dK = dS^T q, written into dqkv; with RoPE they are computed in the rotated frame
+  // and rotated back (by -theta) in the epilogue.
+  e = merged_epi(dqkv, 3L * E, T, hd, CAUSAL_K_LOWER);
+  e.bdiv = H;
   if (rope) {
-    e = headmajor_epi(sc.dq, T, H, hd, CAUSAL_K_LOWER);
-    e.bdiv = H;
-    RC(gemm_tf32(st, T, hd, T, BH, dS, mn(w.k), e, flags, precision));
-    e = headmajor_epi(sc.dk, T, H, hd, CAUSAL_K_UPPER);
-    e.bdiv = H;
-    RC(gemm_tf32(st, T, hd, T, BH, dST, mn(w.q), e, flags, precision));
-    k_unrope_heads<<<dim3(grid_for((long)B * T * H * hd / 4), 2), 256, 0, st>>>(sc.dq, sc.dk, rope_cs, dqkv, B, T, H,
-                                                                                hd);
-    TURT_LAUNCH_CHECK();
-  } else {
-    e = merged_epi(dqkv, 3L * E, T, hd, CAUSAL_K_LOWER);
-    e.bdiv = H;
-    RC(gemm_tf32(st, T, hd, T, BH, dS, mn(w.k), e, flags, precision));
-    e = merged_epi(dqkv + E, 3L * E, T, hd, CAUSAL_K_UPPER);
-    e.bdiv = H;
-    RC(gemm_tf32(st, T, hd, T, BH, dST, mn(w.q), e, flags, precision));
+    e.kind = EPI_STORE_UNROPE;
+    e.rope = rope_cs;
+    e.rope_hd = hd;
   }
+  RC(gemm_tf32(st, T, hd, T, BH, dS, mn(w.k), e, flags, precision));
+  e.C = dqkv + E;
+  e.causal = CAUSAL_K_UPPER;
+  RC(gemm_tf32(st, T, hd, T, BH, dST, mn(w.q), e, flags, precision));
   return OK;
 }
 

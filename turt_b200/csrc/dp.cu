@@ -90,7 +90,9 @@ bool dp_active(turt_model* m) { return m->dp && m->dp->world > 1; }
 
 static int reduce_range(turt_model* m, size_t begin, size_t end, cudaEvent_t ev) {
   DpState* d = m->dp;
-  TURT_CHECK_CUDA(cudaEventRecord(ev, m->ctx->stream));
+  cudaStream_t gs = nullptr;
+  RC(grad_writes_stream(m, &gs));
+  TURT_CHECK_CUDA(cudaEventRecord(ev, gs));
   TURT_CHECK_CUDA(cudaStreamWaitEvent(d->comm_stream, ev, 0));
   NCCL_CHECK(api().AllReduce(m->G + begin, m->G + begin, end - begin, ncclFloat32, ncclSum, d->comm, d->comm_stream));
   return OK;

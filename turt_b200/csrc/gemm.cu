@@ -205,6 +205,39 @@ __device__ __forceinline__ void epi_chunk(const GemmEpi& epi, const EpiVec& vec,
           }
       }
     } break;
+    case EPI_QKV_ROPE: {
+      const int hd = epi.rope_hd, H = epi.rope_H, T = epi.rope_T, E = H * hd;
+      const int sec = col0 / E;  // 0 q, 1 k, 2 v (E is a multiple of 32: a chunk never straddles)
+      if (sec == 2) {
+        st32(dst, v, n, vec.C);
+        break;
+      }
+      float* base = sec == 0 ? epi.qr : epi.kr;
+      const int t = (int)(row % T);
+      const long b = row / T;
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        if (j >= n) break;
+        const int c = col0 - sec * E + j, h = c / hd, d = c % hd;
+        const float2 c0 = epi.rope[(long)t * (hd / 2) + d / 2], c1 = epi.rope[(long)t * (hd / 2) + d / 2 + 1];
+        const float4 y = make_float4(v[j] * c0.x - v[j + 1] * c0.y, v[j] * c0.y + v[j + 1] * c0.x,
+                                     v[j + 2] * c1.x - v[j + 3] * c1.y, v[j + 2] * c1.y + v[j + 3] * c1.x);
+        *reinterpret_cast<float4*>(base + ((b * H + h) * T + t) * hd + d) = y;
+      }
+    } break;
+    case EPI_STORE_UNROPE: {
+      const int hd = epi.rope_hd;
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        if (j < n) {
+          const float2 cs = epi.rope[row * (hd / 2) + (col0 + j) / 2];
+          const float g0 = v[j], g1 = v[j + 1];
+          v[j] = g0 * cs.x + g1 * cs.y;
+          v[j + 1] = -g0 * cs.y + g1 * cs.x;
+        }
+      }
+      st32(dst, v, n, vec.C);
+    } break;
     default:
       break;
   }

@@ -16,6 +16,9 @@ enum EpiKind : int {
   EPI_SWIGLU_FWD = 6,  // C = acc (interleaved gate|up pre-activations), C2 = silu(gate) * up
   EPI_SWIGLU_BWD = 7,  // acc = d(act); R = interleaved gate|up pre-acts; C = interleaved d(gate)|d(up)
   EPI_GELU_BWD = 8,    // C = acc * gelu'(R)
+  EPI_QKV_ROPE = 9,    // acc = fused q|k|v projection of token `row`: q, k rotated (RoPE) into the
+                       // head-major qr / kr [B*H][T][hd]; v stored into C (columns [2E, 3E))
+  EPI_STORE_UNROPE = 10,  // C = acc rotated back by -theta (row = position t, columns = head dims)
 };
 
 // Interleave granularity of the fused gate|up weight and activations: columns
@@ -47,6 +50,11 @@ struct GemmEpi {
   int bdiv = 0;
   long strideC_hi = 0;
   int causal = CAUSAL_NONE;
+  // RoPE epilogues: cos/sin table [T][hd/2] and the head geometry; qr / kr for EPI_QKV_ROPE.
+  const float2* rope = nullptr;
+  int rope_T = 0, rope_H = 0, rope_hd = 0;
+  float* qr = nullptr;
+  float* kr = nullptr;
 };
 
 // Operand description.  `mn_major` = the operand's contiguous dimension is M (for A) or N

@@ -200,7 +200,7 @@ int ensure_workspace(turt_model* m, int B, int T) {
   size_t logits = take((size_t)N * V), loss_rows = take(N);
   size_t dx = take(NE), dy = take(NE), datt = take(NE), dqkv = take(3 * NE), dpre = take((size_t)N * W1);
   size_t Dsc = take(BHT);
-  size_t dS = tc ? take((size_t)S_need) : 0, dqh = tc && rope ? take(NE) : 0, dkh = tc && rope ? take(NE) : 0;
+  size_t dS = tc ? take((size_t)S_need) : 0;
   const int C = 3 * E > W1 ? 3 * E : W1;
   size_t part = take((size_t)2 * norm_parts(N) * (C > E ? C : E));
   size_t ids = take(N), tgt = take(N);
@@ -243,8 +243,6 @@ int ensure_workspace(turt_model* m, int B, int T) {
   m->dpre = F(dpre);
   m->Dsc = F(Dsc);
   m->dS = tc ? F(dS) : nullptr;
-  m->dqh = tc && rope ? F(dqh) : nullptr;
-  m->dkh = tc && rope ? F(dkh) : nullptr;
   m->part = F(part);
   m->d_ids = reinterpret_cast<uint32_t*>(base + ids);
   m->d_tgt = reinterpret_cast<uint32_t*>(base + tgt);
@@ -301,10 +299,21 @@ int forward(turt_model* m, int B, int T, bool train, float loss_scale) {
       RC(ln_fwd(st, a.x, P + L.ln1g, P + L.ln1b, a.y1, a.mu1, a.rs1, N, E, m->eps));
     GemmEpi e = epi(m->modern ? EPI_STORE : EPI_BIAS, a.qkv, 3 * E);
     if (!m->modern) e.bias = P + L.bqkv;
+    const bool rope_epi = m->modern && m->attn_tc;  // q, k rotated straight into the head-major copies
+    if (rope_epi) {
+      e.kind = EPI_QKV_ROPE;
+      e.rope = m->rope_cs;
+      e.rope_T = T;
+      e.rope_H = H;
+      e.rope_hd = hd;
+      e.qr = a.qr;
+      e.kr = a.kr;
+    }
     RC(gemm_tf32(st, N, 3 * E, E, 1, opK(a.y1, E), opMN(P + L.wqkv, 3 * E), e, flags, mp(m)));
     if (m->attn_tc) {
       AttnTensors at{a.P, a.qr, a.kr};
-      RC(attention_tc_fwd(st, a.qkv, m->rope_cs, a.att, at, B, T, H, hd, m->modern ? 1 : 0, flags, mp(m)));
+      RC(attention_tc_fwd(st, a.qkv, m->rope_cs, a.att, at, B, T, H, hd, m->modern ? 1 : 0, rope_epi ? 1 : 0, flags,
+                          mp(m)));
     } else {
       RC(attention_fwd(st, a.qkv, m->rope_cs, a.att, a.lse, B, T, H, hd, m->modern ? 1 : 0));
     }
@@ -349,15 +358,51 @@ int forward(turt_model* m, int B, int T, bool train, float loss_scale) {
   return OK;
 }
 
+}  // namespace
+
+int turt::stream_join(turt_model* m, cudaStream_t from, cudaStream_t to) {
+  cudaEvent_t e = m->wg_ring[m->wg_next++ % 16];
+  TURT_CHECK_CUDA(cudaEventRecord(e, from));
+  TURT_CHECK_CUDA(cudaStreamWaitEvent(to, e, 0));
+  return OK;
+}
+
+int turt::grad_writes_stream(turt_model* m, cudaStream_t* out) {
+  RC(stream_join(m, m->ctx->stream, m->wg));
+  *out = m->wg;
+  return OK;
+}
+
+namespace {
+
 int backward(turt_model* m, int B, int T) {
-  cudaStream_t st = m->ctx->stream;
+  cudaStream_t st = m->ctx->stream, wg = m->wg;
   int* flags = m->ctx->flags;
   const int N = B * T, E = m->cfg.n_embd, H = m->cfg.n_head, hd = E / H, V = m->cfg.vocab_size, h = m->hid;
   const float* P = m->P;
   float* G = m->G;
+  // Weight-gradient GEMMs (dW = X^T dY) are forked onto `wg` as soon as dY exists.  The main
+  // stream waits for them only where it overwrites a buffer they read: dx (updated in place by
+  // the norm backward), dpre and dqkv (reused by the next layer), and the wte gradient (the
+  // embedding backward accumulates into it).  mark[0]: after dW2 (reads dx), mark[1]: after
+  // dW1 (reads dpre), mark[2]: after dWproj (reads dx), mark[3]: after dWqkv (reads dqkv).
+  cudaEvent_t* mark = m->wg_mark;
+  bool pending[4] = {false, false, false, false};
+  auto fork = [&]() { return stream_join(m, st, wg); };
+  auto set_mark = [&](int i) -> int {
+    TURT_CHECK_CUDA(cudaEventRecord(mark[i], wg));
+    pending[i] = true;
+    return OK;
+  };
+  auto wait_mark = [&](int i) -> int {
+    if (pending[i]) TURT_CHECK_CUDA(cudaStreamWaitEvent(st, mark[i], 0));
+    pending[i] = false;
+    return OK;
+  };
   // head: dyf = dlogits * wte ; dwte += dlogits^T * yf
   RC(gemm_tf32(st, N, E, V, 1, opK(m->logits, V), opMN(P + m->wte, E), epi(EPI_STORE, m->dy, E), flags, mp(m)));
-  RC(gemm_tf32(st, V, E, N, 1, opMN(m->logits, V), opMN(m->yf, E), epi(EPI_ACCUM, G + m->wte, E), flags, mp(m)));
+  RC(fork());
+  RC(gemm_tf32(wg, V, E, N, 1, opMN(m->logits, V), opMN(m->yf, E), epi(EPI_ACCUM, G + m->wte, E), flags, mp(m)));
   if (m->modern)
     RC(rms_bwd(st, m->xL, m->dy, P + m->lnfg, m->rsf, nullptr, m->dx, G + m->lnfg, m->part, N, E));
   else
@@ -366,36 +411,50 @@ int backward(turt_model* m, int B, int T) {
     const LayerOff& L = m->layers[l];
     LayerAct& a = m->act[l];
     // ---- MLP
+    RC(wait_mark(1));  // dpre is rewritten below; the previous layer's dW1 reads it
     if (m->modern) {
       GemmEpi e = epi(EPI_SWIGLU_BWD, m->dpre, 2 * h);
       e.R = a.pre;
       e.ldr = 2 * h;
       RC(gemm_tf32(st, N, h, E, 1, opK(m->dx, E), opK(P + L.w2, E), e, flags, mp(m)));
-      RC(gemm_tf32(st, h, E, N, 1, opMN(a.act, h), opMN(m->dx, E), epi(EPI_ACCUM, G + L.w2, E), flags, mp(m)));
+      RC(fork());
+      RC(gemm_tf32(wg, h, E, N, 1, opMN(a.act, h), opMN(m->dx, E), epi(EPI_ACCUM, G + L.w2, E), flags, mp(m)));
+      RC(set_mark(0));
       RC(gemm_tf32(st, N, E, 2 * h, 1, opK(m->dpre, 2 * h), opK(P + L.w1, 2 * h), epi(EPI_STORE, m->dy, E), flags, mp(m)));
-      RC(gemm_tf32(st, E, 2 * h, N, 1, opMN(a.y2, E), opMN(m->dpre, 2 * h), epi(EPI_ACCUM, G + L.w1, 2 * h), flags, mp(m)));
+      RC(fork());
+      RC(gemm_tf32(wg, E, 2 * h, N, 1, opMN(a.y2, E), opMN(m->dpre, 2 * h), epi(EPI_ACCUM, G + L.w1, 2 * h), flags,
+                   mp(m)));
+      RC(set_mark(1));
     } else {
       GemmEpi e = epi(EPI_GELU_BWD, m->dpre, h);
       e.R = a.pre;
       e.ldr = h;
       RC(gemm_tf32(st, N, h, E, 1, opK(m->dx, E), opK(P + L.w2, E), e, flags, mp(m)));
-      RC(gemm_tf32(st, h, E, N, 1, opMN(a.act, h), opMN(m->dx, E), epi(EPI_ACCUM, G + L.w2, E), flags, mp(m)));
+      RC(fork());
+      RC(gemm_tf32(wg, h, E, N, 1, opMN(a.act, h), opMN(m->dx, E), epi(EPI_ACCUM, G + L.w2, E), flags, mp(m)));
+      RC(set_mark(0));
       RC(colsum_accum(st, m->dx, N, E, G + L.b2, m->part));
       RC(gemm_tf32(st, N, E, h, 1, opK(m->dpre, h), opK(P + L.w1, h), epi(EPI_STORE, m->dy, E), flags, mp(m)));
-      RC(gemm_tf32(st, E, h, N, 1, opMN(a.y2, E), opMN(m->dpre, h), epi(EPI_ACCUM, G + L.w1, h), flags, mp(m)));
+      RC(fork());
+      RC(gemm_tf32(wg, E, h, N, 1, opMN(a.y2, E), opMN(m->dpre, h), epi(EPI_ACCUM, G + L.w1, h), flags, mp(m)));
+      RC(set_mark(1));
       RC(colsum_accum(st, m->dpre, N, h, G + L.b1, m->part));
     }
+    RC(wait_mark(0));  // dx is rewritten in place below; dW2 reads it
     if (m->modern)
       RC(rms_bwd(st, a.h, m->dy, P + L.ln2g, a.rs2, m->dx, m->dx, G + L.ln2g, m->part, N, E));
     else
       RC(ln_bwd(st, a.h, m->dy, P + L.ln2g, a.mu2, a.rs2, m->dx, m->dx, G + L.ln2g, G + L.ln2b, m->part, N, E));
     // ---- attention
     RC(gemm_tf32(st, N, E, E, 1, opK(m->dx, E), opK(P + L.wproj, E), epi(EPI_STORE, m->datt, E), flags, mp(m)));
-    RC(gemm_tf32(st, E, E, N, 1, opMN(a.att, E), opMN(m->dx, E), epi(EPI_ACCUM, G + L.wproj, E), flags, mp(m)));
+    RC(fork());
+    RC(gemm_tf32(wg, E, E, N, 1, opMN(a.att, E), opMN(m->dx, E), epi(EPI_ACCUM, G + L.wproj, E), flags, mp(m)));
+    RC(set_mark(2));
     if (!m->modern) RC(colsum_accum(st, m->dx, N, E, G + L.bproj, m->part));
+    RC(wait_mark(3));  // dqkv is rewritten below; the previous layer's dWqkv reads it
     if (m->attn_tc) {
       AttnTensors at{a.P, a.qr, a.kr};
-      AttnScratch sc{m->dS, m->dqh, m->dkh};
+      AttnScratch sc{m->dS};
       RC(attention_tc_bwd(st, a.qkv, m->rope_cs, m->datt, at, sc, m->dqkv, B, T, H, hd, m->modern ? 1 : 0, flags,
                           mp(m)));
     } else {
@@ -404,13 +463,20 @@ int backward(turt_model* m, int B, int T) {
     }
     if (!m->modern) RC(colsum_accum(st, m->dqkv, N, 3 * E, G + L.bqkv, m->part));
     RC(gemm_tf32(st, N, E, 3 * E, 1, opK(m->dqkv, 3 * E), opK(P + L.wqkv, 3 * E), epi(EPI_STORE, m->dy, E), flags, mp(m)));
-    RC(gemm_tf32(st, E, 3 * E, N, 1, opMN(a.y1, E), opMN(m->dqkv, 3 * E), epi(EPI_ACCUM, G + L.wqkv, 3 * E), flags, mp(m)));
+    RC(fork());
+    RC(gemm_tf32(wg, E, 3 * E, N, 1, opMN(a.y1, E), opMN(m->dqkv, 3 * E), epi(EPI_ACCUM, G + L.wqkv, 3 * E), flags,
+                 mp(m)));
+    RC(set_mark(3));
+    RC(wait_mark(2));  // dx is rewritten in place below; dWproj reads it
     if (m->modern)
       RC(rms_bwd(st, a.x, m->dy, P + L.ln1g, a.rs1, m->dx, m->dx, G + L.ln1g, m->part, N, E));
     else
       RC(ln_bwd(st, a.x, m->dy, P + L.ln1g, a.mu1, a.rs1, m->dx, m->dx, G + L.ln1g, G + L.ln1b, m->part, N, E));
     if (dp_active(m) && !m->dp_defer) RC(dp_after_layer(m, l));
   }
+  // the embedding backward accumulates into the wte gradient that the head's dW GEMM (on wg)
+  // writes, and the next forward rewrites the activations the weight-gradient GEMMs read
+  RC(stream_join(m, wg, st));
   RC(embed_bwd(st, m->dx, m->d_ids, G + m->wte, m->modern ? nullptr : G + m->wpe, N, T, E, V));
   if (dp_active(m) && !m->dp_defer) {
     RC(dp_after_head(m));
@@ -504,6 +570,9 @@ int turt_model_create(turt_ctx* ctx, const turt_config* cfg, turt_model** out) {
   TURT_CHECK_CUDA(cudaMalloc(&m->norm_dev, 16));
   TURT_CHECK_CUDA(cudaMalloc(&m->norm_scratch, sizeof(double) * norm_scratch_doubles()));
   TURT_CHECK_CUDA(cudaMallocHost(&m->h_loss, 16));
+  TURT_CHECK_CUDA(cudaStreamCreateWithFlags(&m->wg, cudaStreamNonBlocking));
+  for (auto& e : m->wg_ring) TURT_CHECK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  for (auto& e : m->wg_mark) TURT_CHECK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   TURT_CHECK_CUDA(cudaStreamSynchronize(st));
   *out = m;
   return OK;
@@ -523,6 +592,14 @@ int turt_model_set_attention(turt_model* m, int mode) {
 int turt_model_destroy(turt_model* m) {
   MODEL_GUARD(m);
   cudaStreamSynchronize(m->ctx->stream);
+  if (m->wg) {
+    cudaStreamSynchronize(m->wg);
+    cudaStreamDestroy(m->wg);
+  }
+  for (auto& e : m->wg_ring)
+    if (e) cudaEventDestroy(e);
+  for (auto& e : m->wg_mark)
+    if (e) cudaEventDestroy(e);
   if (m->dp) turt_dp_destroy(m);
   free_workspace(m);
   cudaFree(m->P);

@@ -58,7 +58,7 @@ struct turt_model {
   float *xL = nullptr, *yf = nullptr, *rsf = nullptr, *muf = nullptr, *logits = nullptr, *loss_rows = nullptr;
   float *dx = nullptr, *dy = nullptr, *datt = nullptr, *dqkv = nullptr, *dpre = nullptr, *Dsc = nullptr,
         *part = nullptr;
-  float *dS = nullptr, *dqh = nullptr, *dkh = nullptr;  // tensor-core attention backward scratch
+  float* dS = nullptr;  // tensor-core attention backward scratch
   uint32_t *d_ids = nullptr, *d_tgt = nullptr;
   uint32_t *h_ids = nullptr, *h_tgt = nullptr;  // pinned staging
   float* loss_dev = nullptr;
@@ -68,9 +68,21 @@ struct turt_model {
   float* h_loss = nullptr;  // pinned
   turt::DpState* dp = nullptr;
   bool dp_defer = false;
+  // Weight-gradient GEMMs of the backward pass run on their own stream, overlapping the
+  // data-gradient chain; `wg_ring` events order the forks / joins, `wg_mark` ones are kept
+  // until the main stream reuses a buffer that a pending weight-gradient GEMM reads.
+  cudaStream_t wg = nullptr;
+  cudaEvent_t wg_ring[16] = {};
+  cudaEvent_t wg_mark[4] = {};
+  int wg_next = 0;
 };
 
 namespace turt {
+// Makes stream `to` wait for everything issued so far on stream `from`.
+int stream_join(turt_model* m, cudaStream_t from, cudaStream_t to);
+// The stream whose completion implies every gradient write issued so far (joins the
+// weight-gradient stream behind the main one).
+int grad_writes_stream(turt_model* m, cudaStream_t* out);
 // DP hooks called by the backward pass (dp.cu).
 int dp_after_layer(turt_model* m, int layer);
 int dp_after_head(turt_model* m);
