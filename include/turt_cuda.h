@@ -63,8 +63,9 @@ int turt_set_precision(turt_ctx* ctx, int precision);
 int turt_get_precision(turt_ctx* ctx, int* precision);
 /* Process-wide tuning override of the tensor-core GEMM: output-tile width `bn` (64, 128, 192
  * or 256 columns; 0 = chosen per problem shape, the default) and kernel `pair` (1 = two-CTA
- * cluster kernel with 256-row tiles, 3xTF32 only; 0 = single-CTA kernel; -1 = chosen per
- * shape, the default).  No reference counterpart: the reference's WGSL matmul has one fixed
+ * cluster kernel with 256-row tiles, 3xTF32 only; 0 = single-CTA kernel; 2 = single-CTA
+ * kernel with two CTAs resident per SM, 3xTF32, tile width 64 or 128; -1 = chosen per shape,
+ * the default).  No reference counterpart: the reference's WGSL matmul has one fixed
  * 16x16 workgroup tile. */
 int turt_gemm_set_tile(int bn, int pair);
 

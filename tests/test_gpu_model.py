@@ -157,13 +157,15 @@ def test_sequence_longer_than_block_rejected(ctx):
         model.close()
 
 
-@pytest.mark.parametrize("pair", [0, 1])
+@pytest.mark.parametrize("pair", [0, 1, 2])
 @pytest.mark.parametrize("bn", [64, 128, 192, 256])
 @pytest.mark.parametrize("arch", ["gpt2", "modern"])
 def test_fused_epilogues_every_tile_width(ctx, orc, arch, bn, pair):
     """Bias / GELU / SwiGLU / residual epilogues and the attention GEMMs (two-level batch,
     causal skips) under each forced GEMM tile width and kernel (single CTA / CTA pair)."""
     from turt_b200._lib import check, lib
+    if pair == 2 and bn > 128:
+        pytest.skip("two CTAs per SM exist for tile widths 64 and 128")
     check(lib().turt_gemm_set_tile(bn, pair))
     try:
         loss, ref, le, ge, name = _run_parity(ctx, orc, 512, 96, 2, 2, 128, arch, 3, 80, 352 if arch == "modern" else 0)
@@ -174,10 +176,11 @@ def test_fused_epilogues_every_tile_width(ctx, orc, arch, bn, pair):
 
 
 @pytest.mark.parametrize("arch", ["gpt2", "modern"])
-@pytest.mark.parametrize("t", [7, 130, 200])
+@pytest.mark.parametrize("t", [7, 130, 200, 301])
 def test_tensor_attention_ragged(ctx, orc, arch, t):
     """Tensor-core attention with sequence lengths that are not multiples of 4 (padded score
-    pitch), of the 128-row tile (diagonal tiles split), and above one tile; head dim 16."""
-    loss, ref, le, ge, name = _run_parity(ctx, orc, 256, 256, 2, 4, 64, arch, 2, t, attn=1)
+    pitch), of the 128-row tile (diagonal tiles split), above one tile, and above 256 (softmax
+    in separate row kernels instead of the score GEMMs' epilogues); head dim 16."""
+    loss, ref, le, ge, name = _run_parity(ctx, orc, 256, 320, 2, 4, 64, arch, 2, t, attn=1)
     assert le <= LOSS_TOL, (loss, ref)
     assert ge <= GRAD_TOL, (ge, name)

@@ -131,7 +131,8 @@ int turt_get_precision(turt_ctx* ctx, int* precision) {
 
 int turt_gemm_set_tile(int bn, int pair) {
   TURT_REQUIRE(bn == 0 || bn == 64 || bn == 128 || bn == 192 || bn == 256, "tile width must be 0, 64, 128, 192 or 256");
-  TURT_REQUIRE(pair >= -1 && pair <= 1, "pair must be -1 (automatic), 0 (single CTA) or 1 (CTA pair)");
+  TURT_REQUIRE(pair >= -1 && pair <= 2,
+               "kernel must be -1 (automatic), 0 (single CTA), 1 (CTA pair) or 2 (two single CTAs per SM)");
   gemm_set_tile_override(bn, pair);
   return OK;
 }
