@@ -563,7 +563,7 @@ __global__ void __launch_bounds__(GemmShape<BN, BK, X3, MINB>::THREADS, MINB)
 // single-CTA kernel.  Both accumulators (128 lanes x BN columns, double-buffered) live in each
 // CTA's own TMEM, so each CTA drains its own rows.
 //
-// Cross-CTA signalling, all without multicast:
+// Cross-CTA signalling, every arrive and commit aimed at one barrier of one CTA:
 //   full[s]    (each CTA)  its own TMA bytes landed              -> its converter warps
 //   conv[s]    (each CTA)  its 4 converter warps done            -> MMA issuer / odd relay
 //   pconv[s]   (even CTA)  odd CTA's conv[s] completed (relayed) -> MMA issuer
