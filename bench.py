@@ -332,7 +332,8 @@ def run_gpu(args, w, rank: int, world: int, local_rank: int) -> None:
                        "last_loss": last_loss},
             "roofline": {"bound": "tensor", "kernel": "k_gemm_tf32 (head projection %dx%dx%d)" % (N_tok, V, E),
                          "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s", "frac": achieved / tf32_peak,
-                         "traffic": read_profile_traffic("gemm_pair_head_fwd_8192x8192x384.md"),
+                         "traffic": (read_profile_traffic("gemm_pair_head_fwd_8192x8192x384.md")
+                                     if (N_tok, V, E) == (8192, 8192, 384) else None),
                          "peak_source": f"{peaks['source']} bf16 dense / 2",
                          "launch_ms": gemm_ms,
                          "mma_issue_factor": 3 if args.precision == 3 else 1,

@@ -647,7 +647,8 @@ struct PairShape {
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(352, 1)
     k_gemm_tf32_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmEpi epi,
-                     int M, int N, int K, int batches, int bdiv, int causal, int* flags) {
+                     int M, int N, int K, int batches, int bdiv, int causal, int ksplits, int kt_per_split,
+                     int* flags) {
   using S = PairShape<BN>;
   constexpr int STAGES = S::STAGES, BK = S::BK;
   static_assert(BN % 64 == 0 && BN <= 256, "BN");
@@ -668,7 +669,7 @@ __global__ void __launch_bounds__(352, 1)
   const uint32_t rank = cluster_rank();
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int mt = (M + 2 * BM - 1) / (2 * BM), nt = (N + BN - 1) / BN;
-  const int units = mt * nt * batches;
+  const int units = mt * nt * ksplits * batches;
   const int kt_total = (K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -706,12 +707,14 @@ __global__ void __launch_bounds__(352, 1)
     m0 = (u % mt) * 2 * BM;
     u /= mt;
     n0 = (u % nt) * BN;
-    b = u / nt;
-    kt0 = 0;
-    int kt1 = kt_total;
+    u /= nt;
+    const int split = u % ksplits;
+    b = u / ksplits;
+    kt0 = split * kt_per_split;
+    int kt1 = min(kt_total, kt0 + kt_per_split);
     if (causal == CAUSAL_SKIP_UPPER && n0 >= m0 + 2 * BM) return false;
     if (causal == CAUSAL_K_LOWER) kt1 = min(kt1, (m0 + 2 * BM + BK - 1) / BK);
-    if (causal == CAUSAL_K_UPPER) kt0 = m0 / BK;
+    if (causal == CAUSAL_K_UPPER) kt0 = max(kt0, m0 / BK);
     nkt = kt1 - kt0;
     return nkt > 0;
   };
@@ -1143,7 +1146,7 @@ int launch_pair(const LaunchArgs& a) {
     }
     max_pairs = n;
   }
-  const long units = (long)ceil_div(a.M, 2 * BM) * ceil_div(a.N, BN) * a.batch;
+  const long units = (long)ceil_div(a.M, 2 * BM) * ceil_div(a.N, BN) * a.batch * a.ks;
   const int pairs = (int)(units < max_pairs ? units : max_pairs);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -1157,7 +1160,8 @@ int launch_pair(const LaunchArgs& a) {
   cfg.stream = a.st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  TURT_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kfn, a.ma, a.mb, a.epi, a.M, a.N, a.K, a.batch, a.bdiv, a.causal, a.flags));
+  TURT_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kfn, a.ma, a.mb, a.epi, a.M, a.N, a.K, a.batch, a.bdiv, a.causal, a.ks,
+                                     a.kt_per, a.flags));
   note_launch();
   return OK;
 }
@@ -1218,8 +1222,7 @@ struct TilePlan {
 // Tile width, K-split count and single-CTA / CTA-pair kernel with the shortest modelled
 // makespan: ceil(units / concurrent units) x (k-steps per unit x step cost) + pipeline fill
 // + one epilogue drain, plus, per extra split, the atomic reduction of the M x N output.
-// `max_ks` is 1 when the epilogue cannot accumulate partial sums.  Pairs run 3xTF32 only,
-// without K splits.
+// `max_ks` is 1 when the epilogue cannot accumulate partial sums.  Pairs run 3xTF32 only.
 TilePlan plan_tiles(int M, int N, int K, int batch, bool x3, int max_ks, int force_bn, int force_pair) {
   const int sms = num_sms();
   const long k32 = (K + 31) / 32;
@@ -1234,7 +1237,7 @@ TilePlan plan_tiles(int M, int N, int K, int batch, bool x3, int max_ks, int for
       const int rows = pair ? 2 * BM : BM;
       const long tiles = (long)ceil_div(M, rows) * ceil_div(N, bn) * batch;
       const long slots = pair ? sms / 2 : sms;
-      for (int ks = 1; ks <= (pair ? 1 : max_ks); ks++) {
+      for (int ks = 1; ks <= max_ks; ks++) {
         if (ks > 1 && tiles * (ks - 1) >= slots) break;  // already a full wave without this split
         const long units = tiles * ks;
         const long rounds = (units + slots - 1) / slots;
@@ -1315,7 +1318,7 @@ int gemm_tf32(cudaStream_t stream, int M, int N, int K, int batch, const GemmOpe
     plan.pair = false;
   }
   const int BN = plan.bn;
-  const int kt_total = ceil_div(K, BK);
+  const int kt_total = ceil_div(K, plan.pair ? PairShape<64>::BK : BK);
   const int ks = force_splits > 0 ? force_splits : plan.ks;
   la.kt_per = ceil_div(kt_total, ks);
   la.ks = ceil_div(kt_total, la.kt_per);
