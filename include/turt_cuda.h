@@ -87,6 +87,14 @@ int turt_fused_ce(turt_ctx* ctx, float* logits, const uint32_t* targets, float* 
                   float gscale);
 int turt_fused_adamw_clip(turt_ctx* ctx, float* p, const float* g, float* m, float* v, size_t n, float lr, float b1,
                           float b2, float eps, float wd, float bc1, float bc2, float clip, double* norm_out);
+/* Corpus window gather of the pretraining data feed (sampleBatch, scripts/gpu-pretrain.ts:57-68):
+ * for i < b, j < t: ids[i*t + j] = tokens[starts[i] + j], targets[i*t + j] = tokens[starts[i] +
+ * j + 1].  tokens: device uint16 corpus of n_tokens; starts: HOST uint64[b] (copied in order on
+ * the context's stream), each at most n_tokens - t - 1 (a start beyond that raises
+ * TURT_ERR_RANGE at the next synchronization and its window is left unwritten); ids / targets:
+ * device uint32[b*t]. */
+int turt_sample_windows(turt_ctx* ctx, const uint16_t* tokens, size_t n_tokens, const uint64_t* starts, int b, int t,
+                        uint32_t* ids, uint32_t* targets);
 
 /* ------------------------------------------------------------------ buffers
  * GpuEngine.buffer / free / reclaim / read / fill / tensor / indexBuffer,
@@ -201,6 +209,17 @@ int turt_param_info(turt_model* model, int index, char* name, int name_cap, int*
 int turt_param_upload(turt_model* model, int index, const float* host, size_t n);
 int turt_param_download(turt_model* model, int index, float* host, size_t n);
 int turt_grad_download(turt_model* model, int index, float* host, size_t n);
+/* Sets every parameter as the reference's CPU constructor GPT(config, mulberry32(seed)) does
+ * (src/models/gpt.ts:225-239 with nn/linear.ts:20-22, math/tensor.ts:83-88,
+ * math/random.ts:8-25): N(0, 0.02) weights drawn in parameters() order, residual projections
+ * scaled by 1/sqrt(2 nLayer), unit gains, zero biases.  scripts/gpu-pretrain.ts seeds its GPU
+ * model this way (seed 1337).  The draws run on the host. */
+int turt_model_init(turt_model* model, uint32_t seed);
+/* AdamW first / second moments of one parameter, same layout and sizes as the parameter.  No
+ * reference counterpart: scripts/gpu-pretrain.ts keeps m and v in device buffers only and
+ * restarts them at zero on --resume (:171-173); these let a checkpoint carry them. */
+int turt_adam_state_download(turt_model* model, int index, float* m, float* v, size_t n);
+int turt_adam_state_upload(turt_model* model, int index, const float* m, const float* v, size_t n);
 /* zeroGrad on every parameter (gpu-gpt usage: scripts/gpu-pretrain.ts:502). */
 int turt_zero_grad(turt_model* model);
 /* GpuGPT.loss + backward (gpu-gpt.ts:185-201, autograd.ts:1196-1209): accumulates
@@ -218,6 +237,11 @@ int turt_read_loss(turt_model* model, float* loss_out);
 int turt_launch_count(uint64_t* count);
 /* Forward only (evaluation loss), gpu-pretrain.ts:485-497. */
 int turt_forward(turt_model* model, const uint32_t* ids, const uint32_t* targets, int b, int t, float* loss_out);
+/* turt_forward with ids / targets already in device memory (uint32[b*t] each); synchronizes
+ * to return the mean loss.  The pretraining eval loss (scripts/gpu-pretrain.ts:188-200) runs it
+ * on device-sampled validation windows. */
+int turt_forward_device(turt_model* model, const uint32_t* ids, const uint32_t* targets, int b, int t,
+                        float* loss_out);
 /* clipGradNorm (src/optim/clip.ts:7-24) over all gradients; norm_out may be NULL. */
 int turt_clip_grad_norm(turt_model* model, double max_norm, double* norm_out);
 /* AdamW over every parameter (one fused pass over the flat buffers), autograd.ts:516-531 with

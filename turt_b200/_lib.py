@@ -42,7 +42,8 @@ class TurtConfig(C.Structure):
                 ("n_embd", C.c_int), ("arch", C.c_int), ("hidden", C.c_int)]
 
 
-_SCALARS = {"int": C.c_int, "size_t": C.c_size_t, "float": C.c_float, "double": C.c_double}
+_SCALARS = {"int": C.c_int, "size_t": C.c_size_t, "float": C.c_float, "double": C.c_double,
+            "uint16_t": C.c_uint16, "uint32_t": C.c_uint32, "uint64_t": C.c_uint64}
 
 
 def _ctype(decl: str):

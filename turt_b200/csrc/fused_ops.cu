@@ -43,6 +43,21 @@ __global__ void k_swiglu_bwd_tail(const float* a, const float* u, const float* d
   da[i] = d[i] * u[i] * (s + sl * (1.0f - s));
 }
 
+// One block per window; threads stride over its t positions.
+__global__ void k_sample_windows(const uint16_t* __restrict__ tokens, size_t n_tokens, const uint64_t* __restrict__ starts,
+                                 int t, uint32_t* __restrict__ ids, uint32_t* __restrict__ tgt, int* flags) {
+  const int i = blockIdx.x;
+  const uint64_t s = starts[i];
+  if (s + (uint64_t)t + 1 > n_tokens) {
+    if (threadIdx.x == 0) atomicExch(&flags[FLAG_RANGE], 1);
+    return;
+  }
+  for (int j = threadIdx.x; j < t; j += blockDim.x) {
+    ids[(size_t)i * t + j] = tokens[s + j];
+    tgt[(size_t)i * t + j] = tokens[s + j + 1];
+  }
+}
+
 int scratch(turt_ctx* ctx, size_t bytes, void** out) {
   if (ctx->scratch_bytes < bytes) {
     if (ctx->scratch) {
@@ -139,4 +154,18 @@ extern "C" int turt_fused_adamw_clip(turt_ctx* ctx, float* p, const float* g, fl
     }
   }
   return adamw_flat(ctx->stream, p, g, m, v, n, lr, b1, b2, eps, wd, bc1, bc2, 1.0f, coef);
+}
+
+extern "C" int turt_sample_windows(turt_ctx* ctx, const uint16_t* tokens, size_t n_tokens, const uint64_t* starts,
+                                   int b, int t, uint32_t* ids, uint32_t* targets) {
+  FCTX(ctx);
+  TURT_REQUIRE(tokens && starts && ids && targets, "sample_windows: null buffer");
+  TURT_REQUIRE(b > 0 && t > 0 && n_tokens > (size_t)t + 1, "sample_windows: corpus shorter than one window");
+  void* d_starts = nullptr;
+  RC(scratch(ctx, (size_t)b * 8, &d_starts));
+  TURT_CHECK_CUDA(cudaMemcpyAsync(d_starts, starts, (size_t)b * 8, cudaMemcpyHostToDevice, ctx->stream));
+  k_sample_windows<<<b, 256, 0, ctx->stream>>>(tokens, n_tokens, static_cast<const uint64_t*>(d_starts), t, ids,
+                                                targets, ctx->flags);
+  TURT_LAUNCH_CHECK();
+  return OK;
 }

@@ -17,6 +17,7 @@
 // [0, head_end) and each layer are contiguous ranges for the gradient all-reduce.
 #include <math.h>
 
+#include <cmath>
 #include <string>
 
 #include "attention.cuh"
@@ -647,16 +648,21 @@ int turt_param_info(turt_model* m, int i, char* name, int cap, int* shape2, int*
   return OK;
 }
 
-static int copy_param(turt_model* m, int i, float* host, size_t n, bool up, bool grad) {
+// Which flat buffer a per-parameter copy addresses.
+enum ParamBuf { BUF_PARAM = 0, BUF_GRAD = 1, BUF_ADAM_M = 2, BUF_ADAM_V = 3 };
+
+static int copy_param(turt_model* m, int i, float* host, size_t n, bool up, int which) {
   MODEL_GUARD(m);
   TURT_REQUIRE(i >= 0 && i < (int)m->params.size(), "param index out of range");
+  TURT_REQUIRE(host, "null host array");
   const ParamSlot& s = m->params[i];
   if (n != s.count()) {
     set_error("param " + std::to_string(i) + " size mismatch: expected " + std::to_string(s.count()) + ", got " +
               std::to_string(n));
     return ERR_INVALID;
   }
-  float* dev = (grad ? m->G : m->P) + s.off;
+  float* base = which == BUF_GRAD ? m->G : which == BUF_ADAM_M ? m->M : which == BUF_ADAM_V ? m->V : m->P;
+  float* dev = base + s.off;
   cudaStream_t st = m->ctx->stream;
   if (up)
     TURT_CHECK_CUDA(cudaMemcpy2DAsync(dev, (size_t)s.pitch * 4, host, (size_t)s.width * 4, (size_t)s.width * 4, s.rows,
@@ -669,10 +675,65 @@ static int copy_param(turt_model* m, int i, float* host, size_t n, bool up, bool
 }
 
 int turt_param_upload(turt_model* m, int i, const float* host, size_t n) {
-  return copy_param(m, i, const_cast<float*>(host), n, true, false);
+  return copy_param(m, i, const_cast<float*>(host), n, true, BUF_PARAM);
 }
-int turt_param_download(turt_model* m, int i, float* host, size_t n) { return copy_param(m, i, host, n, false, false); }
-int turt_grad_download(turt_model* m, int i, float* host, size_t n) { return copy_param(m, i, host, n, false, true); }
+int turt_param_download(turt_model* m, int i, float* host, size_t n) {
+  return copy_param(m, i, host, n, false, BUF_PARAM);
+}
+int turt_grad_download(turt_model* m, int i, float* host, size_t n) { return copy_param(m, i, host, n, false, BUF_GRAD); }
+int turt_adam_state_download(turt_model* m, int i, float* mom1, float* mom2, size_t n) {
+  RC(copy_param(m, i, mom1, n, false, BUF_ADAM_M));
+  return copy_param(m, i, mom2, n, false, BUF_ADAM_V);
+}
+int turt_adam_state_upload(turt_model* m, int i, const float* mom1, const float* mom2, size_t n) {
+  RC(copy_param(m, i, const_cast<float*>(mom1), n, true, BUF_ADAM_M));
+  return copy_param(m, i, const_cast<float*>(mom2), n, true, BUF_ADAM_V);
+}
+
+// mulberry32 (src/math/random.ts:8-17): the uint32 state advances by 0x6d2b79f5 and is
+// mixed by two wrapping multiplies; the draw is the mixed word / 2^32.
+static double mulberry32_next(uint32_t* state) {
+  *state += 0x6d2b79f5u;
+  uint32_t t = *state;
+  t = (t ^ (t >> 15)) * (t | 1u);
+  t ^= t + (t ^ (t >> 7)) * (t | 61u);
+  return (double)(t ^ (t >> 14)) / 4294967296.0;
+}
+
+// Box-Muller over mulberry32, redrawing u while it is 0 (src/math/random.ts:20-25).
+static double gaussian_next(uint32_t* state) {
+  double u = 0.0;
+  while (u == 0.0) u = mulberry32_next(state);
+  const double v = mulberry32_next(state);
+  return std::sqrt(-2.0 * std::log(u)) * std::cos(2.0 * M_PI * v);
+}
+
+// The reference's CPU constructor GPT(config, rng) draws, in parameters() order, every weight
+// matrix as Float32(gaussian(rng) * std) (Tensor.randn, src/math/tensor.ts:83-88): std 0.02
+// (INIT_STD) for wte, wpe, q, k, v, gate, up, fc and 0.02 / sqrt(2 nLayer) for the residual
+// projections proj, down, mp (src/models/gpt.ts:97-102,154-155,182-184,225-239); norm gains
+// are 1 and biases 0 (no draws).  The draws run on the host, then each tensor is uploaded.
+int turt_model_init(turt_model* m, uint32_t seed) {
+  MODEL_GUARD(m);
+  uint32_t state = seed;
+  const double std0 = 0.02, std_res = 0.02 / std::sqrt(2.0 * m->cfg.n_layer);
+  std::vector<float> buf;
+  for (int i = 0; i < (int)m->params.size(); i++) {
+    const ParamSlot& s = m->params[i];
+    const std::string& n = s.name;
+    const std::string leaf = n.substr(n.rfind('.') + 1);
+    buf.assign(s.count(), 0.0f);
+    if (s.ndim == 2) {
+      const bool residual = leaf == "projW" || leaf == "downW" || leaf == "mpW";
+      const double sd = residual ? std_res : std0;
+      for (size_t j = 0; j < buf.size(); j++) buf[j] = (float)(gaussian_next(&state) * sd);
+    } else if (leaf.back() == 'g') {
+      std::fill(buf.begin(), buf.end(), 1.0f);  // norm gain
+    }
+    RC(copy_param(m, i, buf.data(), buf.size(), true, BUF_PARAM));
+  }
+  return OK;
+}
 
 int turt_zero_grad(turt_model* m) {
   MODEL_GUARD(m);
@@ -714,6 +775,18 @@ int turt_forward(turt_model* m, const uint32_t* ids, const uint32_t* tgt, int b,
   RC(check_batch(m, ids, tgt, b, t));
   RC(ensure_workspace(m, b, t));
   RC(stage_tokens(m, ids, tgt, b * t));
+  RC(forward(m, b, t, false, 1.0f));
+  return read_loss(m, loss_out);
+}
+
+int turt_forward_device(turt_model* m, const uint32_t* d_ids, const uint32_t* d_tgt, int b, int t, float* loss_out) {
+  MODEL_GUARD(m);
+  RC(check_batch(m, d_ids, d_tgt, b, t));
+  TURT_REQUIRE(loss_out, "null loss_out");
+  RC(ensure_workspace(m, b, t));
+  cudaStream_t st = m->ctx->stream;
+  TURT_CHECK_CUDA(cudaMemcpyAsync(m->d_ids, d_ids, (size_t)b * t * 4, cudaMemcpyDeviceToDevice, st));
+  TURT_CHECK_CUDA(cudaMemcpyAsync(m->d_tgt, d_tgt, (size_t)b * t * 4, cudaMemcpyDeviceToDevice, st));
   RC(forward(m, b, t, false, 1.0f));
   return read_loss(m, loss_out);
 }

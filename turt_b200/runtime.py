@@ -141,6 +141,43 @@ class Model:
     def params_flat(self) -> np.ndarray:
         return self._download_flat(lib().turt_param_download)
 
+    def init_reference(self, seed: int) -> None:
+        """Weights exactly as the reference's CPU GPT(config, mulberry32(seed)) draws them."""
+        check(lib().turt_model_init(self._h, seed & 0xFFFFFFFF))
+
+    def param_list(self):
+        """Every parameter, in parameters() order, as arrays of the reference's shapes."""
+        out = []
+        for i, shp in enumerate(self.shapes):
+            a = np.empty(int(np.prod(shp)), dtype=np.float32)
+            check(lib().turt_param_download(self._h, i, ptr(a), a.size))
+            out.append(a.reshape(shp))
+        return out
+
+    def load_param_list(self, arrays) -> None:
+        for i, (a, shp) in enumerate(zip(arrays, self.shapes)):
+            a = np.ascontiguousarray(a, dtype=np.float32).reshape(-1)
+            if a.size != int(np.prod(shp)):
+                raise ValueError(f"param {i} has {a.size} values, the model expects shape {shp}")
+            check(lib().turt_param_upload(self._h, i, ptr(a), a.size))
+
+    def adam_state(self):
+        """AdamW first and second moments per parameter ([m...], [v...])."""
+        ms, vs = [], []
+        for i, shp in enumerate(self.shapes):
+            m = np.empty(int(np.prod(shp)), dtype=np.float32)
+            v = np.empty_like(m)
+            check(lib().turt_adam_state_download(self._h, i, ptr(m), ptr(v), m.size))
+            ms.append(m.reshape(shp))
+            vs.append(v.reshape(shp))
+        return ms, vs
+
+    def load_adam_state(self, ms, vs) -> None:
+        for i, (m, v) in enumerate(zip(ms, vs)):
+            m = np.ascontiguousarray(m, dtype=np.float32).reshape(-1)
+            v = np.ascontiguousarray(v, dtype=np.float32).reshape(-1)
+            check(lib().turt_adam_state_upload(self._h, i, ptr(m), ptr(v), m.size))
+
     def grads_flat(self) -> np.ndarray:
         return self._download_flat(lib().turt_grad_download)
 
@@ -163,6 +200,12 @@ class Model:
     def read_loss(self) -> float:
         loss = C.c_float()
         check(lib().turt_read_loss(self._h, C.byref(loss)))
+        return loss.value
+
+    def forward_device(self, d_ids: int, d_targets: int, b: int, t: int) -> float:
+        """Mean loss of a forward pass on device-resident ids / targets (synchronizes)."""
+        loss = C.c_float()
+        check(lib().turt_forward_device(self._h, d_ids, d_targets, b, t, C.byref(loss)))
         return loss.value
 
     def forward(self, ids, targets, b: int, t: int) -> float:
