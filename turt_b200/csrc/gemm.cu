@@ -179,30 +179,51 @@ __device__ __forceinline__ void epi_chunk(const GemmEpi& epi, const EpiVec& vec,
     } break;
     case EPI_SWIGLU_BWD: {
       // v = d(act) for hidden units [col0, col0+32); pre-activations and outputs are interleaved.
+      // Two 16-column halves (float4 accesses on full chunks) keep the live registers low.
       const long ic = (long)(col0 / kGluBlock) * (2 * kGluBlock);
       const float* pg = epi.R + row * epi.ldr + ic;
       float* o = epi.C + row * epi.ldc + ic;
+      const bool full = n >= 32 && vec.R && vec.C;
 #pragma unroll
-      for (int j0 = 0; j0 < 32; j0 += 8) {
-        float g[8], u[8], dg[8], du[8];
+      for (int h0 = 0; h0 < 32; h0 += 16) {
+        float g[16], u[16];
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-          g[j] = j0 + j < n ? pg[j0 + j] : 0.0f;
-          u[j] = j0 + j < n ? pg[kGluBlock + j0 + j] : 0.0f;
-        }
+        for (int j = 0; j < 16; j += 4) {
+          if (full) {
+            const float4 a = *reinterpret_cast<const float4*>(pg + h0 + j);
+            const float4 b = *reinterpret_cast<const float4*>(pg + kGluBlock + h0 + j);
+            g[j] = a.x, g[j + 1] = a.y, g[j + 2] = a.z, g[j + 3] = a.w;
+            u[j] = b.x, u[j + 1] = b.y, u[j + 2] = b.z, u[j + 3] = b.w;
+          } else {
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-          const float s = sigmoid_f(g[j]);
-          const float sl = g[j] * s;
-          du[j] = v[j0 + j] * sl;
-          dg[j] = v[j0 + j] * u[j] * (s + sl * (1.0f - s));
-        }
-#pragma unroll
-        for (int j = 0; j < 8; j++)
-          if (j0 + j < n) {
-            o[j0 + j] = dg[j];
-            o[kGluBlock + j0 + j] = du[j];
+            for (int q = 0; q < 4; q++) {
+              g[j + q] = h0 + j + q < n ? pg[h0 + j + q] : 0.0f;
+              u[j + q] = h0 + j + q < n ? pg[kGluBlock + h0 + j + q] : 0.0f;
+            }
           }
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+          const float sg = sigmoid_f(g[j]);
+          const float sl = g[j] * sg;
+          const float dv = v[h0 + j];
+          g[j] = dv * u[j] * (sg + sl * (1.0f - sg));  // d(gate)
+          u[j] = dv * sl;                              // d(up)
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+          if (full) {
+            *reinterpret_cast<float4*>(o + h0 + j) = make_float4(g[j], g[j + 1], g[j + 2], g[j + 3]);
+            *reinterpret_cast<float4*>(o + kGluBlock + h0 + j) = make_float4(u[j], u[j + 1], u[j + 2], u[j + 3]);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+              if (h0 + j + q < n) {
+                o[h0 + j + q] = g[j + q];
+                o[kGluBlock + h0 + j + q] = u[j + q];
+              }
+          }
+        }
       }
     } break;
     case EPI_QKV_ROPE: {
