@@ -177,55 +177,6 @@ __device__ __forceinline__ void epi_chunk(const GemmEpi& epi, const EpiVec& vec,
       for (int j = 0; j < 32; j++) v[j] *= gelu_grad_f(z[j]);
       st32(dst, v, n, vec.C);
     } break;
-    case EPI_SWIGLU_BWD: {
-      // v = d(act) for hidden units [col0, col0+32); pre-activations and outputs are interleaved.
-      // Two 16-column halves (float4 accesses on full chunks) keep the live registers low.
-      const long ic = (long)(col0 / kGluBlock) * (2 * kGluBlock);
-      const float* pg = epi.R + row * epi.ldr + ic;
-      float* o = epi.C + row * epi.ldc + ic;
-      const bool full = n >= 32 && vec.R && vec.C;
-#pragma unroll
-      for (int h0 = 0; h0 < 32; h0 += 16) {
-        float g[16], u[16];
-#pragma unroll
-        for (int j = 0; j < 16; j += 4) {
-          if (full) {
-            const float4 a = *reinterpret_cast<const float4*>(pg + h0 + j);
-            const float4 b = *reinterpret_cast<const float4*>(pg + kGluBlock + h0 + j);
-            g[j] = a.x, g[j + 1] = a.y, g[j + 2] = a.z, g[j + 3] = a.w;
-            u[j] = b.x, u[j + 1] = b.y, u[j + 2] = b.z, u[j + 3] = b.w;
-          } else {
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-              g[j + q] = h0 + j + q < n ? pg[h0 + j + q] : 0.0f;
-              u[j + q] = h0 + j + q < n ? pg[kGluBlock + h0 + j + q] : 0.0f;
-            }
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < 16; j++) {
-          const float sg = sigmoid_f(g[j]);
-          const float sl = g[j] * sg;
-          const float dv = v[h0 + j];
-          g[j] = dv * u[j] * (sg + sl * (1.0f - sg));  // d(gate)
-          u[j] = dv * sl;                              // d(up)
-        }
-#pragma unroll
-        for (int j = 0; j < 16; j += 4) {
-          if (full) {
-            *reinterpret_cast<float4*>(o + h0 + j) = make_float4(g[j], g[j + 1], g[j + 2], g[j + 3]);
-            *reinterpret_cast<float4*>(o + kGluBlock + h0 + j) = make_float4(u[j], u[j + 1], u[j + 2], u[j + 3]);
-          } else {
-#pragma unroll
-            for (int q = 0; q < 4; q++)
-              if (h0 + j + q < n) {
-                o[h0 + j + q] = g[j + q];
-                o[kGluBlock + h0 + j + q] = u[j + q];
-              }
-          }
-        }
-      }
-    } break;
     case EPI_QKV_ROPE: {
       const int hd = epi.rope_hd, H = epi.rope_H, T = epi.rope_T, E = H * hd;
       const int sec = col0 / E;  // 0 q, 1 k, 2 v (E is a multiple of 32: a chunk never straddles)

@@ -14,7 +14,6 @@ enum EpiKind : int {
   EPI_BIAS = 4,        // C = acc + bias[n]
   EPI_BIAS_GELU = 5,   // C = acc + bias[n] (pre-activation), C2 = gelu(C)
   EPI_SWIGLU_FWD = 6,  // C = acc (interleaved gate|up pre-activations), C2 = silu(gate) * up
-  EPI_SWIGLU_BWD = 7,  // acc = d(act); R = interleaved gate|up pre-acts; C = interleaved d(gate)|d(up)
   EPI_GELU_BWD = 8,    // C = acc * gelu'(R)
   EPI_QKV_ROPE = 9,    // acc = fused q|k|v projection of token `row`: q, k rotated (RoPE) into the
                        // head-major qr / kr [B*H][T][hd]; v stored into C (columns [2E, 3E))

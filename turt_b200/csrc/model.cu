@@ -202,6 +202,7 @@ int ensure_workspace(turt_model* m, int B, int T) {
   size_t dx = take(NE), dy = take(NE), datt = take(NE), dqkv = take(3 * NE), dpre = take((size_t)N * W1);
   size_t Dsc = take(BHT);
   size_t dS = tc ? take((size_t)S_need) : 0;
+  size_t dact = rope ? take((size_t)N * h) : 0;
   const int C = 3 * E > W1 ? 3 * E : W1;
   size_t part = take((size_t)2 * norm_parts(N) * (C > E ? C : E));
   size_t ids = take(N), tgt = take(N);
@@ -244,6 +245,7 @@ int ensure_workspace(turt_model* m, int B, int T) {
   m->dpre = F(dpre);
   m->Dsc = F(Dsc);
   m->dS = tc ? F(dS) : nullptr;
+  m->dact = rope ? F(dact) : nullptr;
   m->part = F(part);
   m->d_ids = reinterpret_cast<uint32_t*>(base + ids);
   m->d_tgt = reinterpret_cast<uint32_t*>(base + tgt);
@@ -414,10 +416,10 @@ int backward(turt_model* m, int B, int T) {
     // ---- MLP
     RC(wait_mark(1));  // dpre is rewritten below; the previous layer's dW1 reads it
     if (m->modern) {
-      GemmEpi e = epi(EPI_SWIGLU_BWD, m->dpre, 2 * h);
-      e.R = a.pre;
-      e.ldr = 2 * h;
-      RC(gemm_tf32(st, N, h, E, 1, opK(m->dx, E), opK(P + L.w2, E), e, flags, mp(m)));
+      // d(act) = dx W2^T, then the coalesced elementwise SwiGLU backward into dpre (a fused
+      // epilogue reads and writes the gate|up rows one row per lane and measured slower)
+      RC(gemm_tf32(st, N, h, E, 1, opK(m->dx, E), opK(P + L.w2, E), epi(EPI_STORE, m->dact, h), flags, mp(m)));
+      RC(swiglu_bwd_interleaved(st, m->dact, a.pre, m->dpre, N, h));
       RC(fork());
       RC(gemm_tf32(wg, h, E, N, 1, opMN(a.act, h), opMN(m->dx, E), epi(EPI_ACCUM, G + L.w2, E), flags, mp(m)));
       RC(set_mark(0));

@@ -322,6 +322,37 @@ __global__ void k_colsum_parts(const float* __restrict__ g, int rows, int C, flo
   part[(size_t)c * gridDim.y + blockIdx.y] = s;
 }
 
+// SwiGLU backward over the interleaved gate|up layout (kGluBlock = 32: columns [64j, 64j+32)
+// gate units [32j, 32j+32), [64j+32, 64j+64) the matching up units): from d(act) [N][h] and the
+// pre-activations [N][2h], s = sigmoid(gate): d(up) = dact * gate * s,
+// d(gate) = dact * up * (s + gate*s*(1 - s)) (SILU_BWD, autograd.ts:1044-1054, and the product
+// rule).  One thread per float4 of d(act); consecutive threads read consecutive 16-byte pieces.
+__global__ void __launch_bounds__(256) k_swiglu_bwd_il(const float* __restrict__ dact, const float* __restrict__ pre,
+                                                       float* __restrict__ dpre, long N, int h) {
+  const int h4 = h / 4;
+  const long total = N * h4;
+  for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (long)gridDim.x * blockDim.x) {
+    const long n = e / h4;
+    const int u = (int)(e % h4) * 4;                // hidden unit
+    const long gi = n * 2L * h + (u / 32) * 64 + u % 32;  // gate column; up is 32 further
+    const float4 d = reinterpret_cast<const float4*>(dact)[e];
+    const float4 g = *reinterpret_cast<const float4*>(pre + gi);
+    const float4 v = *reinterpret_cast<const float4*>(pre + gi + 32);
+    float4 dg, du;
+#define SWIL(c)                                  \
+  {                                              \
+    const float sg = sigmoid_f(g.c);             \
+    const float sl = g.c * sg;                   \
+    du.c = d.c * sl;                             \
+    dg.c = d.c * v.c * (sg + sl * (1.0f - sg));  \
+  }
+    SWIL(x) SWIL(y) SWIL(z) SWIL(w)
+#undef SWIL
+    *reinterpret_cast<float4*>(dpre + gi) = dg;
+    *reinterpret_cast<float4*>(dpre + gi + 32) = du;
+  }
+}
+
 // -------------------------------------------------- fused softmax + cross-entropy
 // One block per row of logits[N][V]: per-row loss (CE_FWD, autograd.ts:441-454) and the
 // gradient (CE_BWD, :455-471) written in place over the logits: one HBM read, one write.
@@ -689,6 +720,15 @@ int colsum_accum(cudaStream_t st, const float* g, int rows, int C, float* out_ac
   k_colsum_parts<<<grid, 128, 0, st>>>(g, rows, C, part);
   TURT_LAUNCH_CHECK();
   k_reduce_parts<<<ceil_div(C, 8), 256, 0, st>>>(part, nb, C, out_accum);
+  TURT_LAUNCH_CHECK();
+  return OK;
+}
+int swiglu_bwd_interleaved(cudaStream_t st, const float* dact, const float* pre, float* dpre, int N, int h) {
+  TURT_REQUIRE(h % 32 == 0, "swiglu backward: hidden width must be a multiple of 32");
+  const long total = (long)N * (h / 4);
+  long blocks = (total + 255) / 256;
+  if (blocks > 148L * 16) blocks = 148L * 16;
+  k_swiglu_bwd_il<<<(int)blocks, 256, 0, st>>>(dact, pre, dpre, N, h);
   TURT_LAUNCH_CHECK();
   return OK;
 }

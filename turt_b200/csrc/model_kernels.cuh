@@ -18,6 +18,8 @@ int ln_fwd(cudaStream_t st, const float* x, const float* g, const float* b, floa
 int ln_bwd(cudaStream_t st, const float* x, const float* dy, const float* g, const float* mean, const float* rstd,
            const float* dres, float* dx, float* dg_accum, float* db_accum, float* part, int rows, int E);
 int colsum_accum(cudaStream_t st, const float* g, int rows, int C, float* out_accum, float* part);
+// SwiGLU backward: d(act) [N][h] and interleaved gate|up pre-activations [N][2h] -> interleaved grads.
+int swiglu_bwd_interleaved(cudaStream_t st, const float* dact, const float* pre, float* dpre, int N, int h);
 int ce_fused(cudaStream_t st, float* logits, const uint32_t* tgt, float* loss_rows, int N, int V, float gscale,
              int* flags);
 int ce_loss(cudaStream_t st, const float* logits, const uint32_t* tgt, float* loss_rows, int N, int V, int* flags);
