@@ -159,7 +159,7 @@ def run_reference(args, w, rank: int) -> None:
 # ----------------------------------------------------------------------------- GPU arm
 def init_weights(model, w, seed: int):
     """N(0, 0.02) weights, residual projections scaled by 1/sqrt(2L), unit gains, zero biases
-    (src/models/gpt.ts:124-129,181-182,209-211)."""
+    (src/models/gpt.ts:97-102,154-155,182-184)."""
     import numpy as np
     rng = np.random.default_rng(seed)
     parts = []

@@ -185,7 +185,7 @@ typedef struct turt_config {
   int n_head;
   int n_embd;
   int arch;   /* TURT_ARCH_GPT2 or TURT_ARCH_MODERN */
-  int hidden; /* MLP width; 0 = mlpHidden(config) (gpt.ts:96-99) */
+  int hidden; /* MLP width; 0 = mlpHidden(config) (gpt.ts:69-72) */
 } turt_config;
 
 int turt_model_create(turt_ctx* ctx, const turt_config* cfg, turt_model** out);
@@ -242,6 +242,15 @@ int turt_forward(turt_model* model, const uint32_t* ids, const uint32_t* targets
  * on device-sampled validation windows. */
 int turt_forward_device(turt_model* model, const uint32_t* ids, const uint32_t* targets, int b, int t,
                         float* loss_out);
+/* Generation with a KV cache, the forward half of GPT.generate (src/models/gpt.ts:291-321).
+ * prefill runs the forward over t <= block_size host token ids (one sequence), refills the
+ * per-layer key / value cache and writes the last position's logits (V floats, host).  step
+ * appends token `id` at position `pos` (which must equal the number of cached positions, and
+ * be < block_size) and writes its logits.  When the context outgrows the block, the caller
+ * prefills the cropped window again, as the reference's per-token forward over
+ * ids.slice(-blockSize) does.  Both synchronize. */
+int turt_generate_prefill(turt_model* model, const uint32_t* ids, int t, float* logits_out);
+int turt_generate_step(turt_model* model, uint32_t id, int pos, float* logits_out);
 /* clipGradNorm (src/optim/clip.ts:7-24) over all gradients; norm_out may be NULL. */
 int turt_clip_grad_norm(turt_model* model, double max_norm, double* norm_out);
 /* AdamW over every parameter (one fused pass over the flat buffers), autograd.ts:516-531 with

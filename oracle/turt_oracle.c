@@ -21,7 +21,7 @@
  *   - src/math/tensor.ts:607-700     gelu (tanh approx), silu, rope (interleaved pairs)
  *   - src/math/tensor.ts:708-745     crossEntropyLogits
  *   - src/nn/rmsnorm.ts:24-27, src/nn/layernorm.ts:20-26  composite norms
- *   - src/models/gpt.ts:96-305       mlpHidden, attention, MLPs, Block, GPT init order + tied head
+ *   - src/models/gpt.ts:69-283       mlpHidden, attention, MLPs, Block, GPT init order + tied head
  *   - src/optim/adam.ts:31-54, src/optim/clip.ts:7-24    AdamW step, global-norm clip
  *   - scripts/train-gpt.ts:105-123,200-242, scripts/params.ts   DP shard / weighted mean
  *
@@ -540,7 +540,7 @@ typedef struct {
 static gcfg read_cfg(const int* c) {
   gcfg g = {c[0], c[1], c[2], c[3], c[4], c[5], c[6]};
   if (g.hid <= 0) {
-    /* mlpHidden, src/models/gpt.ts:96-99 (Math.round == floor(x + 0.5) for x > 0) */
+    /* mlpHidden, src/models/gpt.ts:69-72 (Math.round == floor(x + 0.5) for x > 0) */
     g.hid = g.modern ? (int)fmax(64.0, floor((8.0 * g.E) / 3.0 / 64.0 + 0.5) * 64.0) : 4 * g.E;
   }
   return g;
@@ -556,7 +556,7 @@ typedef struct {
   boff b[256];
 } moff;
 
-/* parameters() order: src/models/gpt.ts:252-266 + src/nn/module.ts:13-35 field walk
+/* parameters() order: src/models/gpt.ts:225-239 + src/nn/module.ts:13-35 field walk
    (identical to src/models/gpu-gpt.ts:118-132). */
 static void layout(const gcfg* c, moff* o) {
   size_t p = 0;
@@ -663,7 +663,7 @@ EXPORT int oc_param_shapes(const int* cfg, int* shapes) {
   return k;
 }
 
-/* GPT constructor init, src/models/gpt.ts:252-266 with Linear (src/nn/linear.ts:18-23):
+/* GPT constructor init, src/models/gpt.ts:225-239 with Linear (src/nn/linear.ts:18-23):
    wte, [wpe], then per block q,k,v,proj, then gate,up,down | fc,proj.  Gains 1, biases 0. */
 EXPORT void oc_init_state(const int* cfg, uint32_t* state, real* params);
 EXPORT void oc_init(const int* cfg, uint32_t seed, real* params) {
@@ -731,7 +731,7 @@ typedef struct {
 
 #define ALLOC(n) ((real*)calloc((size_t)(n), sizeof(real)))
 
-/* x[N,E] -> heads [G,T,hd] (reshape/permute/reshape, gpt.ts:133-138). */
+/* x[N,E] -> heads [G,T,hd] (reshape/permute/reshape, gpt.ts:105-110). */
 static void split_heads(const real* x, real* out, int b, int t, int H, int hd) {
   int E = H * hd;
   for (int bi = 0; bi < b; bi++)
@@ -740,7 +740,7 @@ static void split_heads(const real* x, real* out, int b, int t, int H, int hd) {
         memcpy(out + (((size_t)bi * H + h) * t + ti) * hd, x + ((size_t)bi * t + ti) * E + (size_t)h * hd,
                sizeof(real) * hd);
 }
-/* heads [G,T,hd] -> x[N,E] (gpt.ts:162-166) */
+/* heads [G,T,hd] -> x[N,E] (gpt.ts:135-139) */
 static void merge_heads(const real* in, real* x, int b, int t, int H, int hd) {
   int E = H * hd;
   for (int bi = 0; bi < b; bi++)
@@ -793,7 +793,7 @@ static double gpt_run(const int* cfg, const real* params, real* grads, const int
   layer_act* A = (layer_act*)calloc(c.L, sizeof(layer_act));
   real* x = ALLOC((size_t)N * E);
   real* pos = NULL;
-  /* embeddings (gpt.ts:289-296) */
+  /* embeddings (gpt.ts:262-270) */
   oc_gather_fwd(params + o.wte, ids, x, N, V, E);
   int32_t* pids = NULL;
   if (!c.modern) {
@@ -823,7 +823,7 @@ static double gpt_run(const int* cfg, const real* params, real* grads, const int
       a->c1 = ALLOC((size_t)N * E);
       ln_fwd(x, params + bo->ln1g, params + bo->ln1b, a->y1, N, E, eps, a->c1, a->xn1, a->r1);
     }
-    /* attention (gpt.ts:140-169) */
+    /* attention (gpt.ts:112-141) */
     a->q = ALLOC((size_t)G * t * hd);
     a->k = ALLOC((size_t)G * t * hd);
     a->v = ALLOC((size_t)G * t * hd);
@@ -865,7 +865,7 @@ static double gpt_run(const int* cfg, const real* params, real* grads, const int
     a->s1 = ALLOC((size_t)N * hidn);
     real* xo = ALLOC((size_t)N * E);
     if (c.modern) {
-      /* SwiGLU, gpt.ts:214-219 */
+      /* SwiGLU, gpt.ts:187-192 */
       a->a2 = ALLOC((size_t)N * hidn);
       a->hid = ALLOC((size_t)N * hidn);
       oc_mm_fwd(a->y2, params + bo->gateW, a->a1, N, E, hidn);
@@ -874,7 +874,7 @@ static double gpt_run(const int* cfg, const real* params, real* grads, const int
       for (size_t i = 0; i < (size_t)N * hidn; i++) a->hid[i] = R((double)a->s1[i] * a->a2[i]);
       oc_mm_fwd(a->hid, params + bo->downW, tmpN, N, hidn, E);
     } else {
-      /* GeluMLP, gpt.ts:185-190 */
+      /* GeluMLP, gpt.ts:158-163 */
       linear_fwd(a->y2, params + bo->fcW, params + bo->fcb, a->a1, N, E, hidn);
       oc_gelu_fwd(a->a1, a->s1, (size_t)N * hidn);
       linear_fwd(a->s1, params + bo->mpW, params + bo->mpb, tmpN, N, hidn, E);
@@ -882,7 +882,7 @@ static double gpt_run(const int* cfg, const real* params, real* grads, const int
     for (size_t i = 0; i < (size_t)N * E; i++) xo[i] = R((double)a->h[i] + tmpN[i]);
     x = xo;
   }
-  /* final norm + tied head + CE (gpt.ts:300-310) */
+  /* final norm + tied head + CE (gpt.ts:271-283) */
   real* yf = ALLOC((size_t)N * E);
   real* xnf = ALLOC((size_t)N * E);
   real* rf = ALLOC(N);
@@ -1221,7 +1221,7 @@ EXPORT double oc_loss_grad(const int* cfg, const real* params, real* grads, cons
   return gpt_run(cfg, params, grads, ids, tgt, b, t, err, NULL);
 }
 
-/* GPT.forward logits [b*t, V] (gpt.ts:280-305). */
+/* GPT.forward logits [b*t, V] (gpt.ts:253-276). */
 EXPORT int oc_logits(const int* cfg, const real* params, const int32_t* ids, int b, int t, real* logits_out) {
   int N = b * t, err = 0;
   int32_t* tg = (int32_t*)calloc(N, sizeof(int32_t));
@@ -1230,7 +1230,7 @@ EXPORT int oc_logits(const int* cfg, const real* params, const int32_t* ids, int
   return err;
 }
 
-/* GPT.generate + sampleFromLogits, src/models/gpt.ts:318-368.  topk <= 0 disables top-k.
+/* GPT.generate + sampleFromLogits, src/models/gpt.ts:291-341.  topk <= 0 disables top-k.
    out receives prompt followed by the sampled ids; returns the number written. */
 EXPORT int oc_generate(const int* cfg, const real* params, const int32_t* prompt, int n_prompt, int max_new,
                        double temperature, int topk, uint32_t* rng_state, int32_t* out) {

@@ -35,7 +35,7 @@ size_t align64(size_t x) { return (x + 63) & ~size_t(63); }
 int mlp_hidden(const turt_config& c) {
   if (c.hidden > 0) return c.hidden;
   if (c.arch == TURT_ARCH_GPT2) return 4 * c.n_embd;
-  // Math.max(64, Math.round((8 * nEmbd) / 3 / 64) * 64), src/models/gpt.ts:96-99
+  // Math.max(64, Math.round((8 * nEmbd) / 3 / 64) * 64), src/models/gpt.ts:69-72
   double v = floor((8.0 * c.n_embd) / 3.0 / 64.0 + 0.5) * 64.0;
   return (int)(v < 64 ? 64 : v);
 }
@@ -285,7 +285,7 @@ int stage_tokens(turt_model* m, const uint32_t* ids, const uint32_t* tgt, int N)
   return OK;
 }
 
-int forward(turt_model* m, int B, int T, bool train, float loss_scale) {
+int forward(turt_model* m, int B, int T, bool train, float loss_scale, bool logits_only = false) {
   cudaStream_t st = m->ctx->stream;
   int* flags = m->ctx->flags;
   const int N = B * T, E = m->cfg.n_embd, H = m->cfg.n_head, hd = E / H, V = m->cfg.vocab_size, h = m->hid;
@@ -353,6 +353,7 @@ int forward(turt_model* m, int B, int T, bool train, float loss_scale) {
     RC(ln_fwd(st, m->xL, P + m->lnfg, P + m->lnfb, m->yf, m->muf, m->rsf, N, E, m->eps));
   // tied head: logits = yf * wte^T (wte [V][E] is the K-major B operand)
   RC(gemm_tf32(st, N, V, E, 1, opK(m->yf, E), opK(P + m->wte, E), epi(EPI_STORE, m->logits, V), flags, mp(m)));
+  if (logits_only) return OK;
   if (train)
     RC(ce_fused(st, m->logits, m->d_tgt, m->loss_rows, N, V, loss_scale / (float)N, flags));
   else
@@ -508,6 +509,13 @@ int check_batch(turt_model* m, const uint32_t* ids, const uint32_t* tgt, int b, 
 
 }  // namespace
 
+int turt::model_forward_logits(turt_model* m, const uint32_t* ids, int t) {
+  RC(check_batch(m, ids, ids, 1, t));
+  RC(ensure_workspace(m, 1, t));
+  RC(stage_tokens(m, ids, ids, t));
+  return forward(m, 1, t, false, 1.0f, true);
+}
+
 #define MODEL_GUARD(m)                                   \
   do {                                                   \
     if (!(m)) {                                          \
@@ -614,6 +622,9 @@ int turt_model_destroy(turt_model* m) {
   cudaFree(m->coef_dev);
   cudaFree(m->norm_dev);
   cudaFree(m->norm_scratch);
+  if (m->kcache) cudaFree(m->kcache);
+  if (m->vcache) cudaFree(m->vcache);
+  if (m->dec) cudaFree(m->dec);
   cudaFreeHost(m->h_loss);
   if (m->h_ids) cudaFreeHost(m->h_ids);
   if (m->h_tgt) cudaFreeHost(m->h_tgt);

@@ -76,9 +76,17 @@ struct turt_model {
   cudaEvent_t wg_ring[16] = {};
   cudaEvent_t wg_mark[4] = {};
   int wg_next = 0;
+  // Generation: KV cache [n_layer][n_head][block_size][head_dim] (k RoPE-rotated), the number of
+  // positions it holds, and the decode-step vectors.
+  float *kcache = nullptr, *vcache = nullptr, *dec = nullptr;
+  size_t dec_floats = 0;
+  int dec_len = 0;
 };
 
 namespace turt {
+// Logits-only forward of one sequence (b = 1) of t host token ids; logits land in m->logits and
+// every layer's activations (qkv, rotated q / k copies) in the workspace.
+int model_forward_logits(turt_model* m, const uint32_t* ids, int t);
 // Makes stream `to` wait for everything issued so far on stream `from`.
 int stream_join(turt_model* m, cudaStream_t from, cudaStream_t to);
 // The stream whose completion implies every gradient write issued so far (joins the

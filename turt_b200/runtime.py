@@ -214,6 +214,20 @@ class Model:
         check(lib().turt_forward(self._h, ptr(ids), ptr(targets), b, t, C.byref(loss)))
         return loss.value
 
+    def generate_prefill(self, ids) -> np.ndarray:
+        """Forward over one context of <= block_size token ids; refills the KV cache and returns
+        the last position's logits (float32 [vocab])."""
+        ids = u32(ids)
+        out = np.empty(self.cfg.vocab_size, dtype=np.float32)
+        check(lib().turt_generate_prefill(self._h, ptr(ids), len(ids), ptr(out)))
+        return out
+
+    def generate_step(self, token: int, pos: int) -> np.ndarray:
+        """Appends `token` at `pos` (= the cached length) and returns its logits."""
+        out = np.empty(self.cfg.vocab_size, dtype=np.float32)
+        check(lib().turt_generate_step(self._h, int(token), int(pos), ptr(out)))
+        return out
+
     def clip_grad_norm(self, max_norm: float) -> float:
         n = C.c_double()
         check(lib().turt_clip_grad_norm(self._h, max_norm, C.byref(n)))
