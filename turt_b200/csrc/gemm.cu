@@ -89,7 +89,59 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
 // ------------------------------------------------------------ epilogue
+// tcgen05.ld gives one epilogue lane one accumulator row (32 consecutive columns per load).
+// Stored lane by lane, every warp store would touch 32 rows with 16 bytes each; instead each
+// warp turns its 32 x 32 chunk around in a private shared-memory tile, 16 columns at a time,
+// so that a warp access covers 8 rows x 64 contiguous bytes.  The tile pitch of 20 floats
+// keeps both the row-wise float4 writes and the column-group float4 reads free of bank
+// conflicts (each 8-lane phase hits 8 distinct 4-bank groups).
+constexpr int kEpiPitch = 20;
+constexpr int kEpiTileFloats = 32 * kEpiPitch;
+constexpr int kEpiStageBytes = 4 * kEpiTileFloats * 4;  // four epilogue warps
+
+struct EpiVec {
+  bool C, R, C2;
+};
+
+__device__ __forceinline__ void st4(float* p, float4 x, int nv, bool vec) {
+  if (vec && nv == 4) {
+    *reinterpret_cast<float4*>(p) = x;
+  } else {
+    p[0] = x.x;
+    if (nv > 1) p[1] = x.y;
+    if (nv > 2) p[2] = x.z;
+    if (nv > 3) p[3] = x.w;
+  }
+}
+
+__device__ __forceinline__ float4 ld4(const float* p, int nv, bool vec) {
+  if (vec && nv == 4) return *reinterpret_cast<const float4*>(p);
+  return make_float4(p[0], nv > 1 ? p[1] : 0.f, nv > 2 ? p[2] : 0.f, nv > 3 ? p[3] : 0.f);
+}
+
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+  return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+
+__device__ __forceinline__ float4 bias4(const float* bias, int col, int nv) {
+  return make_float4(bias[col], nv > 1 ? bias[col + 1] : 0.f, nv > 2 ? bias[col + 2] : 0.f,
+                     nv > 3 ? bias[col + 3] : 0.f);
+}
+
 // One epilogue lane owns one accumulator row; `v` holds 32 consecutive columns of it.
 __device__ __forceinline__ void st32(float* dst, const float* v, int n, bool vec) {
   if (vec && n >= 32) {
@@ -117,10 +169,6 @@ __device__ __forceinline__ void ld32(const float* src, float* v, int n, bool vec
     for (int j = 0; j < 32; j++) v[j] = j < n ? src[j] : 0.0f;
   }
 }
-
-struct EpiVec {
-  bool C, R, C2;
-};
 
 // Columns [col0, col0 + 32) of one output row (every kind except the fused SwiGLU forward).
 __device__ __forceinline__ void epi_chunk(const GemmEpi& epi, const EpiVec& vec, float* v, float* Cb, long row,
@@ -212,6 +260,175 @@ __device__ __forceinline__ void epi_chunk(const GemmEpi& epi, const EpiVec& vec,
     } break;
     default:
       break;
+  }
+}
+
+// Hands the lane's row v[0..n) of a 16-column group to fn(x, row, col, nv) as float4 groups in
+// the coalesced order: fn sees columns [col, col + nv) of `row` (nv <= 4), rows < M only.
+template <typename F>
+__device__ __forceinline__ void half_t(float* tile, int lane, const float* v, long rowbase, int M, int col0, int n,
+                                       F&& fn) {
+  __syncwarp();
+  float4* tr = reinterpret_cast<float4*>(tile + lane * kEpiPitch);
+#pragma unroll
+  for (int j = 0; j < 4; j++) tr[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  __syncwarp();
+#pragma unroll
+  for (int p = 0; p < 4; p++) {
+    const int r = 8 * p + (lane & 7), c = 4 * (lane >> 3);
+    const float4 x = *reinterpret_cast<const float4*>(tile + r * kEpiPitch + c);
+    const long row = rowbase + r;
+    const int nv = min(4, n - c);
+    if (row < M && nv > 0) fn(x, row, col0 + c, nv);
+  }
+}
+
+// The same for a 32-column chunk (two 16-column groups).
+template <typename F>
+__device__ __forceinline__ void chunk_t(float* tile, int lane, const float* v, long rowbase, int M, int col0, int n,
+                                        F&& fn) {
+  half_t(tile, lane, v, rowbase, M, col0, n, fn);
+  if (n > 16) half_t(tile, lane, v + 16, rowbase, M, col0 + 16, n - 16, fn);
+}
+
+// Columns [col, col + nv) of one output row, every kind except the fused SwiGLU forward.
+__device__ __forceinline__ void epi_quad(const GemmEpi& epi, const EpiVec& vec, float4 x, float* Cb, long row, int col,
+                                         int nv, long cboff) {
+  float* dst = Cb + row * epi.ldc + col;
+  switch (epi.kind) {
+    case EPI_STORE:
+      st4(dst, x, nv, vec.C);
+      break;
+    case EPI_ACCUM:
+      st4(dst, add4(x, ld4(dst, nv, vec.C)), nv, vec.C);
+      break;
+    case EPI_RED:
+      if (vec.C && nv == 4) {
+        atomicAdd(reinterpret_cast<float4*>(dst), x);
+      } else {
+        atomicAdd(dst, x.x);
+        if (nv > 1) atomicAdd(dst + 1, x.y);
+        if (nv > 2) atomicAdd(dst + 2, x.z);
+        if (nv > 3) atomicAdd(dst + 3, x.w);
+      }
+      break;
+    case EPI_ADD_RES:
+      x = add4(x, ld4(epi.R + cboff + row * epi.ldr + col, nv, vec.R));
+      if (epi.bias) x = add4(x, bias4(epi.bias, col, nv));
+      st4(dst, x, nv, vec.C);
+      break;
+    case EPI_BIAS:
+    case EPI_BIAS_GELU:
+      x = add4(x, bias4(epi.bias, col, nv));
+      st4(dst, x, nv, vec.C);
+      if (epi.kind == EPI_BIAS_GELU)
+        st4(epi.C2 + row * epi.ldc2 + col, make_float4(gelu_f(x.x), gelu_f(x.y), gelu_f(x.z), gelu_f(x.w)), nv,
+            vec.C2);
+      break;
+    case EPI_GELU_BWD: {
+      const float4 z = ld4(epi.R + row * epi.ldr + col, nv, vec.R);
+      x = make_float4(x.x * gelu_grad_f(z.x), x.y * gelu_grad_f(z.y), x.z * gelu_grad_f(z.z), x.w * gelu_grad_f(z.w));
+      st4(dst, x, nv, vec.C);
+    } break;
+    case EPI_QKV_ROPE: {
+      // E and the head dim are multiples of 16: a group of 4 never straddles q / k / v or heads
+      const int hd = epi.rope_hd, H = epi.rope_H, T = epi.rope_T, E = H * hd;
+      const int sec = col / E;  // 0 q, 1 k, 2 v
+      if (sec == 2) {
+        st4(dst, x, nv, vec.C);
+        break;
+      }
+      float* base = sec == 0 ? epi.qr : epi.kr;
+      const int t = (int)(row % T);
+      const long b = row / T;
+      const int c = col - sec * E, h = c / hd, d = c % hd;
+      const float2 c0 = epi.rope[(long)t * (hd / 2) + d / 2], c1 = epi.rope[(long)t * (hd / 2) + d / 2 + 1];
+      *reinterpret_cast<float4*>(base + ((b * H + h) * T + t) * hd + d) =
+          make_float4(x.x * c0.x - x.y * c0.y, x.x * c0.y + x.y * c0.x, x.z * c1.x - x.w * c1.y,
+                      x.z * c1.y + x.w * c1.x);
+    } break;
+    case EPI_STORE_UNROPE: {
+      // rows are positions (one head per batch entry); (col, col + 1), (col + 2, col + 3) are pairs
+      const int hd = epi.rope_hd;
+      const float2 c0 = epi.rope[row * (hd / 2) + col / 2], c1 = epi.rope[row * (hd / 2) + col / 2 + 1];
+      x = make_float4(x.x * c0.x + x.y * c0.y, -x.x * c0.y + x.y * c0.x, x.z * c1.x + x.w * c1.y,
+                      -x.z * c1.y + x.w * c1.x);
+      st4(dst, x, nv, vec.C);
+    } break;
+    default:
+      break;
+  }
+}
+
+// One accumulator tile of an epilogue warp: 32 rows from `rowbase`, columns [n0, n0 + BN).
+// `tile` != nullptr selects the shared-memory-transposed stores (8 rows x 64 B per warp
+// access); otherwise each lane stores its own row.  Measured on B200: the transposed stores
+// win when the epilogue overlaps a long mainloop (they disturb it less), the row stores when
+// the epilogue itself is the critical path (short K).
+template <int BN, bool T>
+__device__ __forceinline__ void epi_tile(const GemmEpi& epi, const EpiVec& vec, float* tile, int lane,
+                                         uint32_t tbase, long rowbase, int M, int N, int n0, float* Cb, long cboff) {
+  const long row = rowbase + lane;
+  if (!T) tile = nullptr;
+  if (epi.kind == EPI_SWIGLU_FWD) {
+    // Chunk pairs (gate, up): C keeps both pre-activations, C2 gets silu(gate) * up.
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; c += 2) {
+      const int col0 = n0 + c * 32;
+      if (col0 >= N) break;  // warp-uniform
+      const int nu = min(32, N - col0 - 32);
+      if (!tile) {
+        float g[32], v[32];
+        tmem_ld32(tbase + c * 32, g);
+        tmem_ld32(tbase + (c + 1) * 32, v);
+        if (row < M) {
+          st32(Cb + row * epi.ldc + col0, g, min(32, N - col0), vec.C);
+          st32(Cb + row * epi.ldc + col0 + 32, v, nu, vec.C);
+#pragma unroll
+          for (int j = 0; j < 32; j++) v[j] *= g[j] * sigmoid_f(g[j]);
+          st32(epi.C2 + row * epi.ldc2 + col0 / 2, v, nu, vec.C2);
+        }
+        continue;
+      }
+      const bool vc = vec.C, vc2 = vec.C2;
+      const long ldc = epi.ldc, ldc2 = epi.ldc2;
+      float* C2 = epi.C2;
+      auto to_c = [&](float4 x, long r, int col, int nv) { st4(Cb + r * ldc + col, x, nv, vc); };
+      {
+        float g[32];
+        tmem_ld32(tbase + c * 32, g);
+        chunk_t(tile, lane, g, rowbase, M, col0, min(32, N - col0), to_c);
+      }
+      {
+        float v[32];
+        tmem_ld32(tbase + (c + 1) * 32, v);
+        chunk_t(tile, lane, v, rowbase, M, col0 + 32, nu, to_c);
+      }
+      // silu(gate) * up, 16 columns at a time (TMEM is re-read: it is cheaper than registers)
+#pragma unroll 1
+      for (int h = 0; h < 32 && h < nu; h += 16) {
+        float g[16], v[16];
+        tmem_ld16(tbase + c * 32 + h, g);
+        tmem_ld16(tbase + (c + 1) * 32 + h, v);
+#pragma unroll
+        for (int j = 0; j < 16; j++) v[j] *= g[j] * sigmoid_f(g[j]);
+        half_t(tile, lane, v, rowbase, M, col0 / 2 + h, nu - h,
+               [&](float4 x, long r, int col, int nv) { st4(C2 + r * ldc2 + col, x, nv, vc2); });
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; c++) {
+      const int col0 = n0 + c * 32;
+      if (col0 >= N) break;  // warp-uniform
+      float v[32];
+      tmem_ld32(tbase + c * 32, v);
+      if (tile)
+        chunk_t(tile, lane, v, rowbase, M, col0, min(32, N - col0),
+                [&](float4 x, long r, int col, int nv) { epi_quad(epi, vec, x, Cb, r, col, nv, cboff); });
+      else if (row < M)
+        epi_chunk(epi, vec, v, Cb, row, col0, min(32, N - col0), cboff);
+    }
   }
 }
 
@@ -483,36 +700,9 @@ __global__ void __launch_bounds__(GemmShape<BN, BK, X3, MINB>::THREADS, MINB)
         break;
       }
       tc_fence_after();
-      const long row = m0 + q * 32 + lane;
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       const long cboff = (long)(b % bdiv) * epi.strideC + (long)(b / bdiv) * epi.strideC_hi;
-      float* Cb = epi.C + cboff;
-      if (epi.kind == EPI_SWIGLU_FWD) {
-        // Chunk pairs (gate, up): C keeps both pre-activations, C2 gets silu(gate) * up.
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; c += 2) {
-          const int col0 = n0 + c * 32;
-          float g[32], v[32];
-          tmem_ld32(tbase + c * 32, g);
-          tmem_ld32(tbase + (c + 1) * 32, v);
-          if (row < M && col0 < N) {
-            st32(Cb + row * epi.ldc + col0, g, min(32, N - col0), vec.C);
-            st32(Cb + row * epi.ldc + col0 + 32, v, min(32, N - col0 - 32), vec.C);
-#pragma unroll
-            for (int j = 0; j < 32; j++) v[j] *= g[j] * sigmoid_f(g[j]);
-            st32(epi.C2 + row * epi.ldc2 + col0 / 2, v, min(32, N - col0 - 32), vec.C2);
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; c++) {
-          const int col0 = n0 + c * 32;
-          if (col0 >= N) break;  // warp-uniform
-          float v[32];
-          tmem_ld32(tbase + c * 32, v);
-          if (row < M) epi_chunk(epi, vec, v, Cb, row, col0, min(32, N - col0), cboff);
-        }
-      }
+      epi_tile<BN, false>(epi, vec, nullptr, lane, tbase, m0 + q * 32, M, N, n0, epi.C + cboff, cboff);
       // hand the accumulator back to the MMA issuer
       tc_fence_before();
       __syncwarp();
@@ -611,9 +801,12 @@ struct PairShape {
   static constexpr int MN_BOX = 32 * BK * 4;
   static constexpr int THREADS = 352;
   static constexpr uint32_t TMEM_COLS = 2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512);
-  static constexpr int STAGES_FIT = (232448 - 1024 - 512) / STAGE_BYTES;
+  // Transposed-store tiles only where they cost no pipeline stage (BN = 256: 3 stages either way).
+  static constexpr int EPI_BYTES = BN == 256 ? kEpiStageBytes : 0;
+  static constexpr int STAGES_FIT = (232448 - 1024 - 512 - EPI_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 512;
+  // stages | barriers (512 B) | epilogue tiles, plus 1 KB of alignment slack
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 512 + EPI_BYTES;
 };
 
 template <int BN, bool A_MN, bool B_MN>
@@ -874,6 +1067,10 @@ __global__ void __launch_bounds__(352, 1)
   } else {
     // -------------------------------------------------- epilogue warps (2..5, both CTAs)
     const int q = warp & 3;
+    // transposed stores when the tiles exist and the mainloop is long (>= 8 k-steps per unit)
+    float* tile = (S::EPI_BYTES && kt_per_split >= 8)
+                      ? reinterpret_cast<float*>(smem + STAGES * S::STAGE_BYTES + 512) + q * kEpiTileFloats
+                      : nullptr;
     const EpiVec vec{(epi.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(epi.C) & 15) == 0) && (epi.strideC % 4 == 0) &&
                          (epi.strideC_hi % 4 == 0),
                      epi.R && (epi.ldr % 4 == 0) && ((reinterpret_cast<uintptr_t>(epi.R) & 15) == 0),
@@ -889,35 +1086,10 @@ __global__ void __launch_bounds__(352, 1)
         break;
       }
       tc_fence_after();
-      const long row = m0 + (int)rank * BM + q * 32 + lane;
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       const long cboff = (long)(b % bdiv) * epi.strideC + (long)(b / bdiv) * epi.strideC_hi;
-      float* Cb = epi.C + cboff;
-      if (epi.kind == EPI_SWIGLU_FWD) {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; c += 2) {
-          const int col0 = n0 + c * 32;
-          float g[32], v[32];
-          tmem_ld32(tbase + c * 32, g);
-          tmem_ld32(tbase + (c + 1) * 32, v);
-          if (row < M && col0 < N) {
-            st32(Cb + row * epi.ldc + col0, g, min(32, N - col0), vec.C);
-            st32(Cb + row * epi.ldc + col0 + 32, v, min(32, N - col0 - 32), vec.C);
-#pragma unroll
-            for (int j = 0; j < 32; j++) v[j] *= g[j] * sigmoid_f(g[j]);
-            st32(epi.C2 + row * epi.ldc2 + col0 / 2, v, min(32, N - col0 - 32), vec.C2);
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; c++) {
-          const int col0 = n0 + c * 32;
-          if (col0 >= N) break;
-          float v[32];
-          tmem_ld32(tbase + c * 32, v);
-          if (row < M) epi_chunk(epi, vec, v, Cb, row, col0, min(32, N - col0), cboff);
-        }
-      }
+      epi_tile<BN, (S::EPI_BYTES > 0)>(epi, vec, tile, lane, tbase, m0 + (int)rank * BM + q * 32, M, N, n0,
+                                       epi.C + cboff, cboff);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
