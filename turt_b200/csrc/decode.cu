@@ -20,12 +20,14 @@ namespace {
 
 // Decode-step vectors carved from turt_model::dec.
 struct DecBufs {
-  float *x, *y, *qkv, *att, *h, *pre, *act, *logits, *rstd, *mean, *part;
+  float *x, *y, *qkv, *att, *h, *pre, *act, *logits, *rstd, *mean, *part, *apart;
   size_t part_floats;
 };
 
 constexpr int kGemvCols = 128;  // columns per block (32 lanes x float4)
 constexpr int kGemvRows = 64;   // K rows per block (8 warps x 8)
+constexpr int kAttnWarps = 8;   // decode attention: warps per block
+constexpr int kAttnSplits = 8;  // decode attention: position slices per head
 
 DecBufs dec_bufs(turt_model* m) {
   const int E = m->cfg.n_embd, h = m->hid, V = m->cfg.vocab_size;
@@ -48,6 +50,7 @@ DecBufs dec_bufs(turt_model* m) {
   d.logits = take(V);
   d.rstd = take(16);
   d.mean = take(16);
+  d.apart = take((size_t)kAttnSplits * (E + 2 * m->cfg.n_head));
   d.part_floats = (size_t)((maxK + kGemvRows - 1) / kGemvRows) * maxN;
   d.part = take(d.part_floats);
   return d;
@@ -59,15 +62,17 @@ size_t dec_floats_needed(turt_model* m) {
   const int maxN = std::max(std::max(3 * E, W1), E), maxK = std::max(E, h);
   size_t n = 0;
   for (size_t k : {(size_t)E, (size_t)E, (size_t)3 * E, (size_t)E, (size_t)E, (size_t)W1, (size_t)h, (size_t)V,
-                   (size_t)16, (size_t)16, (size_t)((maxK + kGemvRows - 1) / kGemvRows) * maxN})
+                   (size_t)16, (size_t)16, (size_t)kAttnSplits * (E + 2 * m->cfg.n_head),
+                   (size_t)((maxK + kGemvRows - 1) / kGemvRows) * maxN})
     n += (k + 63) & ~size_t(63);
   return n;
 }
 
-// x = wte[id] (+ wpe[pos]), the embedding of one token.
-__global__ void k_dec_embed(const float* __restrict__ wte, const float* __restrict__ wpe, uint32_t id, int pos,
+// x = wte[id] (+ wpe[pos]) of the token in the device cell tok = {id, pos}.
+__global__ void k_dec_embed(const float* __restrict__ wte, const float* __restrict__ wpe, const int* __restrict__ tok,
                             float* __restrict__ x, int E) {
-  for (int c = threadIdx.x; c < E; c += blockDim.x) x[c] = wte[(size_t)id * E + c] + (wpe ? wpe[(size_t)pos * E + c] : 0.0f);
+  const size_t id = (uint32_t)tok[0], pos = tok[1];
+  for (int c = threadIdx.x; c < E; c += blockDim.x) x[c] = wte[id * E + c] + (wpe ? wpe[pos * E + c] : 0.0f);
 }
 
 // GEMV, first stage: part[ks][n] = sum over K rows [64 ks, 64 ks + 64) of a[k] W[k][n].  A block
@@ -156,9 +161,9 @@ int gemv(cudaStream_t st, const DecBufs& d, const float* a, const float* W, int 
 }
 
 // q, k of the new token rotated at `pos` (RoPE, interleaved pairs); k and v appended to the cache.
-__global__ void k_dec_qkv_post(float* __restrict__ qkv, const float2* __restrict__ cs, int pos, int H, int hd,
-                               int rope, float* __restrict__ kc, float* __restrict__ vc, int Tc) {
-  const int E = H * hd;
+__global__ void k_dec_qkv_post(float* __restrict__ qkv, const float2* __restrict__ cs, const int* __restrict__ tok,
+                               int H, int hd, int rope, float* __restrict__ kc, float* __restrict__ vc, int Tc) {
+  const int E = H * hd, pos = tok[1];
   for (int i = threadIdx.x; i < E / 2; i += blockDim.x) {
     const int c = 2 * i, hh = c / hd, d = c % hd;
     float q0 = qkv[c], q1 = qkv[c + 1], k0 = qkv[E + c], k1 = qkv[E + c + 1];
@@ -178,47 +183,89 @@ __global__ void k_dec_qkv_post(float* __restrict__ qkv, const float2* __restrict
   }
 }
 
-// One block per head: softmax(scale * q . k_j) over cached positions j <= pos, then sum_j p_j v_j.
-__global__ void k_dec_attn(const float* __restrict__ qkv, const float* __restrict__ kc, const float* __restrict__ vc,
-                           int pos, int hd, int Tc, float scale, float* __restrict__ out) {
-  extern __shared__ float sh[];  // [Tc] probabilities, [hd] q
+// Attention of the new token, split over positions (flash-decoding): block (head, s) takes the
+// s-th of kAttnSplits slices of the cached positions j <= pos and writes its running max m,
+// sum l = sum_j exp(score_j - m) and unnormalised output o = sum_j exp(score_j - m) v_j;
+// k_dec_attn_merge combines the slices in a fixed order.  Inside a block each warp takes every
+// 8th position, lanes across the head dim, so every key / value row is one coalesced read.
+__global__ void __launch_bounds__(kAttnWarps * 32) k_dec_attn(const float* __restrict__ qkv, const float* __restrict__ kc,
+                                                              const float* __restrict__ vc, const int* __restrict__ tok,
+                                                              int hd, int Tc, float scale, float* __restrict__ part) {
+  extern __shared__ float sh[];  // [slice] probabilities, [hd] q, [kAttnWarps][hd] partial outputs
+  __shared__ float red[kAttnWarps];
+  const int hh = blockIdx.x, sp = blockIdx.y, n = tok[1] + 1, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int per = (n + kAttnSplits - 1) / kAttnSplits, j0 = sp * per, j1 = min(n, j0 + per);
+  const int cap = (Tc + kAttnSplits - 1) / kAttnSplits;
   float* pr = sh;
-  float* q = sh + Tc;
-  __shared__ float red[32];
-  const int hh = blockIdx.x, n = pos + 1;
+  float* q = sh + cap;
+  float* po = q + hd;
+  float* out = part + ((size_t)hh * kAttnSplits + sp) * (hd + 2);  // [m, l, o[hd]]
   const float* K = kc + (size_t)hh * Tc * hd;
   const float* V = vc + (size_t)hh * Tc * hd;
   for (int d = threadIdx.x; d < hd; d += blockDim.x) q[d] = qkv[hh * hd + d];
   __syncthreads();
   float mx = -INFINITY;
-  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+  for (int j = j0 + w; j < j1; j += kAttnWarps) {
     float s = 0.f;
-    for (int d = 0; d < hd; d++) s += q[d] * K[(size_t)j * hd + d];
-    s *= scale;
-    pr[j] = s;
+    for (int d = lane; d < hd; d += 32) s += q[d] * K[(size_t)j * hd + d];
+    s = warp_sum(s) * scale;
+    if (lane == 0) pr[j - j0] = s;
     mx = fmaxf(mx, s);
   }
-  mx = warp_max(mx);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  if (lane == 0) red[w] = mx;
   __syncthreads();
-  mx = -INFINITY;
-  for (int w = 0; w < (int)(blockDim.x >> 5); w++) mx = fmaxf(mx, red[w]);
+  mx = red[0];
+  for (int i = 1; i < kAttnWarps; i++) mx = fmaxf(mx, red[i]);
   __syncthreads();
   float sum = 0.f;
-  for (int j = threadIdx.x; j < n; j += blockDim.x) {
-    const float e = expf(pr[j] - mx);
-    pr[j] = e;
+  for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
+    const float e = expf(pr[j - j0] - mx);
+    pr[j - j0] = e;
     sum += e;
   }
   sum = warp_sum(sum);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+  if (lane == 0) red[w] = sum;
   __syncthreads();
-  sum = 0.f;
-  for (int w = 0; w < (int)(blockDim.x >> 5); w++) sum += red[w];
-  const float inv = 1.0f / sum;
+  for (int d0 = 0; d0 < hd; d0 += 32) {
+    const int d = d0 + lane;
+    if (d < hd) {
+      float o = 0.f;
+      for (int j = j0 + w; j < j1; j += kAttnWarps) o += pr[j - j0] * V[(size_t)j * hd + d];
+      po[w * hd + d] = o;
+    }
+  }
+  __syncthreads();
   for (int d = threadIdx.x; d < hd; d += blockDim.x) {
     float o = 0.f;
-    for (int j = 0; j < n; j++) o += pr[j] * V[(size_t)j * hd + d];
+    for (int i = 0; i < kAttnWarps; i++) o += po[i * hd + d];
+    out[2 + d] = o;
+  }
+  if (threadIdx.x == 0) {
+    float l = 0.f;
+    for (int i = 0; i < kAttnWarps; i++) l += red[i];
+    out[0] = mx;  // -inf for an empty slice (l = 0, o = 0)
+    out[1] = l;
+  }
+}
+
+// out[h][d] = sum_s exp(m_s - M) o_s[d] / sum_s exp(m_s - M) l_s, slices in order.
+__global__ void k_dec_attn_merge(const float* __restrict__ part, int hd, float* __restrict__ out) {
+  const int hh = blockIdx.x;
+  const float* p = part + (size_t)hh * kAttnSplits * (hd + 2);
+  float M = -INFINITY;
+  for (int i = 0; i < kAttnSplits; i++) M = fmaxf(M, p[i * (hd + 2)]);
+  float L = 0.f;
+  for (int i = 0; i < kAttnSplits; i++) {
+    const float m = p[i * (hd + 2)];
+    if (m > -INFINITY) L += expf(m - M) * p[i * (hd + 2) + 1];
+  }
+  const float inv = 1.0f / L;
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float o = 0.f;
+    for (int i = 0; i < kAttnSplits; i++) {
+      const float m = p[i * (hd + 2)];
+      if (m > -INFINITY) o += expf(m - M) * p[i * (hd + 2) + 2 + d];
+    }
     out[hh * hd + d] = o * inv;
   }
 }
@@ -277,6 +324,10 @@ __global__ void k_cache_fill(const float* __restrict__ qkv, const float* __restr
   }
 }
 
+size_t attn_smem(int Tc, int hd) {
+  return (size_t)((Tc + kAttnSplits - 1) / kAttnSplits + hd + kAttnWarps * hd) * 4;
+}
+
 int ensure_decode(turt_model* m) {
   if (m->kcache) return OK;
   const size_t cache = (size_t)m->cfg.n_layer * m->cfg.block_size * m->cfg.n_embd;
@@ -284,6 +335,79 @@ int ensure_decode(turt_model* m) {
   TURT_CHECK_CUDA(cudaMalloc(&m->vcache, cache * 4));
   m->dec_floats = dec_floats_needed(m);
   TURT_CHECK_CUDA(cudaMalloc(&m->dec, m->dec_floats * 4));
+  TURT_CHECK_CUDA(cudaMalloc(&m->dec_tok, 2 * sizeof(int)));
+  TURT_CHECK_CUDA(cudaMallocHost(&m->h_dec_tok, 2 * sizeof(int)));
+  TURT_CHECK_CUDA(cudaStreamCreateWithFlags(&m->dec_cap, cudaStreamNonBlocking));
+  return OK;
+}
+
+// Every kernel of one decode step on stream `st`; the token and its position come from
+// m->dec_tok.  Returns the number of kernels enqueued in *launches.
+int enqueue_step(turt_model* m, cudaStream_t st, int* launches) {
+  const int E = m->cfg.n_embd, H = m->cfg.n_head, hd = E / H, h = m->hid, V = m->cfg.vocab_size;
+  const int Tc = m->cfg.block_size, W1 = m->modern ? 2 * h : h;
+  const float* P = m->P;
+  const DecBufs d = dec_bufs(m);
+  const size_t per_layer = (size_t)Tc * E;
+  const float scale = 1.0f / sqrtf((float)hd);
+  int n = 0;
+  k_dec_embed<<<1, 256, 0, st>>>(P + m->wte, m->modern ? nullptr : P + m->wpe, m->dec_tok, d.x, E);
+  TURT_LAUNCH_CHECK();
+  n++;
+  for (int l = 0; l < m->cfg.n_layer; l++) {
+    const LayerOff& L = m->layers[l];
+    if (m->modern)
+      RC(rms_fwd(st, d.x, P + L.ln1g, d.y, d.rstd, 1, E, m->eps));
+    else
+      RC(ln_fwd(st, d.x, P + L.ln1g, P + L.ln1b, d.y, d.mean, d.rstd, 1, E, m->eps));
+    RC(gemv(st, d, d.y, P + L.wqkv, 3 * E, E, 3 * E, m->modern ? nullptr : P + L.bqkv, nullptr, d.qkv));
+    k_dec_qkv_post<<<1, 256, 0, st>>>(d.qkv, m->rope_cs, m->dec_tok, H, hd, m->modern ? 1 : 0,
+                                      m->kcache + l * per_layer, m->vcache + l * per_layer, Tc);
+    TURT_LAUNCH_CHECK();
+    k_dec_attn<<<dim3(H, kAttnSplits), kAttnWarps * 32, attn_smem(Tc, hd), st>>>(
+        d.qkv, m->kcache + l * per_layer, m->vcache + l * per_layer, m->dec_tok, hd, Tc, scale, d.apart);
+    TURT_LAUNCH_CHECK();
+    k_dec_attn_merge<<<H, 64, 0, st>>>(d.apart, hd, d.att);
+    TURT_LAUNCH_CHECK();
+    RC(gemv(st, d, d.att, P + L.wproj, E, E, E, m->modern ? nullptr : P + L.bproj, d.x, d.h));
+    if (m->modern)
+      RC(rms_fwd(st, d.h, P + L.ln2g, d.y, d.rstd, 1, E, m->eps));
+    else
+      RC(ln_fwd(st, d.h, P + L.ln2g, P + L.ln2b, d.y, d.mean, d.rstd, 1, E, m->eps));
+    RC(gemv(st, d, d.y, P + L.w1, W1, E, W1, m->modern ? nullptr : P + L.b1, nullptr, d.pre));
+    k_dec_act<<<(h + 255) / 256, 256, 0, st>>>(d.pre, d.act, h, m->modern ? 1 : 0);
+    TURT_LAUNCH_CHECK();
+    RC(gemv(st, d, d.act, P + L.w2, E, h, E, m->modern ? nullptr : P + L.b2, d.h, d.x));
+    n += 14;
+  }
+  if (m->modern)
+    RC(rms_fwd(st, d.x, P + m->lnfg, d.y, d.rstd, 1, E, m->eps));
+  else
+    RC(ln_fwd(st, d.x, P + m->lnfg, P + m->lnfb, d.y, d.mean, d.rstd, 1, E, m->eps));
+  k_dec_logits<<<(V + 7) / 8, 256, 0, st>>>(d.y, P + m->wte, V, E, d.logits);
+  TURT_LAUNCH_CHECK();
+  *launches = n + 2;
+  return OK;
+}
+
+// Captures enqueue_step into m->dec_graph (on a private stream: capture needs one that is not
+// the legacy default stream).
+int capture_step(turt_model* m) {
+  cudaGraph_t g = nullptr;
+  int n = 0;
+  TURT_CHECK_CUDA(cudaStreamBeginCapture(m->dec_cap, cudaStreamCaptureModeThreadLocal));
+  const int rc = enqueue_step(m, m->dec_cap, &n);
+  const cudaError_t ce = cudaStreamEndCapture(m->dec_cap, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  TURT_CHECK_CUDA(ce);
+  const cudaError_t ie = cudaGraphInstantiate(&m->dec_graph, g, 0);
+  cudaGraphDestroy(g);
+  TURT_CHECK_CUDA(ie);
+  note_launch(-n);  // captured, not run: replays are counted when they are launched
+  m->dec_graph_kernels = n;
   return OK;
 }
 
@@ -302,6 +426,8 @@ extern "C" int turt_generate_prefill(turt_model* m, const uint32_t* ids, int t, 
   TURT_REQUIRE(t > 0 && t <= m->cfg.block_size, "generate_prefill: context must hold 1 .. block_size tokens");
   for (int i = 0; i < t; i++)
     TURT_REQUIRE(ids[i] < (uint32_t)m->cfg.vocab_size, "generate_prefill: token id out of range");
+  TURT_REQUIRE(attn_smem(m->cfg.block_size, m->cfg.n_embd / m->cfg.n_head) <= 48 * 1024,
+               "generate_prefill: the decode attention keeps block_size / 8 + 9 * head_dim floats in 48 KB of shared memory");
   RC(ensure_decode(m));
   RC(model_forward_logits(m, ids, t));
   cudaStream_t st = m->ctx->stream;
@@ -326,43 +452,12 @@ extern "C" int turt_generate_step(turt_model* m, uint32_t id, int pos, float* lo
   TURT_REQUIRE(pos < m->cfg.block_size, "generate_step: the context is full (prefill the cropped window instead)");
   TURT_REQUIRE(id < (uint32_t)m->cfg.vocab_size, "generate_step: token id out of range");
   cudaStream_t st = m->ctx->stream;
-  const int E = m->cfg.n_embd, H = m->cfg.n_head, hd = E / H, h = m->hid, V = m->cfg.vocab_size;
-  const int Tc = m->cfg.block_size, W1 = m->modern ? 2 * h : h;
-  const float* P = m->P;
-  const DecBufs d = dec_bufs(m);
-  const size_t per_layer = (size_t)Tc * E;
-  const float scale = 1.0f / sqrtf((float)hd);
-  k_dec_embed<<<1, 256, 0, st>>>(P + m->wte, m->modern ? nullptr : P + m->wpe, id, pos, d.x, E);
-  TURT_LAUNCH_CHECK();
-  for (int l = 0; l < m->cfg.n_layer; l++) {
-    const LayerOff& L = m->layers[l];
-    if (m->modern)
-      RC(rms_fwd(st, d.x, P + L.ln1g, d.y, d.rstd, 1, E, m->eps));
-    else
-      RC(ln_fwd(st, d.x, P + L.ln1g, P + L.ln1b, d.y, d.mean, d.rstd, 1, E, m->eps));
-    RC(gemv(st, d, d.y, P + L.wqkv, 3 * E, E, 3 * E, m->modern ? nullptr : P + L.bqkv, nullptr, d.qkv));
-    k_dec_qkv_post<<<1, 256, 0, st>>>(d.qkv, m->rope_cs, pos, H, hd, m->modern ? 1 : 0, m->kcache + l * per_layer,
-                                      m->vcache + l * per_layer, Tc);
-    TURT_LAUNCH_CHECK();
-    k_dec_attn<<<H, 128, (size_t)(Tc + hd) * 4, st>>>(d.qkv, m->kcache + l * per_layer, m->vcache + l * per_layer,
-                                                      pos, hd, Tc, scale, d.att);
-    TURT_LAUNCH_CHECK();
-    RC(gemv(st, d, d.att, P + L.wproj, E, E, E, m->modern ? nullptr : P + L.bproj, d.x, d.h));
-    if (m->modern)
-      RC(rms_fwd(st, d.h, P + L.ln2g, d.y, d.rstd, 1, E, m->eps));
-    else
-      RC(ln_fwd(st, d.h, P + L.ln2g, P + L.ln2b, d.y, d.mean, d.rstd, 1, E, m->eps));
-    RC(gemv(st, d, d.y, P + L.w1, W1, E, W1, m->modern ? nullptr : P + L.b1, nullptr, d.pre));
-    k_dec_act<<<(h + 255) / 256, 256, 0, st>>>(d.pre, d.act, h, m->modern ? 1 : 0);
-    TURT_LAUNCH_CHECK();
-    RC(gemv(st, d, d.act, P + L.w2, E, h, E, m->modern ? nullptr : P + L.b2, d.h, d.x));
-  }
-  if (m->modern)
-    RC(rms_fwd(st, d.x, P + m->lnfg, d.y, d.rstd, 1, E, m->eps));
-  else
-    RC(ln_fwd(st, d.x, P + m->lnfg, P + m->lnfb, d.y, d.mean, d.rstd, 1, E, m->eps));
-  k_dec_logits<<<(V + 7) / 8, 256, 0, st>>>(d.y, P + m->wte, V, E, d.logits);
-  TURT_LAUNCH_CHECK();
+  if (!m->dec_graph) RC(capture_step(m));
+  m->h_dec_tok[0] = (int)id;
+  m->h_dec_tok[1] = pos;
+  TURT_CHECK_CUDA(cudaMemcpyAsync(m->dec_tok, m->h_dec_tok, 2 * sizeof(int), cudaMemcpyHostToDevice, st));
+  TURT_CHECK_CUDA(cudaGraphLaunch(m->dec_graph, st));
+  note_launch(m->dec_graph_kernels);
   m->dec_len = pos + 1;
-  return copy_logits_out(m, d.logits, logits_out);
+  return copy_logits_out(m, dec_bufs(m).logits, logits_out);
 }

@@ -625,6 +625,10 @@ int turt_model_destroy(turt_model* m) {
   if (m->kcache) cudaFree(m->kcache);
   if (m->vcache) cudaFree(m->vcache);
   if (m->dec) cudaFree(m->dec);
+  if (m->dec_tok) cudaFree(m->dec_tok);
+  if (m->h_dec_tok) cudaFreeHost(m->h_dec_tok);
+  if (m->dec_graph) cudaGraphExecDestroy(m->dec_graph);
+  if (m->dec_cap) cudaStreamDestroy(m->dec_cap);
   cudaFreeHost(m->h_loss);
   if (m->h_ids) cudaFreeHost(m->h_ids);
   if (m->h_tgt) cudaFreeHost(m->h_tgt);

@@ -81,6 +81,13 @@ struct turt_model {
   float *kcache = nullptr, *vcache = nullptr, *dec = nullptr;
   size_t dec_floats = 0;
   int dec_len = 0;
+  // The decode step is captured once into a CUDA graph that reads (token, position) from a
+  // device cell; each step copies the pair there from pinned memory and replays the graph.
+  int* dec_tok = nullptr;
+  int* h_dec_tok = nullptr;  // pinned
+  cudaStream_t dec_cap = nullptr;
+  cudaGraphExec_t dec_graph = nullptr;
+  int dec_graph_kernels = 0;
 };
 
 namespace turt {
