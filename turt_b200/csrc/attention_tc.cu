@@ -24,6 +24,8 @@ namespace {
 // (x0, x1) -> (x0 c - x1 s, x0 s + x1 c) with (c, s) = rope_cs[t][pair].
 __global__ void k_rope_heads(const float* __restrict__ qkv, const float2* __restrict__ cs, float* __restrict__ qr,
                              float* __restrict__ kr, int B, int T, int H, int hd) {
+  pdl_trigger();
+  pdl_wait();
   const int E = H * hd, q4 = hd / 4;
   const long total = (long)B * T * H * q4;
   const int which = blockIdx.y;  // 0 = q, 1 = k
@@ -56,6 +58,8 @@ constexpr int kRowWarps = 8;       // warps per 256-thread block
 template <int C, int R>
 __global__ void __launch_bounds__(256) k_softmax_causal(float* __restrict__ S, long rows, int T, long pitch,
                                                         float scale) {
+  pdl_trigger();
+  pdl_wait();
   const long row0 = ((long)blockIdx.x * kRowWarps + threadIdx.x / 32) * R;
   const int lane = threadIdx.x & 31;
   if (row0 >= rows) return;
@@ -110,6 +114,8 @@ __global__ void __launch_bounds__(256) k_softmax_causal(float* __restrict__ S, l
 // Rows longer than the register budget: three passes over memory, one warp per row.
 __global__ void __launch_bounds__(256) k_softmax_causal_long(float* __restrict__ S, long rows, int T, long pitch,
                                                              float scale) {
+  pdl_trigger();
+  pdl_wait();
   const long row = (long)blockIdx.x * kRowWarps + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -130,6 +136,8 @@ __global__ void __launch_bounds__(256) k_softmax_causal_long(float* __restrict__
 template <int C, int R>
 __global__ void __launch_bounds__(256) k_softmax_causal_bwd(const float* __restrict__ P, float* __restrict__ dP,
                                                             long rows, int T, long pitch, float scale) {
+  pdl_trigger();
+  pdl_wait();
   const long row0 = ((long)blockIdx.x * kRowWarps + threadIdx.x / 32) * R;
   const int lane = threadIdx.x & 31;
   if (row0 >= rows) return;
@@ -186,6 +194,8 @@ __global__ void __launch_bounds__(256) k_softmax_causal_bwd(const float* __restr
 
 __global__ void __launch_bounds__(256) k_softmax_causal_bwd_long(const float* __restrict__ P, float* __restrict__ dP,
                                                                  long rows, int T, long pitch, float scale) {
+  pdl_trigger();
+  pdl_wait();
   const long row = (long)blockIdx.x * kRowWarps + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -204,9 +214,9 @@ int rows_launch_c(cudaStream_t st, long rows, int T, long pitch, float scale, fl
   constexpr int R = C <= 2 ? 4 : (C <= 4 ? 2 : 1);  // rows per warp: ~8 float4 loads in flight per array
   const int blocks = (int)((rows + kRowWarps * R - 1) / (kRowWarps * R));
   if (!bwd)
-    k_softmax_causal<C, R><<<blocks, 256, 0, st>>>(S, rows, T, pitch, scale);
+    TURT_CHECK_CUDA((launch_pdl(k_softmax_causal<C, R>, dim3(blocks), dim3(256), 0, st, S, rows, T, pitch, scale)));
   else
-    k_softmax_causal_bwd<C, R><<<blocks, 256, 0, st>>>(P, S, rows, T, pitch, scale);
+    TURT_CHECK_CUDA((launch_pdl(k_softmax_causal_bwd<C, R>, dim3(blocks), dim3(256), 0, st, P, S, rows, T, pitch, scale)));
   TURT_LAUNCH_CHECK();
   return OK;
 }
@@ -223,9 +233,9 @@ int rows_launch(cudaStream_t st, long rows, int T, long pitch, float scale, floa
   }
   const int blocks = (int)((rows + kRowWarps - 1) / kRowWarps);
   if (!bwd)
-    k_softmax_causal_long<<<blocks, 256, 0, st>>>(S, rows, T, pitch, scale);
+    TURT_CHECK_CUDA((launch_pdl(k_softmax_causal_long, dim3(blocks), dim3(256), 0, st, S, rows, T, pitch, scale)));
   else
-    k_softmax_causal_bwd_long<<<blocks, 256, 0, st>>>(P, S, rows, T, pitch, scale);
+    TURT_CHECK_CUDA((launch_pdl(k_softmax_causal_bwd_long, dim3(blocks), dim3(256), 0, st, P, S, rows, T, pitch, scale)));
   TURT_LAUNCH_CHECK();
   return OK;
 }
@@ -316,7 +326,7 @@ int attention_tc_fwd(cudaStream_t st, const float* qkv, const float2* rope_cs, f
   const int E = H * hd, BH = B * H;
   const float scale = 1.0f / sqrtf((float)hd);
   if (rope && !rotated) {
-    k_rope_heads<<<dim3(grid_for((long)B * T * H * hd / 4), 2), 256, 0, st>>>(qkv, rope_cs, at.qr, at.kr, B, T, H, hd);
+    TURT_CHECK_CUDA((launch_pdl(k_rope_heads, dim3(dim3(grid_for((long)B * T * H * hd / 4), 2)), dim3(256), 0, st, qkv, rope_cs, at.qr, at.kr, B, T, H, hd)));
     TURT_LAUNCH_CHECK();
   }
   const Views w = views(qkv, nullptr, at, at.P, T, H, hd, rope != 0);

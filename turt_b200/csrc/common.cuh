@@ -157,4 +157,32 @@ __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf
 
 inline int ceil_div(long a, long b) { return (int)((a + b - 1) / b); }
 
+// ------------------------------------------------ programmatic dependent launch
+// The train step is a chain of ~175 kernels on one stream.  Launched with launch_pdl, a kernel
+// may be scheduled while its predecessor is still draining, so its launch and set-up (barrier
+// init, TMEM allocation) overlap the predecessor's tail.  Such a kernel calls pdl_wait() before
+// its first global memory access, read or write: it returns once the predecessor has completed
+// and its writes are visible.  pdl_trigger() lets the successor be scheduled; a grid triggers
+// once every one of its CTAs has triggered or exited, i.e. no earlier than its last wave, so
+// waiting successors only take resources the predecessor no longer asks for.  In a kernel not
+// launched with launch_pdl both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 }  // namespace turt

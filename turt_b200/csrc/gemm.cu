@@ -521,6 +521,9 @@ __global__ void __launch_bounds__(GemmShape<BN, BK, X3, MINB>::THREADS, MINB)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // set-up done: from here on global memory is touched (PDL; no-ops under a plain launch)
+  pdl_trigger();
+  pdl_wait();
 
   // unit -> (m0, n0, batch, first k-tile, k-tile count); false = nothing to compute (causal skip)
   auto decode = [&](int u, int& m0, int& n0, int& b, int& kt0, int& nkt) {
@@ -863,6 +866,8 @@ __global__ void __launch_bounds__(352, 1)
   cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any cross-CTA use
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();
   // shared::cluster addresses of the even CTA's relay targets
   const uint32_t lead_pconv = peer_addr(smem_u32(pconv), 0);
   const uint32_t lead_ptempty = peer_addr(smem_u32(ptempty), 0);
@@ -1234,8 +1239,8 @@ int launch(const LaunchArgs& a) {
   const long units = (long)ceil_div(a.M, BM) * ceil_div(a.N, BN) * a.batch * a.ks;
   const long slots = (long)MINB * num_sms();
   const int grid = (int)(units < slots ? units : slots);
-  kfn<<<grid, S::THREADS, S::SMEM, a.st>>>(a.ma, a.mb, a.epi, a.M, a.N, a.K, a.batch, a.bdiv, a.causal, a.ks, a.kt_per,
-                                           a.flags);
+  TURT_CHECK_CUDA((launch_pdl(kfn, dim3(grid), dim3(S::THREADS), S::SMEM, a.st, a.ma, a.mb, a.epi, a.M, a.N, a.K, a.batch, a.bdiv, a.causal, a.ks, a.kt_per,
+                                           a.flags)));
   TURT_LAUNCH_CHECK();
   return OK;
 }
@@ -1293,17 +1298,19 @@ int launch_pair(const LaunchArgs& a) {
   const long units = (long)ceil_div(a.M, 2 * BM) * ceil_div(a.N, BN) * a.batch * a.ks;
   const int pairs = (int)(units < max_pairs ? units : max_pairs);
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see launch_pdl
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(S::THREADS);
   cfg.dynamicSmemBytes = S::SMEM;
   cfg.stream = a.st;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   TURT_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kfn, a.ma, a.mb, a.epi, a.M, a.N, a.K, a.batch, a.bdiv, a.causal, a.ks,
                                      a.kt_per, a.flags));
   note_launch();

@@ -14,6 +14,8 @@ namespace {
 // x[n,:] = wte[ids[n],:] (+ wpe[n % T,:]); GATHER (+EWISE add), autograd.ts:416-425.
 __global__ void k_embed(const float* __restrict__ wte, const float* __restrict__ wpe, const uint32_t* __restrict__ ids,
                         float* __restrict__ x, int N, int T, int E, int V, int* flags) {
+  pdl_trigger();
+  pdl_wait();
   const int e4 = E / 4;
   GRID_STRIDE(i, (size_t)N * e4) {
     const int n = (int)(i / e4), c = (int)(i % e4);
@@ -38,6 +40,8 @@ __global__ void k_embed(const float* __restrict__ wte, const float* __restrict__
 // as atomics over the N*E gradient elements instead of the reference's O(V*N) scan.
 __global__ void k_embed_bwd(const float* __restrict__ dx, const uint32_t* __restrict__ ids, float* __restrict__ dwte,
                             float* __restrict__ dwpe, int N, int T, int E, int V) {
+  pdl_trigger();
+  pdl_wait();
   GRID_STRIDE(i, (size_t)N * E) {
     const int n = (int)(i / E), c = (int)(i % E);
     const uint32_t id = ids[n];
@@ -63,6 +67,8 @@ template <int NJ>
 __global__ void __launch_bounds__(256) k_rms_fwd(const float* __restrict__ x, const float* __restrict__ g,
                                                  float* __restrict__ y, float* __restrict__ rstd, int rows, int E,
                                                  float eps) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x * kNormWarps + threadIdx.x / 32, lane = threadIdx.x & 31;
   if (row >= rows) return;
   const int n4 = E / 4;
@@ -119,6 +125,8 @@ __global__ void __launch_bounds__(256, 2) k_rms_bwd(const float* __restrict__ x,
                                                  const float* __restrict__ g, const float* __restrict__ rstd,
                                                  const float* dres, float* dx, float* __restrict__ dg_part, int rows,
                                                  int E) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float sm[];
   const int lane = threadIdx.x & 31, n4 = E / 4;
   const int stride = gridDim.x * kNormWarps;
@@ -190,6 +198,8 @@ __global__ void __launch_bounds__(256) k_ln_fwd(const float* __restrict__ x, con
                                                 const float* __restrict__ b, float* __restrict__ y,
                                                 float* __restrict__ mean, float* __restrict__ rstd, int rows, int E,
                                                 float eps) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x * kNormWarps + threadIdx.x / 32, lane = threadIdx.x & 31;
   if (row >= rows) return;
   const int n4 = E / 4;
@@ -238,6 +248,8 @@ __global__ void __launch_bounds__(256, 2) k_ln_bwd(const float* __restrict__ x, 
                                                 const float* __restrict__ rstd, const float* dres, float* dx,
                                                 float* __restrict__ dg_part, float* __restrict__ db_part, int rows,
                                                 int E) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float sm[];
   const int lane = threadIdx.x & 31, n4 = E / 4;
   const int stride = gridDim.x * kNormWarps;
@@ -303,6 +315,8 @@ __global__ void __launch_bounds__(256, 2) k_ln_bwd(const float* __restrict__ x, 
 // column: the lanes' strided loads are all independent (one memory round trip for up to a few
 // hundred partials), then a butterfly sum.
 __global__ void k_reduce_parts(const float* __restrict__ part, int nparts, int C, float* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int c = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
   if (c >= C) return;
   const float* col = part + (size_t)c * nparts;
@@ -315,6 +329,8 @@ __global__ void k_reduce_parts(const float* __restrict__ part, int nparts, int C
 // Column sums of g[rows][C] into column-major partials part[c][p] (bias gradients; SEGSUM,
 // autograd.ts:122-135): partial p sums rows p, p + P, p + 2P, ... (P = gridDim.y).
 __global__ void k_colsum_parts(const float* __restrict__ g, int rows, int C, float* __restrict__ part) {
+  pdl_trigger();
+  pdl_wait();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
   float s = 0.f;
@@ -329,6 +345,8 @@ __global__ void k_colsum_parts(const float* __restrict__ g, int rows, int C, flo
 // rule).  One thread per float4 of d(act); consecutive threads read consecutive 16-byte pieces.
 __global__ void __launch_bounds__(256) k_swiglu_bwd_il(const float* __restrict__ dact, const float* __restrict__ pre,
                                                        float* __restrict__ dpre, long N, int h) {
+  pdl_trigger();
+  pdl_wait();
   const int h4 = h / 4;
   const long total = N * h4;
   for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (long)gridDim.x * blockDim.x) {
@@ -358,6 +376,8 @@ __global__ void __launch_bounds__(256) k_swiglu_bwd_il(const float* __restrict__
 // gradient (CE_BWD, :455-471) written in place over the logits: one HBM read, one write.
 __global__ void __launch_bounds__(512) k_ce_fused(float* __restrict__ logits, const uint32_t* __restrict__ tgt,
                                                   float* __restrict__ loss_rows, int V, float gscale, int* flags) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   float* x = logits + (size_t)row * V;
   __shared__ float red_m[32], red_s[32];
@@ -458,6 +478,8 @@ __global__ void __launch_bounds__(512) k_ce_fused(float* __restrict__ logits, co
 // Forward-only variant: per-row loss, logits untouched.
 __global__ void __launch_bounds__(512) k_ce_loss(const float* __restrict__ logits, const uint32_t* __restrict__ tgt,
                                                  float* __restrict__ loss_rows, int V, int* flags) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   const float* x = logits + (size_t)row * V;
   __shared__ float red_m[32], red_s[32];
@@ -510,6 +532,8 @@ __global__ void __launch_bounds__(512) k_ce_loss(const float* __restrict__ logit
 
 // loss = (sum of per-row losses, in double) / n; one block, fixed order.
 __global__ void k_loss_mean(const float* __restrict__ rows, int n, float* __restrict__ out, int* flags) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ double part[32];
   double s = 0;
   for (int i = threadIdx.x; i < n; i += blockDim.x) s += rows[i];
@@ -531,6 +555,8 @@ __global__ void k_loss_mean(const float* __restrict__ rows, int n, float* __rest
 // Sum of squares of scale*g in double: per-block partials, then a fixed-order final pass.
 constexpr int NORM_BLOCKS = 592;  // 4 x 148 SMs
 __global__ void k_sumsq_parts(const float* __restrict__ g, size_t n, float scale, double* __restrict__ part) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ double red[32];
   double s = 0;
   const size_t n4 = n / 4;
@@ -557,6 +583,8 @@ __global__ void k_sumsq_parts(const float* __restrict__ g, size_t n, float scale
 // norm = sqrt(sum); coef = clip > 0 && norm > clip ? clip / norm : 1 (src/optim/clip.ts:7-24).
 __global__ void k_norm_final(const double* __restrict__ part, int nparts, float clip, double* __restrict__ norm_out,
                              float* __restrict__ coef_out, int* flags) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ double red[32];
   double s = 0;
   for (int i = threadIdx.x; i < nparts; i += blockDim.x) s += part[i];
@@ -581,6 +609,8 @@ __global__ void k_norm_final(const double* __restrict__ part, int nparts, float 
 }
 // g *= coef (standalone clipGradNorm).
 __global__ void k_scale_by(float* __restrict__ g, size_t n, const float* __restrict__ coef, float pre) {
+  pdl_trigger();
+  pdl_wait();
   const float c = coef[0] * pre;
   GRID_STRIDE(i, n) g[i] *= c;
 }
@@ -590,6 +620,8 @@ __global__ void k_scale_by(float* __restrict__ g, size_t n, const float* __restr
 __global__ void k_adamw_flat(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, size_t n, float lr, float b1, float b2, float eps, float wd,
                              float bc1, float bc2, float gscale, const float* __restrict__ coef) {
+  pdl_trigger();
+  pdl_wait();
   const float cs = gscale * (coef ? coef[0] : 1.0f);
   const float rbc1 = 1.0f / bc1, rbc2 = 1.0f / bc2;
   const size_t n4 = n / 4;
@@ -627,14 +659,14 @@ int embed_fwd(cudaStream_t st, const float* wte, const float* wpe, const uint32_
               int V, int* flags) {
   TURT_REQUIRE(E % 4 == 0, "embedding width must be a multiple of 4");
   const size_t n = (size_t)N * (E / 4);
-  k_embed<<<(int)std::min<size_t>((n + 255) / 256, 148 * 32), 256, 0, st>>>(wte, wpe, ids, x, N, T, E, V, flags);
+  TURT_CHECK_CUDA((launch_pdl(k_embed, dim3((int)std::min<size_t>((n + 255) / 256, 148 * 32)), dim3(256), 0, st, wte, wpe, ids, x, N, T, E, V, flags)));
   TURT_LAUNCH_CHECK();
   return OK;
 }
 int embed_bwd(cudaStream_t st, const float* dx, const uint32_t* ids, float* dwte, float* dwpe, int N, int T, int E,
               int V) {
   const size_t n = (size_t)N * E;
-  k_embed_bwd<<<(int)std::min<size_t>((n + 255) / 256, 148 * 32), 256, 0, st>>>(dx, ids, dwte, dwpe, N, T, E, V);
+  TURT_CHECK_CUDA((launch_pdl(k_embed_bwd, dim3((int)std::min<size_t>((n + 255) / 256, 148 * 32)), dim3(256), 0, st, dx, ids, dwte, dwpe, N, T, E, V)));
   TURT_LAUNCH_CHECK();
   return OK;
 }
@@ -665,7 +697,7 @@ int sm_count() {
 
 int rms_fwd(cudaStream_t st, const float* x, const float* g, float* y, float* rstd, int rows, int E, float eps) {
   TURT_REQUIRE(E % 32 == 0 && E <= 32 * MAXV, "norm width must be a multiple of 32, at most 1024");
-#define CALL(NJ) k_rms_fwd<NJ><<<ceil_div(rows, kNormWarps), 256, 0, st>>>(x, g, y, rstd, rows, E, eps)
+#define CALL(NJ) TURT_CHECK_CUDA((launch_pdl(k_rms_fwd<NJ>, dim3(ceil_div(rows, kNormWarps)), dim3(256), 0, st, x, g, y, rstd, rows, E, eps)))
   TURT_NJ_SWITCH(E, CALL)
 #undef CALL
   TURT_LAUNCH_CHECK();
@@ -681,18 +713,18 @@ int rms_bwd(cudaStream_t st, const float* x, const float* dy, const float* g, co
   TURT_REQUIRE(E % 32 == 0 && E <= 32 * MAXV, "norm width must be a multiple of 32, at most 1024");
   const int nb = norm_parts(rows);
   const size_t smem = (size_t)kNormWarps * E * 4;
-#define CALL(NJ) k_rms_bwd<NJ><<<nb, 256, smem, st>>>(x, dy, g, rstd, dres, dx, part, rows, E)
+#define CALL(NJ) TURT_CHECK_CUDA((launch_pdl(k_rms_bwd<NJ>, dim3(nb), dim3(256), smem, st, x, dy, g, rstd, dres, dx, part, rows, E)))
   TURT_NJ_SWITCH(E, CALL)
 #undef CALL
   TURT_LAUNCH_CHECK();
-  k_reduce_parts<<<ceil_div(E, 8), 256, 0, st>>>(part, nb, E, dg_accum);
+  TURT_CHECK_CUDA((launch_pdl(k_reduce_parts, dim3(ceil_div(E, 8)), dim3(256), 0, st, part, nb, E, dg_accum)));
   TURT_LAUNCH_CHECK();
   return OK;
 }
 int ln_fwd(cudaStream_t st, const float* x, const float* g, const float* b, float* y, float* mean, float* rstd, int rows,
            int E, float eps) {
   TURT_REQUIRE(E % 32 == 0 && E <= 32 * MAXV, "norm width must be a multiple of 32, at most 1024");
-#define CALL(NJ) k_ln_fwd<NJ><<<ceil_div(rows, kNormWarps), 256, 0, st>>>(x, g, b, y, mean, rstd, rows, E, eps)
+#define CALL(NJ) TURT_CHECK_CUDA((launch_pdl(k_ln_fwd<NJ>, dim3(ceil_div(rows, kNormWarps)), dim3(256), 0, st, x, g, b, y, mean, rstd, rows, E, eps)))
   TURT_NJ_SWITCH(E, CALL)
 #undef CALL
   TURT_LAUNCH_CHECK();
@@ -704,22 +736,22 @@ int ln_bwd(cudaStream_t st, const float* x, const float* dy, const float* g, con
   const int nb = norm_parts(rows);
   const size_t smem = (size_t)kNormWarps * E * 4;
 #define CALL(NJ) \
-  k_ln_bwd<NJ><<<nb, 256, smem, st>>>(x, dy, g, mean, rstd, dres, dx, part, part + (size_t)nb * E, rows, E)
+  TURT_CHECK_CUDA((launch_pdl(k_ln_bwd<NJ>, dim3(nb), dim3(256), smem, st, x, dy, g, mean, rstd, dres, dx, part, part + (size_t)nb * E, rows, E)))
   TURT_NJ_SWITCH(E, CALL)
 #undef CALL
   TURT_LAUNCH_CHECK();
-  k_reduce_parts<<<ceil_div(E, 8), 256, 0, st>>>(part, nb, E, dg_accum);
+  TURT_CHECK_CUDA((launch_pdl(k_reduce_parts, dim3(ceil_div(E, 8)), dim3(256), 0, st, part, nb, E, dg_accum)));
   TURT_LAUNCH_CHECK();
-  k_reduce_parts<<<ceil_div(E, 8), 256, 0, st>>>(part + (size_t)nb * E, nb, E, db_accum);
+  TURT_CHECK_CUDA((launch_pdl(k_reduce_parts, dim3(ceil_div(E, 8)), dim3(256), 0, st, part + (size_t)nb * E, nb, E, db_accum)));
   TURT_LAUNCH_CHECK();
   return OK;
 }
 int colsum_accum(cudaStream_t st, const float* g, int rows, int C, float* out_accum, float* part) {
   const int nb = norm_parts(rows);
   dim3 grid(ceil_div(C, 128), nb);
-  k_colsum_parts<<<grid, 128, 0, st>>>(g, rows, C, part);
+  TURT_CHECK_CUDA((launch_pdl(k_colsum_parts, dim3(grid), dim3(128), 0, st, g, rows, C, part)));
   TURT_LAUNCH_CHECK();
-  k_reduce_parts<<<ceil_div(C, 8), 256, 0, st>>>(part, nb, C, out_accum);
+  TURT_CHECK_CUDA((launch_pdl(k_reduce_parts, dim3(ceil_div(C, 8)), dim3(256), 0, st, part, nb, C, out_accum)));
   TURT_LAUNCH_CHECK();
   return OK;
 }
@@ -728,37 +760,37 @@ int swiglu_bwd_interleaved(cudaStream_t st, const float* dact, const float* pre,
   const long total = (long)N * (h / 4);
   long blocks = (total + 255) / 256;
   if (blocks > 148L * 16) blocks = 148L * 16;
-  k_swiglu_bwd_il<<<(int)blocks, 256, 0, st>>>(dact, pre, dpre, N, h);
+  TURT_CHECK_CUDA((launch_pdl(k_swiglu_bwd_il, dim3((int)blocks), dim3(256), 0, st, dact, pre, dpre, N, h)));
   TURT_LAUNCH_CHECK();
   return OK;
 }
 int ce_fused(cudaStream_t st, float* logits, const uint32_t* tgt, float* loss_rows, int N, int V, float gscale,
              int* flags) {
-  k_ce_fused<<<N, 512, 0, st>>>(logits, tgt, loss_rows, V, gscale, flags);
+  TURT_CHECK_CUDA((launch_pdl(k_ce_fused, dim3(N), dim3(512), 0, st, logits, tgt, loss_rows, V, gscale, flags)));
   TURT_LAUNCH_CHECK();
   return OK;
 }
 int ce_loss(cudaStream_t st, const float* logits, const uint32_t* tgt, float* loss_rows, int N, int V, int* flags) {
-  k_ce_loss<<<N, 512, 0, st>>>(logits, tgt, loss_rows, V, flags);
+  TURT_CHECK_CUDA((launch_pdl(k_ce_loss, dim3(N), dim3(512), 0, st, logits, tgt, loss_rows, V, flags)));
   TURT_LAUNCH_CHECK();
   return OK;
 }
 int loss_mean(cudaStream_t st, const float* rows, int n, float* out, int* flags) {
-  k_loss_mean<<<1, 1024, 0, st>>>(rows, n, out, flags);
+  TURT_CHECK_CUDA((launch_pdl(k_loss_mean, dim3(1), dim3(1024), 0, st, rows, n, out, flags)));
   TURT_LAUNCH_CHECK();
   return OK;
 }
 size_t norm_scratch_doubles() { return NORM_BLOCKS + 1; }
 int grad_norm(cudaStream_t st, const float* g, size_t n, float gscale, float clip, double* scratch, double* norm_out,
               float* coef_out, int* flags) {
-  k_sumsq_parts<<<NORM_BLOCKS, 512, 0, st>>>(g, n, gscale, scratch);
+  TURT_CHECK_CUDA((launch_pdl(k_sumsq_parts, dim3(NORM_BLOCKS), dim3(512), 0, st, g, n, gscale, scratch)));
   TURT_LAUNCH_CHECK();
-  k_norm_final<<<1, 1024, 0, st>>>(scratch, NORM_BLOCKS, clip, norm_out, coef_out, flags);
+  TURT_CHECK_CUDA((launch_pdl(k_norm_final, dim3(1), dim3(1024), 0, st, scratch, NORM_BLOCKS, clip, norm_out, coef_out, flags)));
   TURT_LAUNCH_CHECK();
   return OK;
 }
 int scale_by(cudaStream_t st, float* g, size_t n, const float* coef, float pre) {
-  k_scale_by<<<148 * 8, 256, 0, st>>>(g, n, coef, pre);
+  TURT_CHECK_CUDA((launch_pdl(k_scale_by, dim3(148 * 8), dim3(256), 0, st, g, n, coef, pre)));
   TURT_LAUNCH_CHECK();
   return OK;
 }
@@ -767,7 +799,7 @@ int adamw_flat(cudaStream_t st, float* p, const float* g, float* m, float* v, si
   TURT_REQUIRE(((uintptr_t)p & 15) == 0 && ((uintptr_t)g & 15) == 0 && ((uintptr_t)m & 15) == 0 &&
                    ((uintptr_t)v & 15) == 0,
                "adamw: buffers must be 16-byte aligned");
-  k_adamw_flat<<<148 * 8, 256, 0, st>>>(p, g, m, v, n, lr, b1, b2, eps, wd, bc1, bc2, gscale, coef);
+  TURT_CHECK_CUDA((launch_pdl(k_adamw_flat, dim3(148 * 8), dim3(256), 0, st, p, g, m, v, n, lr, b1, b2, eps, wd, bc1, bc2, gscale, coef)));
   TURT_LAUNCH_CHECK();
   return OK;
 }
