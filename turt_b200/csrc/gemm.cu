@@ -417,10 +417,13 @@ __device__ __forceinline__ void epi_tile(const GemmEpi& epi, const EpiVec& vec, 
       }
     }
   } else {
+    // Causal scores: a 32-column chunk wholly right of this warp's last row is never read
+    // (the row kernels mask it), so it is not stored either.
+    const long last_col = epi.causal == CAUSAL_SKIP_UPPER ? rowbase + 31 : (long)N;
 #pragma unroll 1
     for (int c = 0; c < BN / 32; c++) {
       const int col0 = n0 + c * 32;
-      if (col0 >= N) break;  // warp-uniform
+      if (col0 >= N || col0 > last_col) break;  // warp-uniform; later chunks lie further right
       float v[32];
       tmem_ld32(tbase + c * 32, v);
       if (tile)

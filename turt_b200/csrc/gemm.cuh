@@ -29,7 +29,7 @@ constexpr int kGluBlock = 32;
 // masked upper triangle is skipped; the skipped products are exact zeros.
 enum GemmCausal : int {
   CAUSAL_NONE = 0,
-  CAUSAL_SKIP_UPPER = 1,  // output [T x T] scores: tiles entirely above the diagonal are not computed
+  CAUSAL_SKIP_UPPER = 1,  // output [T x T] scores: tiles (32-column chunks) wholly above the diagonal are not computed (stored)
   CAUSAL_K_LOWER = 2,     // A = lower-triangular [rows x K]: K-range of a row tile ends at its last row
   CAUSAL_K_UPPER = 3,     // A = upper-triangular (a transposed lower one): K-range starts at the first row
 };
