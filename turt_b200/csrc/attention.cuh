@@ -32,6 +32,12 @@ bool attention_tc_supported(int hd);
 // projection GEMM's EPI_QKV_ROPE epilogue); otherwise they are made here from qkv.
 int attention_tc_fwd(cudaStream_t st, const float* qkv, const float2* rope_cs, float* out, const AttnTensors& at, int B,
                      int T, int H, int hd, int rope, int rotated, int* flags, int precision);
+// Single-kernel forward for T <= 256 and head dims 32 / 64 (attention_fused.cu): the same P
+// (pitch `pitch`, zeros right of the diagonal) and merged output as the three-launch chain.
+struct GemmOperand;
+bool attention_fused_supported(int T, int hd);
+int attention_fused_fwd(cudaStream_t st, const GemmOperand& q, const GemmOperand& k, const GemmOperand& v, float* P,
+                        long pitch, float* out, long ld_out, int B, int T, int H, int hd, float scale, int* flags);
 int attention_tc_bwd(cudaStream_t st, const float* qkv, const float2* rope_cs, const float* dout,
                      const AttnTensors& at, const AttnScratch& sc, float* dqkv, int B, int T, int H, int hd, int rope,
                      int* flags, int precision);

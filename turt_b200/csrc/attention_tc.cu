@@ -330,6 +330,8 @@ int attention_tc_fwd(cudaStream_t st, const float* qkv, const float2* rope_cs, f
     TURT_LAUNCH_CHECK();
   }
   const Views w = views(qkv, nullptr, at, at.P, T, H, hd, rope != 0);
+  if (precision == GEMM_TF32X3 && attention_fused_supported(T, hd))
+    return attention_fused_fwd(st, w.q, w.k, w.v, at.P, w.pitch, out, E, B, T, H, hd, scale, flags);
   // S = q k^T  (k [T][hd] is the K-major B operand)
   RC(gemm_tf32(st, T, T, hd, BH, w.q, w.k, scores_epi(at.P, T, H, w.pitch), flags, precision));
   RC(rows_launch(st, (long)BH * T, T, w.pitch, scale, at.P, nullptr, false));

@@ -16,91 +16,13 @@
 #include <mutex>
 
 #include "gemm.cuh"
+#include "tcgen05.cuh"
 
 namespace turt {
 
 namespace {
 
 constexpr int BM = 128;
-
-// ------------------------------------------------------------ PTX wrappers
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
-      "[%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-      : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// Shared-memory matrix descriptor (tcgen05 format): start>>4 [0,14), LBO>>4 [16,30),
-// SBO>>4 [32,46), version 1 [46,48), layout type [61,64).
-// K-major operands use the 128-byte swizzle (type 2: 16-byte chunks XOR row%8, 8-row atoms)
-// for 32-float k-tiles, or the 64-byte swizzle (type 4: 8 rows of 64 bytes) for 16-float ones.
-// MN-major tf32 operands must use the 128-byte swizzle with 32-byte atomicity (type 1:
-// 32-byte chunks XOR row%4, 4-row atoms); it is the only MN-major layout tf32 accepts.
-constexpr uint32_t kLayoutSW128 = 2;
-constexpr uint32_t kLayoutSW128Atom32 = 1;
-constexpr uint32_t kLayoutSW64 = 4;
-__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)layout << 61;
-  return d;
-}
-
-// Instruction descriptor for kind::tf32 (built inside the kernel): D fp32 [4,6)=1, A tf32
-// [7,10)=2, B tf32 [10,13)=2, A major [15], B major [16], N>>3 [17,23), M>>4 [24,29).
-__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
-        "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
-        "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
-}
 
 // ------------------------------------------------------------ epilogue
 // tcgen05.ld gives one epilogue lane one accumulator row (32 consecutive columns per load).
@@ -1418,6 +1340,12 @@ std::atomic<int> g_pair_override{-1};
 void gemm_set_tile_override(int bn, int pair) {
   g_tile_override.store(bn);
   g_pair_override.store(pair);
+}
+
+int tensor_map_f32(CUtensorMap* map, const GemmOperand& op, long inner, long rows, int bdiv, int batch,
+                   int box_inner, int box_rows, bool mn_major) {
+  return make_map(map, op.ptr, inner, rows, bdiv, batch / bdiv, op.ld, op.stride, op.stride_hi, box_inner, box_rows,
+                  mn_major);
 }
 
 bool gemm_tf32_supported(const GemmOperand& A, const GemmOperand& B) {

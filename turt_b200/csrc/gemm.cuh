@@ -76,6 +76,12 @@ int gemm_tf32(cudaStream_t stream, int M, int N, int K, int batch, const GemmOpe
               const GemmOperand& B, const GemmEpi& epi, int* dev_flags, int precision = GEMM_TF32X3,
               int force_splits = 0);
 
+// 4-D TMA tensor map over operand `op` viewed as [batch / bdiv][bdiv][rows][inner] (the same
+// view gemm_tf32 uses), with a box of box_inner x box_rows floats: K-major boxes 32 floats wide
+// take the 128-byte swizzle, MN-major ones the 128-byte swizzle with 32-byte atoms.
+int tensor_map_f32(CUtensorMap* map, const GemmOperand& op, long inner, long rows, int bdiv, int batch,
+                   int box_inner, int box_rows, bool mn_major);
+
 // True when gemm_tf32 can take these operands (TMA needs 16-byte pitches and bases).
 bool gemm_tf32_supported(const GemmOperand& A, const GemmOperand& B);
 
