@@ -547,6 +547,89 @@ def run_gemm(args, rank: int) -> None:
     print(json.dumps(out), flush=True)
 
 
+# ----------------------------------------------------------------------------- decode workload
+DECODE_MODEL = "gpt-6L-384d"
+
+
+def decode_cpu_sample(seconds: float = 10.0):
+    """GPT.generate on the CPU (oracle C restatement of src/models/gpt.ts:291-341: one full forward
+    over the context per new token), timed on new tokens at contexts 128..; 1 thread."""
+    from oracle.oracle import Oracle
+    w = WORKLOADS[DECODE_MODEL]
+    orc = Oracle()
+    cfg = orc.cfg(w["V"], w["T"], w["L"], w["H"], w["E"], w["arch"], w["hidden"])
+    params = orc.init(cfg, 1)
+    prompt = list(range(1, w["T"] // 2 + 1))
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds and n < 16:
+        orc.generate(cfg, params, prompt + [n % w["V"]] * n, 1, temperature=1.0, topk=0, rng_state=orc.rng(n))
+        n += 1
+    secs = time.perf_counter() - t0
+    return {"value": n / secs, "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"{n} new tokens of {DECODE_MODEL} at contexts {w['T'] // 2}..{w['T'] // 2 + n - 1}, one full "
+                      f"forward each (oracle C restatement of GPT.generate, 1 thread)"}
+
+
+def run_decode(args, rank: int) -> None:
+    """KV-cached generation on one GPU: prefill T/2 tokens, then T/2 decode steps, each the host
+    call a user makes (token in, logits out).  value / e2e: new tokens per second over the K
+    timed steps (CUDA events, 8-byte token copy in, 32 KB logits copy out per step included).
+    Roofline: the bytes a step must read (every weight once + the cached keys / values) over
+    the step time, against the HBM copy peak (the weights mostly sit in L2, so a fraction near
+    or above 1 would be possible; a low one means the step is latency-bound)."""
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+
+    from turt_b200.runtime import Context, Model, make_config
+    w = WORKLOADS[DECODE_MODEL]
+    V, T, L, E = w["V"], w["T"], w["L"], w["E"]
+    ctx = Context(0)
+    model = Model(ctx, make_config(V, T, L, w["H"], E, w["arch"], w["hidden"]))
+    model.init_reference(1)
+    ids = [int(x) for x in np.random.default_rng(0).integers(0, V, T)]
+    n0 = T // 2
+    steps = min(args.steps * 8, T - n0)
+    warm = min(args.warmup, 8)
+    model.generate_prefill(ids[:n0 - warm])
+    for pos in range(n0 - warm, n0):  # warm-up steps (graph capture happens in the first)
+        model.generate_step(ids[pos], pos)
+    launches0 = Context.launch_count()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for pos in range(n0, n0 + steps):
+            model.generate_step(ids[pos], pos)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    launches = Context.launch_count() - launches0
+    value = steps / (ms / 1000.0)
+    weight_bytes = model.num_params() * 4
+    kv_bytes = 2 * L * E * 4 * (n0 + steps / 2)  # mean cached positions read per step
+    achieved = (weight_bytes + kv_bytes) / (ms / 1000.0 / steps) / 1e9
+    peaks = measured_peaks()
+    line = {"metric": "decode tokens/sec (KV-cached generation, batch 1)", "value": value, "unit": "tokens/s",
+            "n_gpus": 1, "steps": steps, "warmup": warm, "ms_per_step": ms / steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "decode", "model": DECODE_MODEL, "context": f"{n0}..{n0 + steps}",
+                       "l2": "no flush: a step re-reads the same weights (the L2 keeps them, as in use)"},
+            "roofline": {"bound": "hbm", "kernel": "decode step (GEMVs, split attention, head)",
+                         "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                         "bytes_per_step": weight_bytes + kv_bytes, "peak_source": f"{peaks['source']} HBM copy"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": V * 4},
+            "gpu_launches": launches, "clocks": clk.summary()}
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = decode_cpu_sample()
+    model.close()
+    ctx.close()
+    print(json.dumps(line), flush=True)
+
+
 def cpu_ops_baseline():
     """The oracle's restatement of the same four ops (single thread) on 1/8 of each workload."""
     import numpy as np
@@ -579,7 +662,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="turt", choices=["turt", "reference"])
-    ap.add_argument("--workload", default="gpt-6L-384d", choices=sorted(WORKLOADS) + ["backward-ops", "gemm"])
+    ap.add_argument("--workload", default="gpt-6L-384d", choices=sorted(WORKLOADS) + ["backward-ops", "gemm", "decode"])
     ap.add_argument("--gemm", default="8192,8192,384", help="M,N,K of the gemm workload")
     ap.add_argument("--precision", type=int, default=3, choices=[1, 3])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -596,6 +679,19 @@ def main():
                                   "with no reference counterpart"}), flush=True)
             return
         run_gemm(args, rank)
+        return
+    if args.workload == "decode":
+        if args.impl == "reference":
+            if rank == 0:
+                line = decode_cpu_sample()
+                print(json.dumps({"impl": "reference", "metric": "decode tokens/sec (KV-cached generation, batch 1)",
+                                  "value": line["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": 1,
+                                  "warmup": 0, "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+                                  "config": {"workload": "decode", "model": DECODE_MODEL}, "cpu_baseline": line,
+                                  "e2e": {"value": line["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                          "d2h_bytes_per_step": 0}}), flush=True)
+            return
+        run_decode(args, rank)
         return
     if args.workload == "backward-ops":
         if args.impl == "reference":
