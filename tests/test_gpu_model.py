@@ -179,8 +179,20 @@ def test_fused_epilogues_every_tile_width(ctx, orc, arch, bn, pair):
 @pytest.mark.parametrize("t", [7, 130, 200, 301])
 def test_tensor_attention_ragged(ctx, orc, arch, t):
     """Tensor-core attention with sequence lengths that are not multiples of 4 (padded score
-    pitch), of the 128-row tile (diagonal tiles split), above one tile, and above 256 (softmax
-    in separate row kernels instead of the score GEMMs' epilogues); head dim 16."""
+    pitch), of the 128-row tile (diagonal tiles split), above one tile, and above 256; head dim
+    16 (the three-launch chain: score GEMM, softmax rows, P.V GEMM)."""
     loss, ref, le, ge, name = _run_parity(ctx, orc, 256, 320, 2, 4, 64, arch, 2, t, attn=1)
+    assert le <= LOSS_TOL, (loss, ref)
+    assert ge <= GRAD_TOL, (ge, name)
+
+
+@pytest.mark.parametrize("arch", ["gpt2", "modern"])
+@pytest.mark.parametrize("E,H", [(64, 2), (128, 2)])
+@pytest.mark.parametrize("t", [7, 64, 130, 200, 256])
+def test_fused_attention_forward(ctx, orc, arch, E, H, t):
+    """The single-kernel attention forward (T <= 256, head dims 32 and 64): one or two query
+    tiles, key counts that are not whole 64-key chunks, a ragged last tile and a row pitch that
+    is not a multiple of 32 (P zero-filled past the causal block); the backward reads its P."""
+    loss, ref, le, ge, name = _run_parity(ctx, orc, 256, 256, 2, H, E, arch, 2, t, attn=1)
     assert le <= LOSS_TOL, (loss, ref)
     assert ge <= GRAD_TOL, (ge, name)
