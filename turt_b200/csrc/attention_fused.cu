@@ -365,6 +365,177 @@ __global__ void __launch_bounds__(kFThreads, 1)
   }
 }
 
+
+// Backward of the softmax for T <= 256 in one kernel: dP = dO v^T into TMEM (the score-product
+// machinery above with dO for q and v for k), P of the tile loaded into shared memory by TMA,
+// then per row D = sum_j P_j dP_j and dS_j = P_j (dP_j - D) * scale (j <= i; 0 right of the
+// diagonal), written over P in place and stored by bulk tensor stores.  Replaces the dP GEMM
+// and the softmax-backward row kernel; same warp roles (warps 2..9 do the row arithmetic).
+template <int HD>
+__global__ void __launch_bounds__(kFThreads, 1)
+    k_attn_dsoftmax_fused(const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmV,
+                          const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmS,
+                          long pitch, int T, int H, float scale, int* flags) {
+  using S = FShape<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::REGION);
+  uint64_t* qk_full = bars + 0;
+  uint64_t* qk_conv = bars + 1;
+  uint64_t* s_full = bars + 2;
+  uint64_t* p_full = bars + 3;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
+  volatile int* sm_ok = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* red = reinterpret_cast<float*>(smem + S::REGION + 256);  // [2 halves][128 rows]
+  constexpr uint32_t kCols = 256;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int q0 = blockIdx.x * kFQ;
+  const int nk = min(T, q0 + kFQ);
+  const int nkr = (nk + 63) & ~63;
+  const int nbox = (nkr + 127) / 128;
+
+  if (threadIdx.x == 0) {
+    mbar_init(qk_full, 1);
+    mbar_init(qk_conv, 4);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 1);
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t sq = smem_u32(smem + S::Q_HI), sk = smem_u32(smem + S::K_HI);
+      mbar_arrive_expect_tx(qk_full, S::SLABS * (S::Q_SLAB + nbox * 16384));
+      for (int sl = 0; sl < S::SLABS; sl++) {
+        tma_load_4d(sq + sl * S::Q_SLAB, &tmO, sl * 32, q0, h, b, qk_full);
+        for (int bx = 0; bx < nbox; bx++)
+          tma_load_4d(sk + sl * S::K_SLAB + bx * 16384, &tmV, sl * 32, bx * 128, h, b, qk_full);
+      }
+      // P reuses the dO / v bytes once the product has read them: 32-key slabs of 128 rows
+      if (mbar_wait(s_full, 0, flags, 151)) {
+        mbar_arrive_expect_tx(p_full, (nkr / 32) * S::P_SLAB);
+        for (int sl = 0; sl < nkr / 32; sl++) tma_load_4d(smem_u32(smem) + sl * S::P_SLAB, &tmP, sl * 32, q0, h, b, p_full);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && mbar_wait(qk_conv, 0, flags, 152)) {
+      tc_fence_after();
+      const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(nkr >> 3) << 17) |
+                             ((uint32_t)(kFQ >> 4) << 24);
+      const uint32_t sq = smem_u32(smem + S::Q_HI), sk = smem_u32(smem + S::K_HI);
+      const uint64_t loq = (uint64_t)(S::Q_BYTES >> 4), lok = (uint64_t)(S::K_BYTES >> 4);
+#pragma unroll
+      for (int kk = 0; kk < HD / 8; kk++) {
+        const uint64_t da = smem_desc(sq + (kk >> 2) * S::Q_SLAB + (kk & 3) * 32, 16, 1024, kLayoutSW128);
+        const uint64_t db = smem_desc(sk + (kk >> 2) * S::K_SLAB + (kk & 3) * 32, 16, 1024, kLayoutSW128);
+        mma_tf32(tmem, da + loq, db, idesc, kk > 0 ? 1u : 0u);
+        mma_tf32(tmem, da, db + lok, idesc, 1u);
+        mma_tf32(tmem, da, db, idesc, 1u);
+      }
+      mma_commit(s_full);
+    }
+  } else if (warp >= 10) {
+    const int ct = threadIdx.x - 320;
+    if (mbar_wait(qk_full, 0, flags, 153)) {
+      lo_split(smem + S::Q_HI, S::Q_BYTES, S::Q_BYTES, ct);
+      for (int sl = 0; sl < S::SLABS; sl++) lo_split(smem + S::K_HI + sl * S::K_SLAB, nbox * 16384, S::K_BYTES, ct);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(qk_conv);
+    }
+  } else {
+    const int q = warp & 3, half = (warp - 2) >> 2;
+    const int row = q * 32 + lane, i = q0 + row;
+    const int n = min(i + 1, T);
+    const int warp_last = q0 + q * 32 + 31;
+    const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+    const bool issuer = threadIdx.x == 64;
+    if (issuer) *sm_ok = (mbar_wait(s_full, 0, flags, 154) && mbar_wait(p_full, 0, flags, 155)) ? 1 : 0;
+    softmax_sync();
+    if (*sm_ok) {
+      mbar_wait(p_full, 0, flags, 156);  // complete already: orders the TMA-written P before the reads below
+      tc_fence_after();
+      float D = 0.f;
+      for (int cc = half; cc < nkr / 32 && cc * 32 <= warp_last; cc += 2) {
+        float g[32];
+        tmem_ld32(trow + cc * 32, g);
+        const uint8_t* prow = smem + cc * S::P_SLAB + row * 128;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+          const float4 p = *reinterpret_cast<const float4*>(prow + ((k ^ (row & 7)) * 16));
+          const int j = cc * 32 + 4 * k;
+          D += (j + 0 < n ? p.x * g[4 * k + 0] : 0.f) + (j + 1 < n ? p.y * g[4 * k + 1] : 0.f) +
+               (j + 2 < n ? p.z * g[4 * k + 2] : 0.f) + (j + 3 < n ? p.w * g[4 * k + 3] : 0.f);
+        }
+      }
+      red[half * 128 + row] = D;
+      softmax_sync();
+      D = red[row] + red[128 + row];
+      for (int cc = half; cc < nkr / 32; cc += 2) {
+        uint8_t* prow = smem + cc * S::P_SLAB + row * 128;
+        if (cc * 32 <= warp_last) {  // warp-uniform
+          float g[32];
+          tmem_ld32(trow + cc * 32, g);
+#pragma unroll
+          for (int k = 0; k < 8; k++) {
+            float4* pp = reinterpret_cast<float4*>(prow + ((k ^ (row & 7)) * 16));
+            const float4 p = *pp;
+            const int j = cc * 32 + 4 * k;
+            *pp = make_float4(j + 0 < n ? p.x * (g[4 * k + 0] - D) * scale : 0.f,
+                              j + 1 < n ? p.y * (g[4 * k + 1] - D) * scale : 0.f,
+                              j + 2 < n ? p.z * (g[4 * k + 2] - D) * scale : 0.f,
+                              j + 3 < n ? p.w * (g[4 * k + 3] - D) * scale : 0.f);
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; k++) *reinterpret_cast<float4*>(prow + 16 * k) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      softmax_sync();
+      if (issuer) {
+        for (int sl = 0; sl < nkr / 32; sl++)
+          if (sl * 32 < pitch) tma_store_4d(&tmS, smem_u32(smem) + sl * S::P_SLAB, sl * 32, q0, h, b);
+        bulk_commit();
+      }
+      // columns [nkr, pitch): zeros from a zeroed slab past the ones just stored
+      if (nkr < pitch) {
+        uint8_t* z = smem + (nkr / 32) * S::P_SLAB + row * 128 + half * 64;
+#pragma unroll
+        for (int k = 0; k < 4; k++) *reinterpret_cast<float4*>(z + 16 * k) = make_float4(0.f, 0.f, 0.f, 0.f);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        softmax_sync();
+        if (issuer) {
+          for (long col = nkr; col < pitch; col += 32)
+            tma_store_4d(&tmS, smem_u32(smem) + (nkr / 32) * S::P_SLAB, (int)col, q0, h, b);
+          bulk_commit();
+        }
+      }
+    }
+    if (issuer) bulk_wait_all();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+  }
+}
+
 template <int HD>
 int launch_fused(cudaStream_t st, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                  const CUtensorMap& mp, long pitch, float* out, long ld_out, int B, int T, int H, float scale,
@@ -383,7 +554,46 @@ int launch_fused(cudaStream_t st, const CUtensorMap& mq, const CUtensorMap& mk, 
   return OK;
 }
 
+template <int HD>
+int launch_dsoftmax(cudaStream_t st, const CUtensorMap& mo, const CUtensorMap& mv, const CUtensorMap& mp,
+                    const CUtensorMap& ms, long pitch, int B, int T, int H, float scale, int* flags) {
+  using S = FShape<HD>;
+  auto kfn = k_attn_dsoftmax_fused<HD>;
+  static bool attr = false;
+  if (!attr) {
+    TURT_CHECK_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM));
+    attr = true;
+  }
+  TURT_CHECK_CUDA((launch_pdl(kfn, dim3(ceil_div(T, kFQ), B * H), dim3(kFThreads), S::SMEM, st, mo, mv, mp, ms, pitch,
+                              T, H, scale, flags)));
+  TURT_LAUNCH_CHECK();
+  return OK;
+}
+
+// P / dS view [B*H][T][pitch] as a GemmOperand (rows of `pitch` floats, heads T * pitch apart).
+GemmOperand score_operand(const float* base, int T, int H, long pitch) {
+  GemmOperand o;
+  o.ptr = base;
+  o.ld = pitch;
+  o.stride = (long)T * pitch;
+  o.stride_hi = (long)H * T * pitch;
+  return o;
+}
+
 }  // namespace
+
+int attention_fused_dsoftmax(cudaStream_t st, const GemmOperand& dout, const GemmOperand& v, const float* P, float* dS,
+                             long pitch, int B, int T, int H, int hd, float scale, int* flags) {
+  TURT_REQUIRE(attention_fused_supported(T, hd), "fused attention: needs T <= 256 and a head dim of 32 or 64");
+  TURT_REQUIRE(pitch % 4 == 0 && pitch >= T, "fused attention: bad probability row pitch");
+  CUtensorMap mo, mv, mp, ms;
+  RC(tensor_map_f32(&mo, dout, hd, T, H, B * H, 32, kFQ, false));
+  RC(tensor_map_f32(&mv, v, hd, T, H, B * H, 32, 128, false));
+  RC(tensor_map_f32(&mp, score_operand(P, T, H, pitch), pitch, T, H, B * H, 32, kFQ, false));
+  RC(tensor_map_f32(&ms, score_operand(dS, T, H, pitch), pitch, T, H, B * H, 32, kFQ, false));
+  if (hd == 64) return launch_dsoftmax<64>(st, mo, mv, mp, ms, pitch, B, T, H, scale, flags);
+  return launch_dsoftmax<32>(st, mo, mv, mp, ms, pitch, B, T, H, scale, flags);
+}
 
 bool attention_fused_supported(int T, int hd) { return T >= 1 && T <= kFKeys && (hd == 32 || hd == 64); }
 

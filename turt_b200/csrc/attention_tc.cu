@@ -350,10 +350,14 @@ int attention_tc_bwd(cudaStream_t st, const float* qkv, const float2* rope_cs, c
   const int E = H * hd, BH = B * H;
   const float scale = 1.0f / sqrtf((float)hd);
   const Views w = views(qkv, dout, at, at.P, T, H, hd, rope != 0);
-  // dP = dO v^T
-  RC(gemm_tf32(st, T, T, hd, BH, w.dout, w.v, scores_epi(sc.dS, T, H, w.pitch), flags, precision));
-  // dS = P (dP - rowsum(P dP)) * scale, in place
-  RC(rows_launch(st, (long)BH * T, T, w.pitch, scale, sc.dS, at.P, true));
+  if (precision == GEMM_TF32X3 && attention_fused_supported(T, hd)) {
+    RC(attention_fused_dsoftmax(st, w.dout, w.v, at.P, sc.dS, w.pitch, B, T, H, hd, scale, flags));
+  } else {
+    // dP = dO v^T
+    RC(gemm_tf32(st, T, T, hd, BH, w.dout, w.v, scores_epi(sc.dS, T, H, w.pitch), flags, precision));
+    // dS = P (dP - rowsum(P dP)) * scale, in place
+    RC(rows_launch(st, (long)BH * T, T, w.pitch, scale, sc.dS, at.P, true));
+  }
   GemmOperand dS = w.P, dST = w.PT;
   dS.ptr = sc.dS;
   dST.ptr = sc.dS;
