@@ -38,9 +38,12 @@ struct GemmOperand;
 bool attention_fused_supported(int T, int hd);
 int attention_fused_fwd(cudaStream_t st, const GemmOperand& q, const GemmOperand& k, const GemmOperand& v, float* P,
                         long pitch, float* out, long ld_out, int B, int T, int H, int hd, float scale, int* flags);
-// dS = P (dP - rowsum(P dP)) * scale with dP = dout v^T, in one kernel (same limits).
-int attention_fused_dsoftmax(cudaStream_t st, const GemmOperand& dout, const GemmOperand& v, const float* P, float* dS,
-                             long pitch, int B, int T, int H, int hd, float scale, int* flags);
+// dS = P (dP - rowsum(P dP)) * scale with dP = dout v^T, and dQ = dS k written into dq (row
+// pitch ld_dq, head columns h * hd; rotated back with `rope` when it is not null), in one
+// kernel (same limits).
+int attention_fused_dsoftmax(cudaStream_t st, const GemmOperand& dout, const GemmOperand& v, const GemmOperand& k,
+                             const float* P, float* dS, long pitch, float* dq, long ld_dq, const float2* rope, int B,
+                             int T, int H, int hd, float scale, int* flags);
 int attention_tc_bwd(cudaStream_t st, const float* qkv, const float2* rope_cs, const float* dout,
                      const AttnTensors& at, const AttnScratch& sc, float* dqkv, int B, int T, int H, int hd, int rope,
                      int* flags, int precision);

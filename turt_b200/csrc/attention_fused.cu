@@ -366,34 +366,54 @@ __global__ void __launch_bounds__(kFThreads, 1)
 }
 
 
-// Backward of the softmax for T <= 256 in one kernel: dP = dO v^T into TMEM (the score-product
-// machinery above with dO for q and v for k), P of the tile loaded into shared memory by TMA,
-// then per row D = sum_j P_j dP_j and dS_j = P_j (dP_j - D) * scale (j <= i; 0 right of the
-// diagonal), written over P in place and stored by bulk tensor stores.  Replaces the dP GEMM
-// and the softmax-backward row kernel; same warp roles (warps 2..9 do the row arithmetic).
+// Backward of the softmax and dQ for T <= 256 in one kernel: dP = dO v^T into TMEM (the
+// score-product machinery above with dO for q and v for k), P of the tile loaded into shared
+// memory by TMA, per row D = sum_j P_j dP_j and dS_j = P_j (dP_j - D) * scale (j <= i; 0 right
+// of the diagonal), written over P in place 64 keys at a time and stored by bulk tensor stores;
+// each dS chunk also feeds dQ += dS_c k_c on the tensor cores (k chunks MN-major from TMA), so
+// dQ leaves the kernel finished (rotated back by -theta for RoPE models).  Replaces the dP GEMM,
+// the softmax-backward row kernel and the dQ GEMM; same warp roles as the forward.
+template <int HD>
+struct DShape {
+  using F = FShape<HD>;
+  static constexpr int DL = 8 * F::P_SLAB;           // dS lo of one 64-key chunk (2 slabs)
+  static constexpr int KC = DL + 2 * F::P_SLAB;      // k chunk, MN-major, hi then lo
+  static constexpr int PH2 = KC + 2 * F::V_BYTES;
+  static constexpr int REGION = F::PH1 > PH2 ? F::PH1 : PH2;
+  static constexpr int SMEM = REGION + 256 + 4096 + 1024;
+};
+
 template <int HD>
 __global__ void __launch_bounds__(kFThreads, 1)
     k_attn_dsoftmax_fused(const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmV,
                           const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmS,
-                          long pitch, int T, int H, float scale, int* flags) {
+                          const __grid_constant__ CUtensorMap tmK, long pitch, float* __restrict__ dq, long ld_dq,
+                          const float2* __restrict__ rope, int T, int H, float scale, int* flags) {
   using S = FShape<HD>;
+  using D = DShape<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::REGION);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + D::REGION);
   uint64_t* qk_full = bars + 0;
   uint64_t* qk_conv = bars + 1;
   uint64_t* s_full = bars + 2;
   uint64_t* p_full = bars + 3;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
+  uint64_t* ds_ready = bars + 4;
+  uint64_t* dsl_free = bars + 5;
+  uint64_t* k_full = bars + 6;
+  uint64_t* k_conv = bars + 7;
+  uint64_t* k_empty = bars + 8;
+  uint64_t* dq_full = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
   volatile int* sm_ok = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* red = reinterpret_cast<float*>(smem + S::REGION + 256);  // [2 halves][128 rows]
-  constexpr uint32_t kCols = 256;
+  float* red = reinterpret_cast<float*>(smem + D::REGION + 256);  // [2 halves][128 rows]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.y, b = bh / H, h = bh % H;
   const int q0 = blockIdx.x * kFQ;
   const int nk = min(T, q0 + kFQ);
   const int nkr = (nk + 63) & ~63;
+  const int nch = nkr / 64;
   const int nbox = (nkr + 127) / 128;
 
   if (threadIdx.x == 0) {
@@ -401,11 +421,17 @@ __global__ void __launch_bounds__(kFThreads, 1)
     mbar_init(qk_conv, 4);
     mbar_init(s_full, 1);
     mbar_init(p_full, 1);
+    mbar_init(ds_ready, 1);
+    mbar_init(dsl_free, 1);
+    mbar_init(k_full, 1);
+    mbar_init(k_conv, 4);
+    mbar_init(k_empty, 1);
+    mbar_init(dq_full, 1);
     mbar_fence_init();
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kCols)
+                 "r"(kFTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -418,6 +444,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
+      // ---------------------------------------------------------------- TMA producer
       const uint32_t sq = smem_u32(smem + S::Q_HI), sk = smem_u32(smem + S::K_HI);
       mbar_arrive_expect_tx(qk_full, S::SLABS * (S::Q_SLAB + nbox * 16384));
       for (int sl = 0; sl < S::SLABS; sl++) {
@@ -425,39 +452,88 @@ __global__ void __launch_bounds__(kFThreads, 1)
         for (int bx = 0; bx < nbox; bx++)
           tma_load_4d(sk + sl * S::K_SLAB + bx * 16384, &tmV, sl * 32, bx * 128, h, b, qk_full);
       }
-      // P reuses the dO / v bytes once the product has read them: 32-key slabs of 128 rows
-      if (mbar_wait(s_full, 0, flags, 151)) {
+      // P and the k chunks reuse the dO / v bytes once the product has read them
+      bool ok = mbar_wait(s_full, 0, flags, 151);
+      if (ok) {
         mbar_arrive_expect_tx(p_full, (nkr / 32) * S::P_SLAB);
-        for (int sl = 0; sl < nkr / 32; sl++) tma_load_4d(smem_u32(smem) + sl * S::P_SLAB, &tmP, sl * 32, q0, h, b, p_full);
+        for (int sl = 0; sl < nkr / 32; sl++)
+          tma_load_4d(smem_u32(smem) + sl * S::P_SLAB, &tmP, sl * 32, q0, h, b, p_full);
+      }
+      for (int c = 0; c < nch && ok; c++) {
+        if (c >= 1 && !mbar_wait(k_empty, (c - 1) & 1, flags, 157)) break;
+        const uint32_t kc = smem_u32(smem + D::KC);
+        mbar_arrive_expect_tx(k_full, S::V_BYTES);
+        for (int sl = 0; sl < 2; sl++)
+          for (int j = 0; j < S::SLABS; j++)
+            tma_load_4d(kc + sl * S::V_SLAB + j * S::V_BOX, &tmK, 32 * j, c * 64 + sl * 32, h, b, k_full);
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && mbar_wait(qk_conv, 0, flags, 152)) {
-      tc_fence_after();
-      const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(nkr >> 3) << 17) |
-                             ((uint32_t)(kFQ >> 4) << 24);
-      const uint32_t sq = smem_u32(smem + S::Q_HI), sk = smem_u32(smem + S::K_HI);
-      const uint64_t loq = (uint64_t)(S::Q_BYTES >> 4), lok = (uint64_t)(S::K_BYTES >> 4);
+    if (lane == 0) {
+      // ---------------------------------------------------------------- MMA issuer
+      bool ok = mbar_wait(qk_conv, 0, flags, 152);
+      if (ok) {
+        tc_fence_after();
+        const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(nkr >> 3) << 17) |
+                               ((uint32_t)(kFQ >> 4) << 24);
+        const uint32_t sq = smem_u32(smem + S::Q_HI), sk = smem_u32(smem + S::K_HI);
+        const uint64_t loq = (uint64_t)(S::Q_BYTES >> 4), lok = (uint64_t)(S::K_BYTES >> 4);
 #pragma unroll
-      for (int kk = 0; kk < HD / 8; kk++) {
-        const uint64_t da = smem_desc(sq + (kk >> 2) * S::Q_SLAB + (kk & 3) * 32, 16, 1024, kLayoutSW128);
-        const uint64_t db = smem_desc(sk + (kk >> 2) * S::K_SLAB + (kk & 3) * 32, 16, 1024, kLayoutSW128);
-        mma_tf32(tmem, da + loq, db, idesc, kk > 0 ? 1u : 0u);
-        mma_tf32(tmem, da, db + lok, idesc, 1u);
-        mma_tf32(tmem, da, db, idesc, 1u);
+        for (int kk = 0; kk < HD / 8; kk++) {
+          const uint64_t da = smem_desc(sq + (kk >> 2) * S::Q_SLAB + (kk & 3) * 32, 16, 1024, kLayoutSW128);
+          const uint64_t db = smem_desc(sk + (kk >> 2) * S::K_SLAB + (kk & 3) * 32, 16, 1024, kLayoutSW128);
+          mma_tf32(tmem, da + loq, db, idesc, kk > 0 ? 1u : 0u);
+          mma_tf32(tmem, da, db + lok, idesc, 1u);
+          mma_tf32(tmem, da, db, idesc, 1u);
+        }
+        mma_commit(s_full);
       }
-      mma_commit(s_full);
+      constexpr uint32_t idesc_q = (1u << 4) | (2u << 7) | (2u << 10) | (1u << 16) | ((uint32_t)(HD >> 3) << 17) |
+                                   ((uint32_t)(kFQ >> 4) << 24);
+      const uint64_t lok = (uint64_t)(S::V_BYTES >> 4);
+      for (int c = 0; c < nch && ok; c++) {
+        if (!mbar_wait(ds_ready, c & 1, flags, 158) || !mbar_wait(k_conv, c & 1, flags, 159)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // dS chunk c: hi in slabs 2c, 2c+1 of the P tile, lo in the DL buffer
+        const uint32_t sd = smem_u32(smem) + 2 * c * S::P_SLAB, sk = smem_u32(smem + D::KC);
+        const uint64_t lod = (uint64_t)((D::DL - 2 * c * S::P_SLAB) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++) {
+          const uint64_t da = smem_desc(sd + (kk >> 2) * S::P_SLAB + (kk & 3) * 32, 16, 1024, kLayoutSW128);
+          const uint64_t db = smem_desc(sk + (kk >> 2) * S::V_SLAB + (kk & 3) * 1024, S::V_BOX, 512, kLayoutSW128Atom32);
+          const uint32_t first = (c > 0 || kk > 0) ? 1u : 0u;
+          mma_tf32(tmem + kFTmemO, da + lod, db, idesc_q, first);
+          mma_tf32(tmem + kFTmemO, da, db + lok, idesc_q, 1u);
+          mma_tf32(tmem + kFTmemO, da, db, idesc_q, 1u);
+        }
+        mma_commit(dsl_free);
+        mma_commit(k_empty);
+      }
+      if (ok) mma_commit(dq_full);
     }
   } else if (warp >= 10) {
+    // ---------------------------------------------------------------- lo-part converters
     const int ct = threadIdx.x - 320;
-    if (mbar_wait(qk_full, 0, flags, 153)) {
+    bool ok = mbar_wait(qk_full, 0, flags, 153);
+    if (ok) {
       lo_split(smem + S::Q_HI, S::Q_BYTES, S::Q_BYTES, ct);
       for (int sl = 0; sl < S::SLABS; sl++) lo_split(smem + S::K_HI + sl * S::K_SLAB, nbox * 16384, S::K_BYTES, ct);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(qk_conv);
     }
+    for (int c = 0; c < nch && ok; c++) {
+      if (!mbar_wait(k_full, c & 1, flags, 160)) break;
+      lo_split(smem + D::KC, S::V_BYTES, S::V_BYTES, ct);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(k_conv);
+    }
   } else {
+    // ---------------------------------------------------------------- row arithmetic + dQ out
     const int q = warp & 3, half = (warp - 2) >> 2;
     const int row = q * 32 + lane, i = q0 + row;
     const int n = min(i + 1, T);
@@ -466,10 +542,11 @@ __global__ void __launch_bounds__(kFThreads, 1)
     const bool issuer = threadIdx.x == 64;
     if (issuer) *sm_ok = (mbar_wait(s_full, 0, flags, 154) && mbar_wait(p_full, 0, flags, 155)) ? 1 : 0;
     softmax_sync();
-    if (*sm_ok) {
+    bool ok = *sm_ok != 0;
+    if (ok) {
       mbar_wait(p_full, 0, flags, 156);  // complete already: orders the TMA-written P before the reads below
       tc_fence_after();
-      float D = 0.f;
+      float Dsum = 0.f;
       for (int cc = half; cc < nkr / 32 && cc * 32 <= warp_last; cc += 2) {
         float g[32];
         tmem_ld32(trow + cc * 32, g);
@@ -478,42 +555,58 @@ __global__ void __launch_bounds__(kFThreads, 1)
         for (int k = 0; k < 8; k++) {
           const float4 p = *reinterpret_cast<const float4*>(prow + ((k ^ (row & 7)) * 16));
           const int j = cc * 32 + 4 * k;
-          D += (j + 0 < n ? p.x * g[4 * k + 0] : 0.f) + (j + 1 < n ? p.y * g[4 * k + 1] : 0.f) +
-               (j + 2 < n ? p.z * g[4 * k + 2] : 0.f) + (j + 3 < n ? p.w * g[4 * k + 3] : 0.f);
+          Dsum += (j + 0 < n ? p.x * g[4 * k + 0] : 0.f) + (j + 1 < n ? p.y * g[4 * k + 1] : 0.f) +
+                  (j + 2 < n ? p.z * g[4 * k + 2] : 0.f) + (j + 3 < n ? p.w * g[4 * k + 3] : 0.f);
         }
       }
-      red[half * 128 + row] = D;
+      red[half * 128 + row] = Dsum;
       softmax_sync();
-      D = red[row] + red[128 + row];
-      for (int cc = half; cc < nkr / 32; cc += 2) {
+      Dsum = red[row] + red[128 + row];
+      for (int c = 0; c < nch; c++) {
+        if (c >= 1) {  // the dS lo buffer is free once the dQ products of chunk c - 1 ran
+          if (issuer) *sm_ok = mbar_wait(dsl_free, (c - 1) & 1, flags, 161) ? 1 : 0;
+          softmax_sync();
+          ok = *sm_ok != 0;
+          if (!ok) break;
+        }
+        const int cc = 2 * c + half;
         uint8_t* prow = smem + cc * S::P_SLAB + row * 128;
+        uint8_t* lrow = smem + D::DL + half * S::P_SLAB + row * 128;
         if (cc * 32 <= warp_last) {  // warp-uniform
           float g[32];
           tmem_ld32(trow + cc * 32, g);
 #pragma unroll
           for (int k = 0; k < 8; k++) {
-            float4* pp = reinterpret_cast<float4*>(prow + ((k ^ (row & 7)) * 16));
+            const int off = (k ^ (row & 7)) * 16;
+            float4* pp = reinterpret_cast<float4*>(prow + off);
             const float4 p = *pp;
             const int j = cc * 32 + 4 * k;
-            *pp = make_float4(j + 0 < n ? p.x * (g[4 * k + 0] - D) * scale : 0.f,
-                              j + 1 < n ? p.y * (g[4 * k + 1] - D) * scale : 0.f,
-                              j + 2 < n ? p.z * (g[4 * k + 2] - D) * scale : 0.f,
-                              j + 3 < n ? p.w * (g[4 * k + 3] - D) * scale : 0.f);
+            const float4 x = make_float4(j + 0 < n ? p.x * (g[4 * k + 0] - Dsum) * scale : 0.f,
+                                         j + 1 < n ? p.y * (g[4 * k + 1] - Dsum) * scale : 0.f,
+                                         j + 2 < n ? p.z * (g[4 * k + 2] - Dsum) * scale : 0.f,
+                                         j + 3 < n ? p.w * (g[4 * k + 3] - Dsum) * scale : 0.f);
+            *pp = x;
+            *reinterpret_cast<float4*>(lrow + off) = lo4(x);
           }
         } else {
 #pragma unroll
-          for (int k = 0; k < 8; k++) *reinterpret_cast<float4*>(prow + 16 * k) = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int k = 0; k < 8; k++) {
+            *reinterpret_cast<float4*>(prow + 16 * k) = make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(lrow + 16 * k) = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        softmax_sync();
+        if (issuer) {
+          for (int hh = 0; hh < 2; hh++)
+            if ((2 * c + hh) * 32 < pitch)
+              tma_store_4d(&tmS, smem_u32(smem) + (2 * c + hh) * S::P_SLAB, (2 * c + hh) * 32, q0, h, b);
+          bulk_commit();
+          mbar_arrive(ds_ready);
         }
       }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      softmax_sync();
-      if (issuer) {
-        for (int sl = 0; sl < nkr / 32; sl++)
-          if (sl * 32 < pitch) tma_store_4d(&tmS, smem_u32(smem) + sl * S::P_SLAB, sl * 32, q0, h, b);
-        bulk_commit();
-      }
-      // columns [nkr, pitch): zeros from a zeroed slab past the ones just stored
-      if (nkr < pitch) {
+      // columns [nkr, pitch) of dS: zeros from a zeroed slab past the tile's chunks
+      if (ok && nkr < pitch) {
         uint8_t* z = smem + (nkr / 32) * S::P_SLAB + row * 128 + half * 64;
 #pragma unroll
         for (int k = 0; k < 4; k++) *reinterpret_cast<float4*>(z + 16 * k) = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -526,13 +619,41 @@ __global__ void __launch_bounds__(kFThreads, 1)
         }
       }
     }
+    if (ok) {
+      if (issuer) *sm_ok = mbar_wait(dq_full, 0, flags, 162) ? 1 : 0;
+      softmax_sync();
+      ok = *sm_ok != 0;
+    }
+    if (ok) {
+      tc_fence_after();
+      const bool store = i < T;
+      float* orow = dq + ((long)b * T + (store ? i : 0)) * ld_dq + (long)h * HD;
+      for (int d0 = half * 32; d0 < HD; d0 += 64) {  // warp-uniform
+        float v[32];
+        tmem_ld32(trow + kFTmemO + d0, v);
+        if (rope && store) {  // rotate back by -theta (pairs (2p, 2p + 1), theta of position i)
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const float2 cs = rope[(long)i * (HD / 2) + (d0 + j) / 2];
+            const float g0 = v[j], g1 = v[j + 1];
+            v[j] = g0 * cs.x + g1 * cs.y;
+            v[j + 1] = -g0 * cs.y + g1 * cs.x;
+          }
+        }
+        if (store) {
+#pragma unroll
+          for (int g = 0; g < 8; g++)
+            *reinterpret_cast<float4*>(orow + d0 + 4 * g) = make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+        }
+      }
+    }
     if (issuer) bulk_wait_all();
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kFTmemCols) : "memory");
   }
 }
 
@@ -556,16 +677,18 @@ int launch_fused(cudaStream_t st, const CUtensorMap& mq, const CUtensorMap& mk, 
 
 template <int HD>
 int launch_dsoftmax(cudaStream_t st, const CUtensorMap& mo, const CUtensorMap& mv, const CUtensorMap& mp,
-                    const CUtensorMap& ms, long pitch, int B, int T, int H, float scale, int* flags) {
-  using S = FShape<HD>;
+                    const CUtensorMap& ms, const CUtensorMap& mk, long pitch, float* dq, long ld_dq,
+                    const float2* rope, int B, int T, int H, float scale, int* flags) {
+  using Dsh = DShape<HD>;
+  static_assert(Dsh::SMEM <= 232448, "fused softmax backward: shared memory budget exceeded");
   auto kfn = k_attn_dsoftmax_fused<HD>;
   static bool attr = false;
   if (!attr) {
-    TURT_CHECK_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM));
+    TURT_CHECK_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, Dsh::SMEM));
     attr = true;
   }
-  TURT_CHECK_CUDA((launch_pdl(kfn, dim3(ceil_div(T, kFQ), B * H), dim3(kFThreads), S::SMEM, st, mo, mv, mp, ms, pitch,
-                              T, H, scale, flags)));
+  TURT_CHECK_CUDA((launch_pdl(kfn, dim3(ceil_div(T, kFQ), B * H), dim3(kFThreads), Dsh::SMEM, st, mo, mv, mp, ms, mk,
+                              pitch, dq, ld_dq, rope, T, H, scale, flags)));
   TURT_LAUNCH_CHECK();
   return OK;
 }
@@ -582,17 +705,19 @@ GemmOperand score_operand(const float* base, int T, int H, long pitch) {
 
 }  // namespace
 
-int attention_fused_dsoftmax(cudaStream_t st, const GemmOperand& dout, const GemmOperand& v, const float* P, float* dS,
-                             long pitch, int B, int T, int H, int hd, float scale, int* flags) {
+int attention_fused_dsoftmax(cudaStream_t st, const GemmOperand& dout, const GemmOperand& v, const GemmOperand& k,
+                             const float* P, float* dS, long pitch, float* dq, long ld_dq, const float2* rope, int B,
+                             int T, int H, int hd, float scale, int* flags) {
   TURT_REQUIRE(attention_fused_supported(T, hd), "fused attention: needs T <= 256 and a head dim of 32 or 64");
   TURT_REQUIRE(pitch % 4 == 0 && pitch >= T, "fused attention: bad probability row pitch");
-  CUtensorMap mo, mv, mp, ms;
+  CUtensorMap mo, mv, mp, ms, mk;
   RC(tensor_map_f32(&mo, dout, hd, T, H, B * H, 32, kFQ, false));
   RC(tensor_map_f32(&mv, v, hd, T, H, B * H, 32, 128, false));
   RC(tensor_map_f32(&mp, score_operand(P, T, H, pitch), pitch, T, H, B * H, 32, kFQ, false));
   RC(tensor_map_f32(&ms, score_operand(dS, T, H, pitch), pitch, T, H, B * H, 32, kFQ, false));
-  if (hd == 64) return launch_dsoftmax<64>(st, mo, mv, mp, ms, pitch, B, T, H, scale, flags);
-  return launch_dsoftmax<32>(st, mo, mv, mp, ms, pitch, B, T, H, scale, flags);
+  RC(tensor_map_f32(&mk, k, hd, T, H, B * H, 32, 32, true));
+  if (hd == 64) return launch_dsoftmax<64>(st, mo, mv, mp, ms, mk, pitch, dq, ld_dq, rope, B, T, H, scale, flags);
+  return launch_dsoftmax<32>(st, mo, mv, mp, ms, mk, pitch, dq, ld_dq, rope, B, T, H, scale, flags);
 }
 
 bool attention_fused_supported(int T, int hd) { return T >= 1 && T <= kFKeys && (hd == 32 || hd == 64); }

@@ -350,8 +350,11 @@ int attention_tc_bwd(cudaStream_t st, const float* qkv, const float2* rope_cs, c
   const int E = H * hd, BH = B * H;
   const float scale = 1.0f / sqrtf((float)hd);
   const Views w = views(qkv, dout, at, at.P, T, H, hd, rope != 0);
-  if (precision == GEMM_TF32X3 && attention_fused_supported(T, hd)) {
-    RC(attention_fused_dsoftmax(st, w.dout, w.v, at.P, sc.dS, w.pitch, B, T, H, hd, scale, flags));
+  const bool fused = precision == GEMM_TF32X3 && attention_fused_supported(T, hd);
+  if (fused) {
+    // dS and dQ (-> dqkv[:, 0:E), rotated back for RoPE) in one kernel
+    RC(attention_fused_dsoftmax(st, w.dout, w.v, w.k, at.P, sc.dS, w.pitch, dqkv, 3L * E, rope ? rope_cs : nullptr, B,
+                                T, H, hd, scale, flags));
   } else {
     // dP = dO v^T
     RC(gemm_tf32(st, T, T, hd, BH, w.dout, w.v, scores_epi(sc.dS, T, H, w.pitch), flags, precision));
@@ -374,7 +377,7 @@ int attention_tc_bwd(cudaStream_t st, const float* qkv, const float2* rope_cs, c
     e.rope = rope_cs;
     e.rope_hd = hd;
   }
-  RC(gemm_tf32(st, T, hd, T, BH, dS, mn(w.k), e, flags, precision));
+  if (!fused) RC(gemm_tf32(st, T, hd, T, BH, dS, mn(w.k), e, flags, precision));
   e.C = dqkv + E;
   e.causal = CAUSAL_K_UPPER;
   RC(gemm_tf32(st, T, hd, T, BH, dST, mn(w.q), e, flags, precision));
