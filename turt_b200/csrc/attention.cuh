@@ -44,6 +44,11 @@ int attention_fused_fwd(cudaStream_t st, const GemmOperand& q, const GemmOperand
 int attention_fused_dsoftmax(cudaStream_t st, const GemmOperand& dout, const GemmOperand& v, const GemmOperand& k,
                              const float* P, float* dS, long pitch, float* dq, long ld_dq, const float2* rope, int B,
                              int T, int H, int hd, float scale, int* flags);
+// dV = P^T dout -> dqkv[:, 2E:3E) and dK = dS^T q -> dqkv[:, E:2E) (rotated back with `rope`
+// when it is not null), in one kernel (same limits).
+int attention_fused_dkv(cudaStream_t st, const float* P, const float* dS, long pitch, const GemmOperand& dout,
+                        const GemmOperand& q, float* dqkv, long ld, const float2* rope, int B, int T, int H, int hd,
+                        int* flags);
 int attention_tc_bwd(cudaStream_t st, const float* qkv, const float2* rope_cs, const float* dout,
                      const AttnTensors& at, const AttnScratch& sc, float* dqkv, int B, int T, int H, int hd, int rope,
                      int* flags, int precision);

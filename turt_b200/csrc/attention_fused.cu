@@ -703,6 +703,187 @@ GemmOperand score_operand(const float* base, int T, int H, long pitch) {
   return o;
 }
 
+
+// dV = P^T dO and dK = dS^T q for T <= 256 in one kernel: one CTA per (key tile of 128, batch
+// entry, head) runs both products over the query slabs from the tile's first key on (the
+// causal blocks; P and dS are zero right of the diagonal), two TMEM accumulators, one k-loop:
+// per 32-query slab P^T and dS^T arrive as MN-major A tiles and dO, q as MN-major B tiles by
+// TMA, the converters split lo parts, and the issuer runs 2 x 3 MMAs per 8 queries.  The
+// epilogue writes dV and dK (rotated back by -theta for RoPE) into dqkv.  Replaces the two
+// batched per-head GEMMs.
+template <int HD>
+struct KVShape {
+  static constexpr int A_BYTES = 4 * 32 * 32 * 4;        // 128 keys x 32 queries (4 MN boxes)
+  static constexpr int B_BYTES = (HD / 32) * 32 * 32 * 4;  // 32 queries x HD
+  static constexpr int HI = 2 * A_BYTES + 2 * B_BYTES;      // P^T, dS^T, dO, q
+  static constexpr int STAGE = 2 * HI;                      // + lo parts
+  static constexpr int STAGES = 2;
+  static constexpr int SMEM = STAGES * STAGE + 256 + 1024;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(320, 1)
+    k_attn_dkv_fused(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmS,
+                     const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmQ,
+                     float* __restrict__ dqkv, long ld, const float2* __restrict__ rope, int T, int H, int* flags) {
+  using S = KVShape<HD>;
+  constexpr int MN_BOX = 32 * 32 * 4;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::STAGES * S::STAGE);
+  uint64_t* full = bars;        // [2]
+  uint64_t* conv = bars + 2;    // [2]
+  uint64_t* empty = bars + 4;   // [2]
+  uint64_t* acc_full = bars + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
+  constexpr uint32_t kCols = 256;  // dV at [0, HD), dK at [128, 128 + HD)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y, b = bh / H, h = bh % H, E = H * HD;
+  const int j0 = blockIdx.x * 128;         // first key of the tile
+  const int nsl = (T - j0 + 31) / 32;      // query slabs from query j0 on
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int sl = 0; sl < nsl; sl++) {
+        const int s = sl & 1;
+        if (sl >= 2 && !mbar_wait(&empty[s], ((sl >> 1) - 1) & 1, flags, 171)) break;
+        const uint32_t base = smem_u32(smem + s * S::STAGE);
+        const int i0 = j0 + sl * 32;  // first query of the slab
+        mbar_arrive_expect_tx(&full[s], S::HI);
+        for (int jb = 0; jb < 4; jb++) {
+          tma_load_4d(base + jb * MN_BOX, &tmP, j0 + 32 * jb, i0, h, b, &full[s]);
+          tma_load_4d(base + S::A_BYTES + jb * MN_BOX, &tmS, j0 + 32 * jb, i0, h, b, &full[s]);
+        }
+        for (int db = 0; db < HD / 32; db++) {
+          tma_load_4d(base + 2 * S::A_BYTES + db * MN_BOX, &tmO, 32 * db, i0, h, b, &full[s]);
+          tma_load_4d(base + 2 * S::A_BYTES + S::B_BYTES + db * MN_BOX, &tmQ, 32 * db, i0, h, b, &full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | (1u << 15) | (1u << 16) |
+                                 ((uint32_t)(HD >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+      bool ok = true;
+      for (int sl = 0; sl < nsl; sl++) {
+        const int s = sl & 1;
+        if (!mbar_wait(&conv[s], (sl >> 1) & 1, flags, 172)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t base = smem_u32(smem + s * S::STAGE);
+        const uint64_t lo = (uint64_t)(S::HI >> 4);
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+          const uint32_t first = (sl > 0 || kk > 0) ? 1u : 0u;
+          const uint64_t dp = smem_desc(base + kk * 1024, MN_BOX, 512, kLayoutSW128Atom32);
+          const uint64_t ds = smem_desc(base + S::A_BYTES + kk * 1024, MN_BOX, 512, kLayoutSW128Atom32);
+          const uint64_t dO = smem_desc(base + 2 * S::A_BYTES + kk * 1024, MN_BOX, 512, kLayoutSW128Atom32);
+          const uint64_t dq = smem_desc(base + 2 * S::A_BYTES + S::B_BYTES + kk * 1024, MN_BOX, 512, kLayoutSW128Atom32);
+          mma_tf32(tmem, dp + lo, dO, idesc, first);
+          mma_tf32(tmem, dp, dO + lo, idesc, 1u);
+          mma_tf32(tmem, dp, dO, idesc, 1u);
+          mma_tf32(tmem + 128, ds + lo, dq, idesc, first);
+          mma_tf32(tmem + 128, ds, dq + lo, idesc, 1u);
+          mma_tf32(tmem + 128, ds, dq, idesc, 1u);
+        }
+        mma_commit(&empty[s]);
+      }
+      if (ok) mma_commit(acc_full);
+    }
+  } else if (warp >= 6) {
+    const int ct = threadIdx.x - 192;
+    for (int sl = 0; sl < nsl; sl++) {
+      const int s = sl & 1;
+      if (!mbar_wait(&full[s], (sl >> 1) & 1, flags, 173)) break;
+      lo_split(smem + s * S::STAGE, S::HI, S::HI, ct);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&conv[s]);
+    }
+  } else {
+    // epilogue: warp w holds keys j0 + 32*(w%4) + lane
+    const int q = warp & 3;
+    const int j = j0 + q * 32 + lane;
+    if (mbar_wait(acc_full, 0, flags, 174)) {
+      tc_fence_after();
+      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+      const bool store = j < T;
+      float* row = dqkv + ((long)b * T + (store ? j : 0)) * ld;
+#pragma unroll 1
+      for (int which = 0; which < 2; which++) {  // 0: dV -> [2E, 3E), 1: dK -> [E, 2E)
+#pragma unroll 1
+        for (int d0 = 0; d0 < HD; d0 += 32) {
+          float v[32];
+          tmem_ld32(trow + which * 128 + d0, v);
+          if (which == 1 && rope && store) {  // rotate back by -theta of key position j
+#pragma unroll
+            for (int t = 0; t < 32; t += 2) {
+              const float2 cs = rope[(long)j * (HD / 2) + (d0 + t) / 2];
+              const float g0 = v[t], g1 = v[t + 1];
+              v[t] = g0 * cs.x + g1 * cs.y;
+              v[t + 1] = -g0 * cs.y + g1 * cs.x;
+            }
+          }
+          if (store) {
+            float* dst = row + (which == 0 ? 2 * E : E) + h * HD + d0;
+#pragma unroll
+            for (int g = 0; g < 8; g++)
+              *reinterpret_cast<float4*>(dst + 4 * g) = make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+  }
+}
+
+template <int HD>
+int launch_dkv(cudaStream_t st, const CUtensorMap& mp, const CUtensorMap& ms, const CUtensorMap& mo,
+               const CUtensorMap& mq, float* dqkv, long ld, const float2* rope, int B, int T, int H, int* flags) {
+  using Sh = KVShape<HD>;
+  static_assert(Sh::SMEM <= 232448, "fused dK/dV: shared memory budget exceeded");
+  auto kfn = k_attn_dkv_fused<HD>;
+  static bool attr = false;
+  if (!attr) {
+    TURT_CHECK_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, Sh::SMEM));
+    attr = true;
+  }
+  TURT_CHECK_CUDA((launch_pdl(kfn, dim3(ceil_div(T, 128), B * H), dim3(320), Sh::SMEM, st, mp, ms, mo, mq, dqkv, ld,
+                              rope, T, H, flags)));
+  TURT_LAUNCH_CHECK();
+  return OK;
+}
+
 }  // namespace
 
 int attention_fused_dsoftmax(cudaStream_t st, const GemmOperand& dout, const GemmOperand& v, const GemmOperand& k,
@@ -718,6 +899,21 @@ int attention_fused_dsoftmax(cudaStream_t st, const GemmOperand& dout, const Gem
   RC(tensor_map_f32(&mk, k, hd, T, H, B * H, 32, 32, true));
   if (hd == 64) return launch_dsoftmax<64>(st, mo, mv, mp, ms, mk, pitch, dq, ld_dq, rope, B, T, H, scale, flags);
   return launch_dsoftmax<32>(st, mo, mv, mp, ms, mk, pitch, dq, ld_dq, rope, B, T, H, scale, flags);
+}
+
+int attention_fused_dkv(cudaStream_t st, const float* P, const float* dS, long pitch, const GemmOperand& dout,
+                        const GemmOperand& q, float* dqkv, long ld, const float2* rope, int B, int T, int H, int hd,
+                        int* flags) {
+  TURT_REQUIRE(attention_fused_supported(T, hd), "fused attention: needs T <= 256 and a head dim of 32 or 64");
+  TURT_REQUIRE(pitch % 4 == 0 && pitch >= T, "fused attention: bad probability row pitch");
+  CUtensorMap mp, ms, mo, mq;
+  // P^T / dS^T: MN-major A tiles (keys contiguous within a query row)
+  RC(tensor_map_f32(&mp, score_operand(P, T, H, pitch), pitch, T, H, B * H, 32, 32, true));
+  RC(tensor_map_f32(&ms, score_operand(dS, T, H, pitch), pitch, T, H, B * H, 32, 32, true));
+  RC(tensor_map_f32(&mo, dout, hd, T, H, B * H, 32, 32, true));
+  RC(tensor_map_f32(&mq, q, hd, T, H, B * H, 32, 32, true));
+  if (hd == 64) return launch_dkv<64>(st, mp, ms, mo, mq, dqkv, ld, rope, B, T, H, flags);
+  return launch_dkv<32>(st, mp, ms, mo, mq, dqkv, ld, rope, B, T, H, flags);
 }
 
 bool attention_fused_supported(int T, int hd) { return T >= 1 && T <= kFKeys && (hd == 32 || hd == 64); }

@@ -361,6 +361,9 @@ int attention_tc_bwd(cudaStream_t st, const float* qkv, const float2* rope_cs, c
     // dS = P (dP - rowsum(P dP)) * scale, in place
     RC(rows_launch(st, (long)BH * T, T, w.pitch, scale, sc.dS, at.P, true));
   }
+  if (fused)  // dV and dK in one kernel as well
+    return attention_fused_dkv(st, at.P, sc.dS, w.pitch, w.dout, w.q, dqkv, 3L * E, rope ? rope_cs : nullptr, B, T, H,
+                               hd, flags);
   GemmOperand dS = w.P, dST = w.PT;
   dS.ptr = sc.dS;
   dST.ptr = sc.dS;
