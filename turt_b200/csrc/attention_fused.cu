@@ -114,8 +114,10 @@ __global__ void __launch_bounds__(kFThreads, 1)
   float* red = reinterpret_cast<float*>(smem + S::REGION + 256);          // [2 halves][128 rows]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y, b = bh / H, h = bh % H;
-  const int q0 = blockIdx.x * kFQ;
+  // grid (heads, query tiles), the last (longest: most keys) query tiles first: CTAs dispatch
+  // x-fastest, so the short tiles fill the tail of the last wave
+  const int bh = blockIdx.x, b = bh / H, h = bh % H;
+  const int q0 = (gridDim.y - 1 - blockIdx.y) * kFQ;
   const int nk = min(T, q0 + kFQ);          // keys any row of this tile can see
   const int nkr = (nk + 63) & ~63;          // rounded up to whole 64-key chunks (<= 256)
   const int nch = nkr / 64;
@@ -409,8 +411,10 @@ __global__ void __launch_bounds__(kFThreads, 1)
   float* red = reinterpret_cast<float*>(smem + D::REGION + 256);  // [2 halves][128 rows]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y, b = bh / H, h = bh % H;
-  const int q0 = blockIdx.x * kFQ;
+  // grid (heads, query tiles), the last (longest: most keys) query tiles first: CTAs dispatch
+  // x-fastest, so the short tiles fill the tail of the last wave
+  const int bh = blockIdx.x, b = bh / H, h = bh % H;
+  const int q0 = (gridDim.y - 1 - blockIdx.y) * kFQ;
   const int nk = min(T, q0 + kFQ);
   const int nkr = (nk + 63) & ~63;
   const int nch = nkr / 64;
@@ -669,7 +673,7 @@ int launch_fused(cudaStream_t st, const CUtensorMap& mq, const CUtensorMap& mk, 
     TURT_CHECK_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM));
     attr = true;
   }
-  TURT_CHECK_CUDA((launch_pdl(kfn, dim3(ceil_div(T, kFQ), B * H), dim3(kFThreads), S::SMEM, st, mq, mk, mv, mp, pitch,
+  TURT_CHECK_CUDA((launch_pdl(kfn, dim3(B * H, ceil_div(T, kFQ)), dim3(kFThreads), S::SMEM, st, mq, mk, mv, mp, pitch,
                               out, ld_out, T, H, scale, flags)));
   TURT_LAUNCH_CHECK();
   return OK;
@@ -687,7 +691,7 @@ int launch_dsoftmax(cudaStream_t st, const CUtensorMap& mo, const CUtensorMap& m
     TURT_CHECK_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, Dsh::SMEM));
     attr = true;
   }
-  TURT_CHECK_CUDA((launch_pdl(kfn, dim3(ceil_div(T, kFQ), B * H), dim3(kFThreads), Dsh::SMEM, st, mo, mv, mp, ms, mk,
+  TURT_CHECK_CUDA((launch_pdl(kfn, dim3(B * H, ceil_div(T, kFQ)), dim3(kFThreads), Dsh::SMEM, st, mo, mv, mp, ms, mk,
                               pitch, dq, ld_dq, rope, T, H, scale, flags)));
   TURT_LAUNCH_CHECK();
   return OK;
@@ -739,8 +743,9 @@ __global__ void __launch_bounds__(320, 1)
   constexpr uint32_t kCols = 256;  // dV at [0, HD), dK at [128, 128 + HD)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y, b = bh / H, h = bh % H, E = H * HD;
-  const int j0 = blockIdx.x * 128;         // first key of the tile
+  // grid (heads, key tiles): the first key tiles (the most query slabs) dispatch first
+  const int bh = blockIdx.x, b = bh / H, h = bh % H, E = H * HD;
+  const int j0 = blockIdx.y * 128;         // first key of the tile
   const int nsl = (T - j0 + 31) / 32;      // query slabs from query j0 on
 
   if (threadIdx.x == 0) {
@@ -878,7 +883,7 @@ int launch_dkv(cudaStream_t st, const CUtensorMap& mp, const CUtensorMap& ms, co
     TURT_CHECK_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, Sh::SMEM));
     attr = true;
   }
-  TURT_CHECK_CUDA((launch_pdl(kfn, dim3(ceil_div(T, 128), B * H), dim3(320), Sh::SMEM, st, mp, ms, mo, mq, dqkv, ld,
+  TURT_CHECK_CUDA((launch_pdl(kfn, dim3(B * H, ceil_div(T, 128)), dim3(320), Sh::SMEM, st, mp, ms, mo, mq, dqkv, ld,
                               rope, T, H, flags)));
   TURT_LAUNCH_CHECK();
   return OK;
