@@ -132,10 +132,28 @@ def cpu_pool_sample(w, workers: int, seed: int):
     return step, n
 
 
+def cpu_info():
+    """Host CPU as the CPU baselines report it: logical cores (nproc) and the model name."""
+    model = None
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"nproc": os.cpu_count(), "cpu_model": model}
+
+
+def pool_workers(w) -> int:
+    """W = host cores - 2 worker threads, capped at the batch (scripts/train-gpt.ts:162)."""
+    return max(1, min((os.cpu_count() or 4) - 2, w["batch"]))
+
+
 def run_reference(args, w, rank: int) -> None:
     if rank != 0:
         return
-    workers = max(1, min((os.cpu_count() or 4) - 2, w["batch"]))
+    workers = pool_workers(w)
     step, tokens = cpu_pool_sample(w, workers, 1)
     for k in range(args.warmup):
         step(k + 1)
@@ -149,8 +167,11 @@ def run_reference(args, w, rank: int) -> None:
         "config": {"workload": args.workload, "model": args.workload, "global_batch": workers, "seq_len": w["T"],
                    "parallelism": f"cpu-dp{workers}"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": workers, "kind": "port",
+                         "workers": workers, **cpu_info(),
                          "sample": f"{workers} sequences x {w['T']} tokens per step (one per worker thread), "
-                                   f"C restatement of the reference worker pool"},
+                                   f"C restatement of the reference worker pool",
+                         "batch_note": "the pool trains one sequence per worker thread per step, the GPU arm "
+                                       f"{w['batch']} per GPU; tokens/s normalises the batch size"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -352,13 +373,29 @@ def run_gpu(args, w, rank: int, world: int, local_rank: int) -> None:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        workers = max(1, min((os.cpu_count() or 4) - 2, w["batch"]))
+        workers = pool_workers(w)
         step, tokens = cpu_pool_sample(w, workers, 2)
         secs = step(1)
+        # the single-thread variant: one sequence on one core (the reference's CPU train step
+        # without the worker pool)
+        step1, tokens1 = cpu_pool_sample(w, 1, 3)
+        secs1 = step1(1)
+        tiny = WORKLOADS["gpt-tiny-4L-128d"]
+        wt = pool_workers(tiny)
+        step_t, tokens_t = cpu_pool_sample(tiny, wt, 4)
+        secs_t = step_t(1)
         out["cpu_baseline"] = {"value": tokens / secs, "unit": "tokens/s", "cores": workers, "kind": "port",
+                               "workers": workers, **cpu_info(),
                                "sample": f"one reference CPU data-parallel step over {workers} sequences x {w['T']} "
                                          f"tokens ({workers} worker threads, C restatement of "
-                                         f"scripts/train-gpt.ts + train-worker.ts)"}
+                                         f"scripts/train-gpt.ts + train-worker.ts)",
+                               "single_thread": {"value": tokens1 / secs1, "unit": "tokens/s", "cores": 1,
+                                                 "sample": f"one sequence of {w['T']} tokens on one thread"},
+                               "tiny_4L_128d": {"value": tokens_t / secs_t, "unit": "tokens/s", "cores": wt,
+                                                "sample": f"one pool step over {wt} sequences x {tiny['T']} tokens "
+                                                          "of the 4-layer / 128-d modern GPT"},
+                               "batch_note": f"the pool trains {workers} sequences per step, the GPU {global_seqs}; "
+                                             "tokens/s normalises the batch size"}
     if out is not None:
         print(json.dumps(out), flush=True)
 

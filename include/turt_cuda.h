@@ -8,7 +8,9 @@
  * everything else is host memory.  No C++ or torch types cross this boundary.
  *
  * The reference interfaces each group replaces are cited as path:line inside the turt
- * project (TypeScript); INTEGRATION.md shows the Deno.dlopen binding for each symbol.
+ * project (TypeScript).  A TypeScript host binds each symbol with Deno.dlopen (or a Node
+ * N-API shim) using the C types declared here: pointers as "buffer" / "pointer", int as "i32",
+ * size_t as "usize", float / double as "f32" / "f64".
  */
 #ifndef TURT_CUDA_H
 #define TURT_CUDA_H
@@ -50,6 +52,13 @@ int turt_ctx_set_stream(turt_ctx* ctx, void* stream);
 void* turt_ctx_stream(turt_ctx* ctx);
 /* Waits for the context's stream and reports device-side error flags (range, timeout). */
 int turt_synchronize(turt_ctx* ctx);
+/* Self-test of the bounded device wait that every tcgen05 kernel of this library uses: one
+ * thread waits on a shared-memory mbarrier that nothing completes, gives up after limit_us
+ * microseconds (1 .. 1,000,000), raises the context's timeout flag and returns, so the call
+ * returns TURT_ERR_TIMEOUT and the context stays usable.  No reference counterpart: the
+ * reference can only notice a failed GPU step through a loss of exactly 0
+ * (scripts/gpu-pretrain.ts:232-238). */
+int turt_wait_selftest(turt_ctx* ctx, int limit_us);
 /* Precision of every GEMM issued through this context:
  * TURT_PRECISION_TF32X3 (default) = error-compensated 3xTF32 on the tensor cores (~2^-20
  * relative per product), meets the reference's gradient tolerance;
@@ -164,20 +173,21 @@ int turt_adamw(turt_ctx* ctx, const float* grad, float* param, float* m, float* 
  * src/infer/backend.ts:11-16 / gpu-backend.ts:45-55: host arrays in, host array out. */
 int turt_host_matmul(turt_ctx* ctx, const float* a, int m, int k, const float* b, int n, float* out);
 int turt_host_bmm(turt_ctx* ctx, const float* a, int batch, int m, int k, const float* b, int n, float* out);
-/* No counterpart in the reference.  Same product as turt_host_matmul, for callers that cannot
- * let the library allocate device memory during the call (a process whose device memory is
- * held by another framework's caching allocator, or a latency-bound host that must not
- * allocate after start-up): A, B and C are staged in one fixed 8 MiB device array owned by
- * the library (every GPU that loads it holds the array until exit) instead of per-call
- * buffers.  Products whose padded A + B + C exceed 2 Mi floats are rejected with
- * TURT_ERR_INVALID.  The first call on a device looks up the array's device address (call it
- * once before any stream capture).  All calls share the array; calls that overlap on the GPU
- * race on it. */
+/* No counterpart in the reference.  Same product as turt_host_matmul (at the context's
+ * precision), for callers that cannot let the library allocate device memory during the call
+ * (a process whose device memory is held by another framework's caching allocator, or a
+ * latency-bound host that must not allocate after start-up): A, B and C are staged in one
+ * fixed 8 MiB device array owned by the library instead of per-call buffers.  turt_init
+ * reserves the array on its device and looks up its address, so no call of this entry point
+ * allocates; the device holds the array until the process exits.  Products whose staged
+ * A + B + C (rows padded to 4 floats on the tensor-core paths, each part rounded up to 64
+ * floats) exceed 2 Mi floats are rejected with TURT_ERR_INVALID.  All calls share the array;
+ * calls that overlap on the GPU race on it. */
 int turt_host_matmul_noalloc(turt_ctx* ctx, const float* a, int m, int k, const float* b, int n, float* out);
 
 /* -------------------------------------------------------------- model level
- * GpuGPT, src/models/gpu-gpt.ts:54-202 (+ GPTConfig, src/models/gpt.ts:67-78) with the
- * AdamW / clipGradNorm step of scripts/gpu-pretrain.ts:502-521 and scripts/train-gpt.ts:241-242. */
+ * GpuGPT, src/models/gpu-gpt.ts:54-202 (+ GPTConfig, src/models/gpt.ts:40-51) with the
+ * AdamW / clipGradNorm step of scripts/gpu-pretrain.ts:204-224 and scripts/train-gpt.ts:241-242. */
 typedef struct turt_config {
   int vocab_size;
   int block_size;
@@ -220,7 +230,7 @@ int turt_model_init(turt_model* model, uint32_t seed);
  * restarts them at zero on --resume (:171-173); these let a checkpoint carry them. */
 int turt_adam_state_download(turt_model* model, int index, float* m, float* v, size_t n);
 int turt_adam_state_upload(turt_model* model, int index, const float* m, const float* v, size_t n);
-/* zeroGrad on every parameter (gpu-gpt usage: scripts/gpu-pretrain.ts:502). */
+/* zeroGrad on every parameter (gpu-gpt usage: scripts/gpu-pretrain.ts:205). */
 int turt_zero_grad(turt_model* model);
 /* GpuGPT.loss + backward (gpu-gpt.ts:185-201, autograd.ts:1196-1209): accumulates
  * loss_scale * d(mean CE)/d(theta) into the gradients.  ids/targets are host arrays of b*t
@@ -235,7 +245,7 @@ int turt_forward_backward_device(turt_model* model, const uint32_t* d_ids, const
 int turt_read_loss(turt_model* model, float* loss_out);
 /* Number of kernels this library has launched in the process (all contexts). */
 int turt_launch_count(uint64_t* count);
-/* Forward only (evaluation loss), gpu-pretrain.ts:485-497. */
+/* Forward only (evaluation loss), gpu-pretrain.ts:188-200. */
 int turt_forward(turt_model* model, const uint32_t* ids, const uint32_t* targets, int b, int t, float* loss_out);
 /* turt_forward with ids / targets already in device memory (uint32[b*t] each); synchronizes
  * to return the mean loss.  The pretraining eval loss (scripts/gpu-pretrain.ts:188-200) runs it

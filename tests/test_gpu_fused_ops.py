@@ -3,7 +3,8 @@
 RMSNorm backward (RMS_DX + RMS_DG, autograd.ts:331-365, with the residual gradient added),
 SwiGLU backward (SILU_BWD and the gate*up product rule), fused softmax cross-entropy
 (CE_FWD + CE_BWD, autograd.ts:441-471) and AdamW with global-norm clipping (adam.ts:31-54,
-clip.ts:7-24).  The kernels compute in fp32; the oracle, like the reference's JavaScript, in
+clip.ts:7-24).  The first case of each test is the standalone backward-op benchmark's full
+shape: RMSNorm [8192,384], SwiGLU [8192,1024], softmax-CE [8192,8192], AdamW over 10M.  The kernels compute in fp32; the oracle, like the reference's JavaScript, in
 doubles.  Two bounds: max|got - ref| / max|ref| <= 1e-5 (fp32 rounding of the tensor's scale)
 and the reference validator's maxRelErr (denominator max(1e-3, |a|, |b|)) <= 1e-3, which is
 what fp32 rounding of O(1) terms leaves on entries that cancel to ~1e-3 (an fp32 emulation of
@@ -46,7 +47,7 @@ def _dev(ctx, a):
     return p
 
 
-@pytest.mark.parametrize("rows,E", [(1024, 384), (100, 32), (37, 768)])
+@pytest.mark.parametrize("rows,E", [(8192, 384), (1024, 384), (100, 32), (37, 768)])
 @pytest.mark.parametrize("with_res", [False, True])
 def test_rms_bwd(ctx, orc, rows, E, with_res):
     from turt_b200._lib import check, lib
@@ -70,7 +71,7 @@ def test_rms_bwd(ctx, orc, rows, E, with_res):
     assert _ok(got_dg, ref_dg + dg0)
 
 
-@pytest.mark.parametrize("n", [8192 * 1024 // 64, 1003])
+@pytest.mark.parametrize("n", [8192 * 1024, 8192 * 1024 // 64, 1003])
 def test_swiglu_bwd(ctx, orc, n):
     from turt_b200._lib import check, lib
     rng = np.random.default_rng(n)
@@ -84,7 +85,7 @@ def test_swiglu_bwd(ctx, orc, n):
     assert _ok(ctx.download(du, n), ref_du)
 
 
-@pytest.mark.parametrize("N,V", [(256, 8192), (33, 48)])
+@pytest.mark.parametrize("N,V", [(8192, 8192), (256, 8192), (33, 48)])
 def test_ce_fused(ctx, orc, N, V):
     from turt_b200._lib import check, lib, u32
     rng = np.random.default_rng(N + V)
@@ -101,11 +102,11 @@ def test_ce_fused(ctx, orc, N, V):
     assert _ok(got_g, ref_g)
 
 
+@pytest.mark.parametrize("n", [10_000_000, 100_003])
 @pytest.mark.parametrize("clip", [0.0, 1.0])
-def test_adamw_clip(ctx, orc, clip):
+def test_adamw_clip(ctx, orc, clip, n):
     from turt_b200._lib import check, lib
     import ctypes as C
-    n = 100_003
     rng = np.random.default_rng(5)
     p, g, m = (rng.standard_normal(n).astype(np.float32) for _ in range(3))
     v = np.abs(rng.standard_normal(n)).astype(np.float32)

@@ -80,7 +80,7 @@ def test_matmul_batched(ctx, prec):
 
 @pytest.mark.parametrize("m,k,n", [(1, 1, 1), (16, 16, 16), (17, 33, 9), (64, 128, 384), (256, 160, 1024)])
 def test_host_matmul(ctx, m, k, n):
-    """scripts/gpu-bench.ts:239-245 correctness cases through the host-array entry point."""
+    """scripts/gpu-bench.ts:67-84 correctness cases through the host-array entry point."""
     from turt_b200._lib import check, lib, ptr
     rng = np.random.default_rng(m * 7 + k)
     a = rng.uniform(-1, 1, (m, k)).astype(np.float32)

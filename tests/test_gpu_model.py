@@ -196,3 +196,22 @@ def test_fused_attention_forward(ctx, orc, arch, E, H, t):
     loss, ref, le, ge, name = _run_parity(ctx, orc, 256, 256, 2, H, E, arch, 2, t, attn=1)
     assert le <= LOSS_TOL, (loss, ref)
     assert ge <= GRAD_TOL, (ge, name)
+
+
+def test_bounded_wait_times_out_and_context_survives(ctx, orc):
+    """A device wait that nothing completes gives up after its limit (1 ms here), the call
+    reports TURT_ERR_TIMEOUT, and the same context then runs a full train step correctly
+    (the reference only notices a failed step by a zero loss, scripts/gpu-pretrain.ts:232-238)."""
+    import time
+
+    from turt_b200._lib import ERR_TIMEOUT, lib, last_error
+    t0 = time.perf_counter()
+    rc = lib().turt_wait_selftest(ctx.handle, 1000)
+    elapsed = time.perf_counter() - t0
+    assert rc == ERR_TIMEOUT
+    assert "timed out" in last_error()
+    assert elapsed < 5.0
+    ctx.synchronize()  # the flag was cleared by the report
+    loss, ref, le, ge, name = _run_parity(ctx, orc, 48, 16, 2, 2, 32, "modern", 2, 8)
+    assert le <= LOSS_TOL, (loss, ref)
+    assert ge <= GRAD_TOL, (ge, name)

@@ -269,20 +269,20 @@ def test_gpt_tape_and_fused_match_oracle(eng, o, arch):
 
 
 def _rand_array(o, n, seed):
-    """randArray of scripts/gpu-bench.ts:206-218: mulberry32 uniforms mapped to [-1, 1)."""
+    """randArray of scripts/gpu-bench.ts:34-46: mulberry32 uniforms mapped to [-1, 1)."""
     st = o.rng(seed)
     return np.array([o.rng_next(st) * 2 - 1 for _ in range(n)], np.float32)
 
 
 def _max_rel_error(a, b):
-    """maxRelError of scripts/gpu-bench.ts:221-228 (denominator floor 1e-4)."""
+    """maxRelError of scripts/gpu-bench.ts:49-56 (denominator floor 1e-4)."""
     a, b = np.asarray(a, np.float64).ravel(), np.asarray(b, np.float64).ravel()
     return float(np.max(np.abs(a - b) / np.maximum(1e-4, np.maximum(np.abs(a), np.abs(b)))))
 
 
 @pytest.mark.parametrize("m,k,n", [(1, 1, 1), (16, 16, 16), (17, 33, 9), (64, 128, 384), (256, 160, 1024)])
 def test_backend_matmul(o, m, k, n):
-    """scripts/gpu-bench.ts:237-286: the GPU matmul against the reference's f32 CPU matmul
+    """scripts/gpu-bench.ts:64-116: the GPU matmul against the reference's f32 CPU matmul
     (i-k-j order, restated in the oracle) on the script's own inputs, tolerance 5e-3."""
     from turt_b200.engine import CudaBackend
     be = CudaBackend(0)
@@ -290,7 +290,7 @@ def test_backend_matmul(o, m, k, n):
     b = _rand_array(o, k * n, n * 13 + k).reshape(k, n)
     assert _max_rel_error(be.matmul(a, b), o.matmul(a, b)) <= 5e-3
     if (m, k, n) == (1, 1, 1):
-        # batched, attention-shaped (gpu-bench.ts:258-279)
+        # batched, attention-shaped (gpu-bench.ts:85-107)
         g, bm, bk, bn = 8, 128, 40, 128
         A = _rand_array(o, g * bm * bk, 3)
         B = _rand_array(o, g * bk * bn, 5)

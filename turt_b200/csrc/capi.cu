@@ -16,6 +16,7 @@ static thread_local std::string g_last_error;
 static std::atomic<uint64_t> g_launches{0};
 void note_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
 void set_error(const std::string& msg) { g_last_error = msg; }
+int noalloc_setup(int dev);  // noalloc.cu
 const char* last_error() { return g_last_error.c_str(); }
 
 int ctx_check_flags(turt_ctx* ctx) {
@@ -87,6 +88,9 @@ int turt_init(int device, turt_ctx** out) {
   c->own_stream = true;
   TURT_CHECK_CUDA(cudaMalloc(&c->flags, sizeof(int) * FLAG_COUNT));
   TURT_CHECK_CUDA(cudaMemset(c->flags, 0, sizeof(int) * FLAG_COUNT));
+  // Reserve turt_host_matmul_noalloc's fixed staging array now.  Best effort: a failure here
+  // is reported again by that entry point's first call, and is no reason to refuse a context.
+  if (noalloc_setup(device) != OK) (void)cudaGetLastError();
   *out = c;
   return OK;
 }

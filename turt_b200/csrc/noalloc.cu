@@ -8,10 +8,14 @@
 // (cudaMalloc can synchronize the device and its latency is unbounded).  For them,
 // turt_host_matmul_noalloc stages A, B and C in one fixed, file-scope device array instead.
 //
-// The array is kNoAllocScratchFloats floats (8 MiB) and is held by every GPU that loads
-// the library until the process exits.  All calls share it and it keeps the last call's
-// contents; each call overwrites every element it reads, so nothing needs clearing.
-// Calls that overlap on the GPU (from several host threads or streams) race on it.
+// The array is kNoAllocScratchFloats floats (8 MiB).  Each .cu file of the library is its
+// own CUDA module, and under CUDA's default lazy module loading a module's device memory is
+// reserved when the module is first used, not when the library is loaded.  So turt_init
+// looks the array's address up for its device (noalloc_setup): from then on the device holds
+// the array until the process exits, and no turt_host_matmul_noalloc call is the one that
+// reserves it.  All calls share it and it keeps the last call's contents; each call
+// overwrites every element it reads, so nothing needs clearing.  Calls that overlap on the
+// GPU (from several host threads or streams) race on it.
 #include <mutex>
 
 #include "../../include/turt_cuda.h"
@@ -49,6 +53,14 @@ int scratch_for_device(int dev, float** out) {
 inline size_t round64(size_t x) { return (x + 63) & ~size_t(63); }
 
 }  // namespace
+
+// Called by turt_init with `dev` current: loads this file's module and records the array's
+// device address, so the 8 MiB are reserved at context creation.
+int noalloc_setup(int dev) {
+  float* p = nullptr;
+  return scratch_for_device(dev, &p);
+}
+
 }  // namespace turt
 
 using namespace turt;
@@ -63,7 +75,11 @@ extern "C" int turt_host_matmul_noalloc(turt_ctx* ctx, const float* a, int m, in
   TURT_REQUIRE(a && b && out, "matmul: null array");
   TURT_REQUIRE(m >= 0 && k >= 0 && n >= 0, "matmul: negative dimension");
   if ((size_t)m * n == 0) return OK;
-  const size_t kp = ((size_t)k + 3) & ~size_t(3), np = ((size_t)n + 3) & ~size_t(3);
+  // Same staging as turt_host_bmm: the tensor-core path pitches rows to a multiple of 4 floats
+  // (TMA needs 16-byte pitches); the FP32 CUDA-core path keeps dense rows.
+  const bool simt = ctx->precision == 0;
+  const size_t kp = simt ? (size_t)k : ((size_t)k + 3) & ~size_t(3);
+  const size_t np = simt ? (size_t)n : ((size_t)n + 3) & ~size_t(3);
   const size_t need = round64((size_t)m * kp) + round64((size_t)k * np) + round64((size_t)m * np);
   if (need > kNoAllocScratchFloats) {
     set_error("turt_host_matmul_noalloc: [" + std::to_string(m) + "x" + std::to_string(k) + "] @ [" +
@@ -84,14 +100,18 @@ extern "C" int turt_host_matmul_noalloc(turt_ctx* ctx, const float* a, int m, in
   } else {
     TURT_CHECK_CUDA(cudaMemcpy2DAsync(da, kp * 4, a, (size_t)k * 4, (size_t)k * 4, m, cudaMemcpyHostToDevice, st));
     TURT_CHECK_CUDA(cudaMemcpy2DAsync(db, np * 4, b, (size_t)n * 4, (size_t)n * 4, k, cudaMemcpyHostToDevice, st));
-    GemmOperand A{da, (long)kp, (long)(m * kp), false};
-    GemmOperand B{db, (long)np, (long)(k * np), true};
-    GemmEpi epi;
-    epi.kind = EPI_STORE;
-    epi.C = dc;
-    epi.ldc = (long)np;
-    epi.strideC = (long)(m * np);
-    rc = gemm_tf32(st, m, n, k, 1, A, B, epi, ctx->flags, ctx->precision);
+    if (simt) {
+      rc = gemm_simt(st, da, db, dc, m, k, n, 1, false, false, false);
+    } else {
+      GemmOperand A{da, (long)kp, (long)(m * kp), false};
+      GemmOperand B{db, (long)np, (long)(k * np), true};
+      GemmEpi epi;
+      epi.kind = EPI_STORE;
+      epi.C = dc;
+      epi.ldc = (long)np;
+      epi.strideC = (long)(m * np);
+      rc = gemm_tf32(st, m, n, k, 1, A, B, epi, ctx->flags, ctx->precision);
+    }
     if (rc) return rc;
   }
   TURT_CHECK_CUDA(cudaMemcpy2DAsync(out, (size_t)n * 4, dc, np * 4, (size_t)n * 4, m, cudaMemcpyDeviceToHost, st));

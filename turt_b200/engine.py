@@ -11,7 +11,7 @@ against them ports line for line:
 * ``GpuGPT`` -- src/models/gpu-gpt.ts:54-202: both architectures built from ``GpuTensor`` ops
   (``fused=False``, the reference's op-by-op graph) or backed by the library's fused train
   step (``fused=True``: one call for forward + backward, same parameters() order and values).
-* ``GpuCompute`` / ``CudaBackend`` -- src/infer/webgpu/gpu.ts:396-491 and
+* ``GpuCompute`` / ``CudaBackend`` -- src/infer/webgpu/gpu.ts:59-141 and
   src/infer/backend.ts:11-16: host-array matmul.
 
 Errors raise ``TurtError`` (the reference throws ``Error``); shape mismatches raise
@@ -757,7 +757,7 @@ class AdamW:
 
 
 class GpuCompute:
-    """Host-array matmul (src/infer/webgpu/gpu.ts:396-491).
+    """Host-array matmul (src/infer/webgpu/gpu.ts:59-141).
 
     Defaults to FP32 CUDA-core arithmetic (precision 0), what the reference's WGSL matmul
     computes, so results meet scripts/gpu-bench.ts's check (5e-3 with a 1e-4 floor); pass
