@@ -522,6 +522,92 @@ def run_backward_ops(args, rank: int) -> None:
     print(json.dumps(out), flush=True)
 
 
+def step_gemm_shapes(w):
+    """The tensor-core GEMMs of one train step of workload `w`, as turt_matmul_into calls:
+    (name, M, N, K, transA, transB, accumulate, launches per step).  A is [M,K] (transA: stored
+    [K,M]), B is [K,N] (transB: stored [N,K]); weight gradients accumulate."""
+    N, E, h, V, L = w["micro"] * w["T"], w["E"], w["hidden"], w["V"], w["L"]
+    W1 = 2 * h if w["arch"] == "modern" else h
+    return [
+        ("fwd qkv", N, 3 * E, E, 0, 0, 0, L), ("fwd proj", N, E, E, 0, 0, 0, L), ("fwd mlp up", N, W1, E, 0, 0, 0, L),
+        ("fwd mlp down", N, E, h, 0, 0, 0, L), ("fwd head", N, V, E, 0, 1, 0, 1),
+        ("dX head", N, E, V, 0, 0, 0, 1), ("dX mlp down (dact)", N, h, E, 0, 1, 0, L),
+        ("dX mlp up", N, E, W1, 0, 1, 0, L), ("dX proj", N, E, E, 0, 1, 0, L), ("dX qkv", N, E, 3 * E, 0, 1, 0, L),
+        ("dW head", V, E, N, 1, 0, 1, 1), ("dW mlp down", h, E, N, 1, 0, 1, L), ("dW mlp up", E, W1, N, 1, 0, 1, L),
+        ("dW proj", E, E, N, 1, 0, 1, L), ("dW qkv", E, 3 * E, N, 1, 0, 1, L),
+    ]
+
+
+def run_gemm_table(args, rank: int) -> None:
+    """Every tensor-core GEMM shape of the train step timed on its own (median of back-to-back
+    launches on L2-warm operands, as in the step where each GEMM reads what the previous kernel
+    wrote), with its algorithmic TFLOP/s and the fraction of the 3xTF32 ceiling (TF32 peak / 3)."""
+    if rank != 0:
+        return
+    import torch
+
+    from turt_b200._lib import check, lib
+    from turt_b200.runtime import Context
+    w = WORKLOADS[args.table_workload]
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx = Context(0)
+    ctx.set_stream(stream.cuda_stream)
+    ctx.set_precision(args.precision)
+    peaks = measured_peaks()
+    tf32 = peaks["bf16_tflops"] / 2.0
+    issue = 3 if args.precision == 3 else 1
+    g = torch.Generator(device="cuda").manual_seed(7)
+    rows, total_ms, total_flop = [], 0.0, 0.0
+    launches0 = Context.launch_count()
+    with ClockSampler(0) as clk:
+        for (name, M, N, K, ta, tb, acc, per_step) in step_gemm_shapes(w):
+            a = torch.randn(M * K, generator=g, device="cuda")
+            b = torch.randn(K * N, generator=g, device="cuda")
+            c = torch.zeros(M * N, device="cuda")
+
+            def fn():
+                check(lib().turt_matmul_into(ctx.handle, a.data_ptr(), b.data_ptr(), c.data_ptr(), M, K, N, 1, ta, tb,
+                                             acc))
+
+            for _ in range(args.warmup):
+                fn()
+            times = []
+            for _ in range(args.steps):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                fn()
+                e1.record(stream)
+                e1.synchronize()
+                times.append(e0.elapsed_time(e1))
+            ms = statistics.median(times)
+            tflops = 2.0 * M * N * K / (ms / 1000.0) / 1e12
+            rows.append({"gemm": name, "M": M, "N": N, "K": K, "A": "MN-major" if ta else "K-major",
+                         "B": "K-major" if tb else "MN-major", "us": ms * 1000.0, "tflops": tflops,
+                         "frac_tf32": tflops / tf32, "frac_of_precision_peak": tflops * issue / tf32,
+                         "per_step": per_step})
+            total_ms += ms * per_step
+            total_flop += 2.0 * M * N * K * per_step
+            del a, b, c
+    launches = Context.launch_count() - launches0
+    ctx.close()
+    agg = total_flop / (total_ms / 1000.0) / 1e12
+    out = {"metric": "train-step GEMM throughput, every shape timed alone (algorithmic 2MNK FLOPs)", "value": agg,
+           "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "tf32x3" if issue == 3 else "tf32", "data": "synthetic",
+           "config": {"workload": "gemm-table", "model": args.table_workload,
+                      "l2": "not flushed: back-to-back launches on the same operands, median per shape"},
+           "shapes": rows,
+           "roofline": {"bound": "tensor", "kernel": "all step GEMM shapes", "achieved": agg, "peak": tf32,
+                        "unit": "TFLOP/s", "frac": agg / tf32, "frac_of_precision_peak": agg * issue / tf32,
+                        "mma_issue_factor": issue, "traffic": None, "peak_source": f"{peaks['source']} bf16 dense / 2"},
+           "e2e": {"value": agg, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0,
+                   "note": "device-resident operands: no host copies belong to this workload"},
+           "gpu_launches": launches, "clocks": clk.summary()}
+    print(json.dumps(out), flush=True)
+
+
 def run_gemm(args, rank: int) -> None:
     """One tensor-core GEMM C[M,N] = A[M,K] B[N,K]^T (both K-major, the head-projection
     layout) repeated: algorithmic 2MNK FLOPs over the median CUDA-event launch time."""
@@ -699,7 +785,10 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="turt", choices=["turt", "reference"])
-    ap.add_argument("--workload", default="gpt-6L-384d", choices=sorted(WORKLOADS) + ["backward-ops", "gemm", "decode"])
+    ap.add_argument("--workload", default="gpt-6L-384d",
+                    choices=sorted(WORKLOADS) + ["backward-ops", "gemm", "gemm-table", "decode"])
+    ap.add_argument("--table-workload", default="gpt-6L-384d", choices=sorted(WORKLOADS),
+                    help="model whose train-step GEMM shapes --workload gemm-table times")
     ap.add_argument("--gemm", default="8192,8192,384", help="M,N,K of the gemm workload")
     ap.add_argument("--precision", type=int, default=3, choices=[1, 3])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -709,13 +798,13 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.workload == "gemm":
+    if args.workload in ("gemm", "gemm-table"):
         if args.impl == "reference":
             if rank == 0:
-                print(json.dumps({"impl": "reference", "unavailable": "the gemm workload is a kernel microbenchmark "
+                print(json.dumps({"impl": "reference", "unavailable": "the gemm workloads are kernel microbenchmarks "
                                   "with no reference counterpart"}), flush=True)
             return
-        run_gemm(args, rank)
+        (run_gemm if args.workload == "gemm" else run_gemm_table)(args, rank)
         return
     if args.workload == "decode":
         if args.impl == "reference":

@@ -202,14 +202,20 @@ int turt_model_create(turt_ctx* ctx, const turt_config* cfg, turt_model** out);
 int turt_model_destroy(turt_model* model);
 /* Attention implementation of the model's fused train step.  No reference counterpart (the
  * reference always materialises scores per head):
- * TURT_ATTN_AUTO (default) = TURT_ATTN_TENSOR when the per-layer [B*H][T][T] probabilities
- * of all layers fit a 16 GiB budget and the head dim is a multiple of 16, else TURT_ATTN_FLASH;
- * TURT_ATTN_TENSOR = score / probability GEMMs on the tensor cores, probabilities kept for
- * the backward pass; TURT_ATTN_FLASH = fused online-softmax kernels on the CUDA cores, no
- * [T][T] buffers (head dim 16, 32 or 64). */
+ * TURT_ATTN_AUTO (default) = TURT_ATTN_TENSOR_ONLINE for sequences longer than 256 tokens at
+ * head dims 32 / 64 (3xTF32), else TURT_ATTN_TENSOR when the per-layer [B*H][T][T]
+ * probabilities of all layers fit a 16 GiB budget and the head dim is a multiple of 16, else
+ * TURT_ATTN_FLASH;
+ * TURT_ATTN_TENSOR = probabilities computed on the tensor cores (one fused kernel per pass for
+ * T <= 256 at head dims 32 / 64, score / probability GEMMs otherwise) and kept for the backward
+ * pass; TURT_ATTN_FLASH = fused online-softmax kernels on the CUDA cores, no [T][T] buffers
+ * (head dim 16, 32 or 64); TURT_ATTN_TENSOR_ONLINE = online-softmax kernels on the tensor cores
+ * at any T (head dim 32 or 64, 3xTF32 GEMMs), no [T][T] buffers, the probabilities recomputed in
+ * the backward pass from the row log-sum-exp. */
 #define TURT_ATTN_AUTO 0
 #define TURT_ATTN_TENSOR 1
 #define TURT_ATTN_FLASH 2
+#define TURT_ATTN_TENSOR_ONLINE 3
 int turt_model_set_attention(turt_model* model, int mode);
 /* parameters() order, gpu-gpt.ts:118-132: count, total scalars, per-tensor name and shape. */
 int turt_param_count(turt_model* model, int* count);
@@ -281,6 +287,39 @@ int turt_dp_defer(turt_model* model, int defer);
  * asynchronous NCCL error and returns TURT_ERR_NCCL. */
 int turt_dp_wait(turt_model* model, int timeout_ms);
 int turt_dp_destroy(turt_model* model);
+
+/* ------------------------------------------------------ one process, several GPUs
+ * The reference's data-parallel worker pool inside one process (scripts/train-gpt.ts:66-101:
+ * one replica per worker; :105-123 contiguous shards; :200-219 row-weighted gradient mean), on
+ * GPUs: a group holds one context + model replica per device, each driven by its own host
+ * thread, joined by one NCCL communicator (the per-layer all-reduce of turt_dp_init, issued
+ * during the backward pass).  Calls come from one host thread.
+ * turt_group_forward_backward splits the b sequences contiguously as the reference's shard()
+ * does (floor(b / ndev) each, one more for the first b mod ndev devices; b >= ndev), scales each
+ * shard's mean-loss gradient by loss_scale * rows_i / b and sums the replicas, so every replica
+ * then holds loss_scale times the full-batch mean gradient; loss_out (may be NULL, else the call
+ * synchronizes) receives the row-weighted mean loss.  Gradients accumulate across calls like
+ * turt_forward_backward's, but the all-reduce sums whole gradient buffers: for micro-batch
+ * accumulation set turt_group_defer(g, 1) for every micro-batch but the last, and start each
+ * step with turt_group_zero_grad.  turt_group_adamw_step runs the fused clip + AdamW on every
+ * replica (identical gradients, so the replicas stay identical).  Parameter uploads go to every
+ * replica; downloads come from replica 0. */
+typedef struct turt_group turt_group;
+int turt_group_create(int ndev, const int* devs, const turt_config* cfg, turt_group** out);
+int turt_group_destroy(turt_group* g);
+int turt_group_size(turt_group* g, int* ndev);
+int turt_group_model(turt_group* g, int replica, turt_model** out);
+int turt_group_param_upload(turt_group* g, int index, const float* host, size_t n);
+int turt_group_param_download(turt_group* g, int index, float* host, size_t n);
+int turt_group_grad_download(turt_group* g, int index, float* host, size_t n);
+int turt_group_model_init(turt_group* g, uint32_t seed);
+int turt_group_zero_grad(turt_group* g);
+int turt_group_defer(turt_group* g, int defer);
+int turt_group_forward_backward(turt_group* g, const uint32_t* ids, const uint32_t* targets, int b, int t,
+                                float loss_scale, float* loss_out);
+int turt_group_adamw_step(turt_group* g, float lr, float b1, float b2, float eps, float wd, float bc1, float bc2,
+                          float clip);
+int turt_group_synchronize(turt_group* g);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

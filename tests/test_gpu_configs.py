@@ -96,3 +96,37 @@ def test_modern_head_dim64_T1024(ctx, orc, attn, t):
     le, ge, name, losses = _parity(ctx, orc, 512, 1024, 2, 2, 128, "modern", 2, t, attn=attn)
     assert le <= LOSS_TOL, losses
     assert ge <= GRAD_TOL, (ge, name)
+
+
+@pytest.mark.parametrize("arch", ["modern", "gpt2", "modern-T1024"])
+def test_gradients_bit_identical_across_runs(ctx, orc, arch):
+    """Two identical train steps give bit-identical losses and gradients: the embedding
+    backward adds each vocab row's positions in a fixed order (the reference's GATHER_BWD is a
+    sequential scan, src/infer/webgpu/autograd.ts:428-438) and split-K GEMMs add their partial
+    sums in split order, so nothing depends on thread scheduling.  Full headline shape (the
+    weight-gradient GEMMs split K there); gpt2 adds the learned-position gradient; T = 1024 runs
+    the long-sequence attention kernels (dQ and dK / dV each summed by one CTA, no atomics)."""
+    from turt_b200.runtime import Model, make_config
+    if arch == "modern":
+        V, T, L, H, E, hidden, b, t = 8192, 256, 6, 6, 384, 1024, 32, 256
+    elif arch == "gpt2":
+        V, T, L, H, E, hidden, b, t = 8192, 256, 2, 6, 384, 0, 32, 256
+    else:  # long sequences: the online-softmax attention kernels
+        arch = "modern"
+        V, T, L, H, E, hidden, b, t = 2048, 1024, 2, 4, 256, 0, 4, 1024
+    cfg = orc.cfg(V, T, L, H, E, arch, hidden)
+    params = orc.init(cfg, 7)
+    ids, tgt = _tokens(orc, b * t, V, seed=5)
+    model = Model(ctx, make_config(V, T, L, H, E, arch, hidden))
+    try:
+        model.load_flat(params)
+        runs = []
+        for _ in range(3):
+            model.zero_grad()
+            loss = model.forward_backward(ids, tgt, b, t)
+            runs.append((loss, model.grads_flat()))
+    finally:
+        model.close()
+    for loss, g in runs[1:]:
+        assert loss == runs[0][0]
+        np.testing.assert_array_equal(g, runs[0][1])

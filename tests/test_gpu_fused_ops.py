@@ -27,6 +27,14 @@ def _ok(got, ref):
     return max_rel_err(got, ref) < TOL and norm < NORM_TOL
 
 
+def _ok_sum(got, ref, abs_terms):
+    """For a column sum over many rows computed in fp32: each entry within 1e-6 of the sum of
+    its terms' magnitudes (about 16 fp32 ulps of that sum; a plain blocked fp32 sum of 8192
+    rows already leaves maxRelErr ~1.1e-3 on entries that cancel to ~0.1)."""
+    got, ref = np.asarray(got, np.float64), np.asarray(ref, np.float64)
+    return bool(np.all(np.abs(got - ref) <= 1e-6 * np.asarray(abs_terms, np.float64) + 1e-7))
+
+
 @pytest.fixture(scope="module")
 def ctx():
     from turt_b200.runtime import Context
@@ -68,7 +76,8 @@ def test_rms_bwd(ctx, orc, rows, E, with_res):
     got_dx = ctx.download(dx, rows * E).reshape(rows, E)
     got_dg = ctx.download(bufs[4], E)
     assert _ok(got_dx, ref_dx)
-    assert _ok(got_dg, ref_dg + dg0)
+    abs_terms = np.abs(dy.astype(np.float64) * x * rstd[:, None]).sum(axis=0) + np.abs(dg0)
+    assert _ok_sum(got_dg, ref_dg + dg0, abs_terms)
 
 
 @pytest.mark.parametrize("n", [8192 * 1024, 8192 * 1024 // 64, 1003])

@@ -215,3 +215,15 @@ def test_bounded_wait_times_out_and_context_survives(ctx, orc):
     loss, ref, le, ge, name = _run_parity(ctx, orc, 48, 16, 2, 2, 32, "modern", 2, 8)
     assert le <= LOSS_TOL, (loss, ref)
     assert ge <= GRAD_TOL, (ge, name)
+
+
+@pytest.mark.parametrize("arch", ["gpt2", "modern"])
+@pytest.mark.parametrize("E,H", [(64, 2), (128, 2)])
+@pytest.mark.parametrize("t", [7, 64, 130, 256, 301])
+def test_online_attention_any_length(ctx, orc, arch, E, H, t):
+    """The tensor-core online-softmax attention (forward, dQ and dK / dV kernels, no [T][T]
+    buffers) forced at every length, head dims 32 and 64: one block of keys, a ragged last
+    block, several 128-row query tiles and key tiles, and the lengths the default takes it at."""
+    loss, ref, le, ge, name = _run_parity(ctx, orc, 256, 320, 2, H, E, arch, 2, t, attn=3)
+    assert le <= LOSS_TOL, (loss, ref)
+    assert ge <= GRAD_TOL, (ge, name)

@@ -17,7 +17,7 @@ ROOT = os.path.dirname(HERE)
 OBJ = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libturt_cuda.so")
 
-SOURCES = ["gemm.cu", "ops.cu", "attention.cu", "attention_tc.cu", "attention_fused.cu", "model_kernels.cu", "capi.cu", "model.cu", "dp.cu", "noalloc.cu", "fused_ops.cu", "decode.cu", "diag.cu"]
+SOURCES = ["gemm.cu", "ops.cu", "attention.cu", "attention_tc.cu", "attention_fused.cu", "attention_flash.cu", "model_kernels.cu", "capi.cu", "model.cu", "dp.cu", "noalloc.cu", "fused_ops.cu", "decode.cu", "diag.cu", "group.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

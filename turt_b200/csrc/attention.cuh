@@ -22,9 +22,12 @@ struct AttnTensors {
   float* P = nullptr;   // [B*H][T][pitch] scores, then probabilities (kept for backward)
   float* qr = nullptr;  // [B*H][T][hd] rotated q (RoPE models; null otherwise)
   float* kr = nullptr;  // [B*H][T][hd] rotated k
+  float* lse = nullptr;  // [B*H][T] row log-sum-exp (online-softmax kernels, instead of P)
+  bool online = false;   // run the online-softmax kernels (attention_flash.cu) instead of keeping P
 };
 struct AttnScratch {
   float* dS = nullptr;  // [B*H][T][pitch]
+  float* D = nullptr;   // [B*H][T] rowsum(dO * O) (long-sequence kernels)
 };
 inline long attn_pitch(int T) { return ((long)T + 3) & ~3L; }
 bool attention_tc_supported(int hd);
@@ -49,7 +52,21 @@ int attention_fused_dsoftmax(cudaStream_t st, const GemmOperand& dout, const Gem
 int attention_fused_dkv(cudaStream_t st, const float* P, const float* dS, long pitch, const GemmOperand& dout,
                         const GemmOperand& q, float* dqkv, long ld, const float2* rope, int B, int T, int H, int hd,
                         int* flags);
-int attention_tc_bwd(cudaStream_t st, const float* qkv, const float2* rope_cs, const float* dout,
+// Online-softmax kernels (head dims 32 / 64, 3xTF32, any T; the default above 256 tokens) that
+// keep no [T][T] buffer (attention_flash.cu).  The forward writes the merged output and the row
+// log-sum-exp; the backward recomputes the probabilities, writes D = rowsum(dO * O) and dQ, dK,
+// dV into dqkv (rotated back with `rope` when it is not null).
+bool attention_flash_supported(int T, int hd);
+// The default choice: the online-softmax kernels for sequences the single-pass fused kernels
+// cannot hold (T > 256), in 3xTF32, at head dims 32 / 64.
+bool attention_tc_prefers_online(int T, int hd, int precision);
+int attention_flash_fwd(cudaStream_t st, const GemmOperand& q, const GemmOperand& k, const GemmOperand& v, float* out,
+                        long ld_out, float* lse, int B, int T, int H, int hd, float scale, int* flags);
+int attention_flash_bwd(cudaStream_t st, const GemmOperand& q, const GemmOperand& k, const GemmOperand& v,
+                        const GemmOperand& dout, const GemmOperand& o, const float* lse, float* D, float* dqkv,
+                        long ld, const float2* rope, int B, int T, int H, int hd, float scale, int* flags);
+// `out` is the forward's merged output (read by the long-sequence backward for D).
+int attention_tc_bwd(cudaStream_t st, const float* qkv, const float2* rope_cs, const float* out, const float* dout,
                      const AttnTensors& at, const AttnScratch& sc, float* dqkv, int B, int T, int H, int hd, int rope,
                      int* flags, int precision);
 }  // namespace turt

@@ -14,7 +14,9 @@
 //             dK = dS^T q  (inverse RoPE in the dQ / dK epilogues)
 // Masked probabilities are exact zeros, so the causal tile / K-range skips change no result.
 // For T <= 256 with head dims 32 / 64 in 3xTF32 the same steps run as three fused kernels
-// (attention_fused.cu: forward; dP + dS + dQ; dV + dK); this chain covers the other shapes.
+// (attention_fused.cu: forward; dP + dS + dQ; dV + dK), for longer sequences with those head
+// dims as online-softmax kernels without [T][T] buffers (attention_flash.cu); this chain covers
+// the other shapes.
 #include "attention.cuh"
 #include "gemm.cuh"
 
@@ -321,10 +323,18 @@ GemmEpi merged_epi(float* base, long ld, int T, int hd, int causal) {
 
 bool attention_tc_supported(int hd) { return hd >= 16 && hd <= 256 && hd % 16 == 0; }
 
+bool attention_tc_prefers_online(int T, int hd, int precision) {
+  return precision == GEMM_TF32X3 && !attention_fused_supported(T, hd) && attention_flash_supported(T, hd);
+}
+
 int attention_tc_fwd(cudaStream_t st, const float* qkv, const float2* rope_cs, float* out, const AttnTensors& at, int B,
                      int T, int H, int hd, int rope, int rotated, int* flags, int precision) {
   TURT_REQUIRE(attention_tc_supported(hd), "attention: head dim must be a multiple of 16 in [16, 256]");
-  TURT_REQUIRE(at.P && (!rope || (at.qr && at.kr)), "attention: buffers missing");
+  const bool flash = at.online;
+  if (flash)
+    TURT_REQUIRE(precision == GEMM_TF32X3 && attention_flash_supported(T, hd),
+                 "online-softmax attention: needs 3xTF32 and a head dim of 32 or 64");
+  TURT_REQUIRE((flash ? at.lse != nullptr : at.P != nullptr) && (!rope || (at.qr && at.kr)), "attention: buffers missing");
   const int E = H * hd, BH = B * H;
   const float scale = 1.0f / sqrtf((float)hd);
   if (rope && !rotated) {
@@ -332,6 +342,7 @@ int attention_tc_fwd(cudaStream_t st, const float* qkv, const float2* rope_cs, f
     TURT_LAUNCH_CHECK();
   }
   const Views w = views(qkv, nullptr, at, at.P, T, H, hd, rope != 0);
+  if (flash) return attention_flash_fwd(st, w.q, w.k, w.v, out, E, at.lse, B, T, H, hd, scale, flags);
   if (precision == GEMM_TF32X3 && attention_fused_supported(T, hd))
     return attention_fused_fwd(st, w.q, w.k, w.v, at.P, w.pitch, out, E, B, T, H, hd, scale, flags);
   // S = q k^T  (k [T][hd] is the K-major B operand)
@@ -344,13 +355,26 @@ int attention_tc_fwd(cudaStream_t st, const float* qkv, const float2* rope_cs, f
   return OK;
 }
 
-int attention_tc_bwd(cudaStream_t st, const float* qkv, const float2* rope_cs, const float* dout,
+int attention_tc_bwd(cudaStream_t st, const float* qkv, const float2* rope_cs, const float* out, const float* dout,
                      const AttnTensors& at, const AttnScratch& sc, float* dqkv, int B, int T, int H, int hd, int rope,
                      int* flags, int precision) {
   TURT_REQUIRE(attention_tc_supported(hd), "attention: head dim must be a multiple of 16 in [16, 256]");
-  TURT_REQUIRE(at.P && sc.dS && (!rope || (at.qr && at.kr)), "attention: buffers missing");
   const int E = H * hd, BH = B * H;
   const float scale = 1.0f / sqrtf((float)hd);
+  if (at.online) {
+    TURT_REQUIRE(precision == GEMM_TF32X3 && attention_flash_supported(T, hd),
+                 "online-softmax attention: needs 3xTF32 and a head dim of 32 or 64");
+    TURT_REQUIRE(at.lse && sc.D && out && (!rope || (at.qr && at.kr)), "attention: buffers missing");
+    const Views w = views(qkv, dout, at, nullptr, T, H, hd, rope != 0);
+    GemmOperand o;  // the forward's merged output [N][E], head h at columns h * hd
+    o.ptr = out;
+    o.ld = E;
+    o.stride = hd;
+    o.stride_hi = (long)T * E;
+    return attention_flash_bwd(st, w.q, w.k, w.v, w.dout, o, at.lse, sc.D, dqkv, 3L * E, rope ? rope_cs : nullptr, B,
+                               T, H, hd, scale, flags);
+  }
+  TURT_REQUIRE(at.P && sc.dS && (!rope || (at.qr && at.kr)), "attention: buffers missing");
   const Views w = views(qkv, dout, at, at.P, T, H, hd, rope != 0);
   const bool fused = precision == GEMM_TF32X3 && attention_fused_supported(T, hd);
   if (fused) {

@@ -102,6 +102,7 @@ int turt_ctx_destroy(turt_ctx* ctx) {
   for (void* p : ctx->live_set) cudaFree(p);
   cudaFree(ctx->flags);
   if (ctx->scratch) cudaFree(ctx->scratch);
+  gemm_release_stream(ctx->stream);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
   return OK;
@@ -110,6 +111,7 @@ int turt_ctx_destroy(turt_ctx* ctx) {
 int turt_ctx_set_stream(turt_ctx* ctx, void* stream) {
   CTX_GUARD(ctx);
   TURT_CHECK_CUDA(cudaStreamSynchronize(ctx->stream));
+  gemm_release_stream(ctx->stream);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   ctx->stream = reinterpret_cast<cudaStream_t>(stream);
   ctx->own_stream = false;

@@ -13,6 +13,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <map>
 #include <mutex>
 
 #include "gemm.cuh"
@@ -107,17 +108,6 @@ __device__ __forceinline__ void epi_chunk(const GemmEpi& epi, const EpiVec& vec,
       for (int j = 0; j < 32; j++) v[j] += o[j];
       st32(dst, v, n, vec.C);
     } break;
-    case EPI_RED:
-      if (vec.C && n >= 32) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 4)
-          atomicAdd(reinterpret_cast<float4*>(dst + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; j++)
-          if (j < n) atomicAdd(dst + j, v[j]);
-      }
-      break;
     case EPI_ADD_RES: {
       float o[32];
       ld32(epi.R + cboff + row * epi.ldr + col0, o, n, vec.R);
@@ -223,16 +213,6 @@ __device__ __forceinline__ void epi_quad(const GemmEpi& epi, const EpiVec& vec, 
       break;
     case EPI_ACCUM:
       st4(dst, add4(x, ld4(dst, nv, vec.C)), nv, vec.C);
-      break;
-    case EPI_RED:
-      if (vec.C && nv == 4) {
-        atomicAdd(reinterpret_cast<float4*>(dst), x);
-      } else {
-        atomicAdd(dst, x.x);
-        if (nv > 1) atomicAdd(dst + 1, x.y);
-        if (nv > 2) atomicAdd(dst + 2, x.z);
-        if (nv > 3) atomicAdd(dst + 3, x.w);
-      }
       break;
     case EPI_ADD_RES:
       x = add4(x, ld4(epi.R + cboff + row * epi.ldr + col, nv, vec.R));
@@ -353,6 +333,80 @@ __device__ __forceinline__ void epi_tile(const GemmEpi& epi, const EpiVec& vec, 
                 [&](float4 x, long r, int col, int nv) { epi_quad(epi, vec, x, Cb, r, col, nv, cboff); });
       else if (row < M)
         epi_chunk(epi, vec, v, Cb, row, col0, min(32, N - col0), cboff);
+    }
+  }
+}
+
+// ------------------------------------------------------------ split-K
+// A split's partial of one 32-row x BN piece (rows rowbase.., columns n0..) goes to its own
+// dense plane of the workspace, [batch][split][M][N], through L2 (st.global.cg).
+template <int BN>
+__device__ __forceinline__ void split_store(const GemmEpi& epi, int lane, uint32_t tbase, long rowbase, int M, int N,
+                                            int n0, int b, int split, int ksplits) {
+  const long row = rowbase + lane;
+  const bool vw = (N & 3) == 0;
+  float* W = epi.split_ws + ((size_t)b * ksplits + split) * ((size_t)M * N) + (size_t)(row < M ? row : 0) * N;
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; c++) {
+    const int col0 = n0 + c * 32;
+    if (col0 >= N) break;  // warp-uniform
+    float v[32];
+    tmem_ld32(tbase + c * 32, v);
+    if (row >= M) continue;
+    const int n = min(32, N - col0);
+    if (vw && n == 32) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        __stcg(reinterpret_cast<float4*>(W + col0 + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+    } else {
+      for (int j = 0; j < n; j++) __stcg(W + col0 + j, v[j]);
+    }
+  }
+}
+
+// Fixed-order reduction of the split-K partial planes, launched right after the GEMM on the
+// same stream: C (=|+=) W[0] + W[1] + ... + W[ks-1], element by element, so the sum does not
+// depend on which split finished first.  Planes are [batch][ks][M][N]; C of batch b is
+// C + (b % bdiv) * strideC + (b / bdiv) * strideC_hi with row pitch ldc.
+__global__ void __launch_bounds__(256) k_splitk_reduce(const float* __restrict__ W, int ks, int M, int N, int batch,
+                                                       float* __restrict__ C, long ldc, long strideC, long strideC_hi,
+                                                       int bdiv, int accumulate, int vec) {
+  pdl_trigger();
+  pdl_wait();
+  const size_t plane = (size_t)M * N;
+  if (vec) {  // N % 4 == 0 and C rows 16-byte aligned
+    const int n4 = N / 4;
+    const size_t total = (size_t)batch * M * n4;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+      const int c4 = (int)(e % n4);
+      const size_t r = e / n4;
+      const int row = (int)(r % M), b = (int)(r / M);
+      const float4* w = reinterpret_cast<const float4*>(W + (size_t)b * ks * plane + (size_t)row * N) + c4;
+      float4 acc = __ldcg(w);
+      for (int sp = 1; sp < ks; sp++) {
+        const float4 t = __ldcg(w + sp * (plane / 4));
+        acc.x += t.x, acc.y += t.y, acc.z += t.z, acc.w += t.w;
+      }
+      float4* dst = reinterpret_cast<float4*>(C + (long)(b % bdiv) * strideC + (long)(b / bdiv) * strideC_hi +
+                                              (long)row * ldc) + c4;
+      if (accumulate) {
+        const float4 o = *dst;
+        acc.x += o.x, acc.y += o.y, acc.z += o.z, acc.w += o.w;
+      }
+      *dst = acc;
+    }
+  } else {
+    const size_t total = (size_t)batch * plane;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+      const int col = (int)(e % N);
+      const size_t r = e / N;
+      const int row = (int)(r % M), b = (int)(r / M);
+      const float* w = W + (size_t)b * ks * plane + (size_t)row * N + col;
+      float acc = __ldcg(w);
+      for (int sp = 1; sp < ks; sp++) acc += __ldcg(w + sp * plane);
+      float* dst = C + (long)(b % bdiv) * strideC + (long)(b / bdiv) * strideC_hi + (long)row * ldc + col;
+      if (accumulate) acc += *dst;
+      *dst = acc;
     }
   }
 }
@@ -630,7 +684,12 @@ __global__ void __launch_bounds__(GemmShape<BN, BK, X3, MINB>::THREADS, MINB)
       tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       const long cboff = (long)(b % bdiv) * epi.strideC + (long)(b / bdiv) * epi.strideC_hi;
-      epi_tile<BN, false>(epi, vec, nullptr, lane, tbase, m0 + q * 32, M, N, n0, epi.C + cboff, cboff);
+      const long rowbase = m0 + q * 32;
+      const bool split_piece = ksplits > 1 && rowbase < M;  // warp-uniform
+      if (split_piece)
+        split_store<BN>(epi, lane, tbase, rowbase, M, N, n0, b, (u / (mt * nt)) % ksplits, ksplits);
+      else if (ksplits == 1)
+        epi_tile<BN, false>(epi, vec, nullptr, lane, tbase, rowbase, M, N, n0, epi.C + cboff, cboff);
       // hand the accumulator back to the MMA issuer
       tc_fence_before();
       __syncwarp();
@@ -1018,8 +1077,12 @@ __global__ void __launch_bounds__(352, 1)
       tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       const long cboff = (long)(b % bdiv) * epi.strideC + (long)(b / bdiv) * epi.strideC_hi;
-      epi_tile<BN, (S::EPI_BYTES > 0)>(epi, vec, tile, lane, tbase, m0 + (int)rank * BM + q * 32, M, N, n0,
-                                       epi.C + cboff, cboff);
+      const long rowbase = m0 + (int)rank * BM + q * 32;
+      const bool split_piece = ksplits > 1 && rowbase < M;  // warp-uniform
+      if (split_piece)
+        split_store<BN>(epi, lane, tbase, rowbase, M, N, n0, b, (u / (mt * nt)) % ksplits, ksplits);
+      else if (ksplits == 1)
+        epi_tile<BN, (S::EPI_BYTES > 0)>(epi, vec, tile, lane, tbase, rowbase, M, N, n0, epi.C + cboff, cboff);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -1319,7 +1382,8 @@ TilePlan plan_tiles(int M, int N, int K, int batch, bool x3, int max_ks, int for
         const long rounds = (units + slots - 1) / slots;
         const double steps = (double)((k32 + ks - 1) / ks);
         double cost = rounds * steps * kstep_cycles(bn, x3, pair) + 2000.0 + 16.0 * bn;
-        if (ks > 1) cost += (double)M * N * batch * ks / (sms * 8.0);  // float4 atomics
+        // split partials: stored by the epilogues, summed by one more launch in a fixed order
+        if (ks > 1) cost += (double)M * N * batch * (ks + 1) / (sms * 8.0) + 3000.0;
         if (best_cost < 0 || cost < best_cost) {
           best_cost = cost;
           best.bn = bn;
@@ -1335,7 +1399,51 @@ TilePlan plan_tiles(int M, int N, int K, int batch, bool x3, int max_ks, int for
 std::atomic<int> g_tile_override{0};
 std::atomic<int> g_pair_override{-1};
 
+// Split-K workspaces, one per (device, stream): GEMMs on one stream run one after another, so
+// they can share partial planes; GEMMs on different streams may overlap.
+struct SplitWorkspace {
+  float* ws = nullptr;
+  size_t floats = 0;
+};
+std::mutex g_split_mu;
+std::map<std::pair<int, cudaStream_t>, SplitWorkspace> g_split_ws;
+constexpr size_t kSplitWsMaxFloats = (size_t)64 << 20;  // 256 MB of partial planes at most
+
+// Grows the stream's workspace to `floats` partial floats.  While the stream is being captured
+// nothing can be allocated: ERR_UNSUPPORTED, and the caller does not split.
+int split_workspace(cudaStream_t st, size_t floats, float** ws) {
+  int dev = 0;
+  TURT_CHECK_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(g_split_mu);
+  SplitWorkspace& w = g_split_ws[{dev, st}];
+  if (w.floats < floats) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    TURT_CHECK_CUDA(cudaStreamIsCapturing(st, &cs));
+    if (cs != cudaStreamCaptureStatusNone) return ERR_UNSUPPORTED;
+    TURT_CHECK_CUDA(cudaStreamSynchronize(st));  // the old buffer is no longer in use
+    if (w.ws) cudaFree(w.ws);
+    w.ws = nullptr;
+    w.floats = 0;
+    const size_t nf = std::max(floats, (size_t)1 << 20);
+    TURT_CHECK_CUDA(cudaMalloc(&w.ws, nf * 4));
+    w.floats = nf;
+  }
+  *ws = w.ws;
+  return OK;
+}
+
 }  // namespace
+
+void gemm_release_stream(cudaStream_t st) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return;
+  std::lock_guard<std::mutex> lock(g_split_mu);
+  auto it = g_split_ws.find({dev, st});
+  if (it == g_split_ws.end()) return;
+  cudaStreamSynchronize(st);
+  if (it->second.ws) cudaFree(it->second.ws);
+  g_split_ws.erase(it);
+}
 
 void gemm_set_tile_override(int bn, int pair) {
   g_tile_override.store(bn);
@@ -1401,18 +1509,26 @@ int gemm_tf32(cudaStream_t stream, int M, int N, int K, int batch, const GemmOpe
   }
   const int BN = plan.bn;
   const int kt_total = ceil_div(K, plan.pair ? PairShape<64>::BK : BK);
-  const int ks = force_splits > 0 ? force_splits : plan.ks;
+  int ks = force_splits > 0 ? force_splits : plan.ks;
+  const size_t plane = (size_t)batch * M * N;
+  if (ks > 1 && plane * ks > kSplitWsMaxFloats) ks = (int)std::max<size_t>(1, kSplitWsMaxFloats / plane);
   la.kt_per = ceil_div(kt_total, ks);
   la.ks = ceil_div(kt_total, la.kt_per);
+  float* split_ws = nullptr;
   if (la.ks > 1) {
     GemmEpi& epi = la.epi;
-    TURT_REQUIRE(can_split, "gemm: split-K needs an accumulating epilogue");
-    if (epi.kind == EPI_STORE) {
-      for (int b = 0; b < batch; b++)
-        TURT_CHECK_CUDA(cudaMemset2DAsync(epi.C + (long)(b % bdiv) * epi.strideC + (long)(b / bdiv) * epi.strideC_hi,
-                                          epi.ldc * 4, 0, (size_t)N * 4, (size_t)M, stream));
+    TURT_REQUIRE(can_split, "gemm: split-K needs a store or accumulate epilogue");
+    const int wrc = split_workspace(stream, plane * la.ks, &split_ws);
+    if (wrc == OK) {
+      epi.split_final = epi.kind == EPI_STORE ? EPI_STORE : EPI_ACCUM;
+      epi.kind = EPI_RED;
+      epi.split_ws = split_ws;
+    } else if (wrc == ERR_UNSUPPORTED) {  // capturing: one pass over K
+      la.kt_per = kt_total;
+      la.ks = 1;
+    } else {
+      return wrc;
     }
-    epi.kind = EPI_RED;
   }
   int rc;
   const int BKm = plan.pair ? PairShape<64>::BK : BK;  // k-tile depth of the chosen kernel
@@ -1427,9 +1543,23 @@ int gemm_tf32(cudaStream_t stream, int M, int N, int K, int batch, const GemmOpe
   else
     rc = make_map(&la.mb, B.ptr, N, K, bdiv, batch / bdiv, B.ld, B.stride, B.stride_hi, 32, BKm, true);
   if (rc) return rc;
-  if (plan.pair) return dispatch_pair(BN, A.mn_major, B.mn_major, la);
-  if (dual) return dispatch_dual(BN, A.mn_major, B.mn_major, la);
-  return x3 ? dispatch_bn<true>(BN, A.mn_major, B.mn_major, la) : dispatch_bn<false>(BN, A.mn_major, B.mn_major, la);
+  if (plan.pair)
+    rc = dispatch_pair(BN, A.mn_major, B.mn_major, la);
+  else if (dual)
+    rc = dispatch_dual(BN, A.mn_major, B.mn_major, la);
+  else
+    rc = x3 ? dispatch_bn<true>(BN, A.mn_major, B.mn_major, la) : dispatch_bn<false>(BN, A.mn_major, B.mn_major, la);
+  if (rc || la.ks == 1) return rc;
+  const GemmEpi& e = la.epi;
+  const bool vec = N % 4 == 0 && e.ldc % 4 == 0 && e.strideC % 4 == 0 && e.strideC_hi % 4 == 0 &&
+                   (reinterpret_cast<uintptr_t>(e.C) & 15) == 0;
+  const size_t work = vec ? plane / 4 : plane;
+  const int blocks = (int)std::min<size_t>((work + 255) / 256, (size_t)num_sms() * 8);
+  TURT_CHECK_CUDA((launch_pdl(k_splitk_reduce, dim3(blocks), dim3(256), 0, stream, (const float*)split_ws, la.ks, M, N,
+                              batch, e.C, e.ldc, e.strideC, e.strideC_hi, bdiv, e.split_final == EPI_ACCUM ? 1 : 0,
+                              vec ? 1 : 0)));
+  TURT_LAUNCH_CHECK();
+  return OK;
 }
 
 int gemm_simt(cudaStream_t stream, const float* A, const float* B, float* C, int M, int K, int N, int batch,

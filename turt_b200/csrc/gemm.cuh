@@ -9,7 +9,8 @@ namespace turt {
 enum EpiKind : int {
   EPI_STORE = 0,       // C = acc
   EPI_ACCUM = 1,       // C += acc
-  EPI_RED = 2,         // C += acc with atomic adds (split-K partial sums)
+  EPI_RED = 2,         // split-K partial sums (set by gemm_tf32): each split stores its partial
+                       // plane; a reduction kernel adds them in split order and applies split_final
   EPI_ADD_RES = 3,     // C = acc + R            (residual add)
   EPI_BIAS = 4,        // C = acc + bias[n]
   EPI_BIAS_GELU = 5,   // C = acc + bias[n] (pre-activation), C2 = gelu(C)
@@ -54,6 +55,10 @@ struct GemmEpi {
   int rope_T = 0, rope_H = 0, rope_hd = 0;
   float* qr = nullptr;
   float* kr = nullptr;
+  // Split-K (kind EPI_RED, filled in by gemm_tf32): partial planes [batch][ksplits][M][N] and the
+  // epilogue the summed result takes (EPI_STORE or EPI_ACCUM).
+  float* split_ws = nullptr;
+  int split_final = EPI_STORE;
 };
 
 // Operand description.  `mn_major` = the operand's contiguous dimension is M (for A) or N
@@ -71,7 +76,10 @@ struct GemmOperand {
 enum GemmPrecision : int { GEMM_TF32 = 1, GEMM_TF32X3 = 3 };
 
 // C[M,N] (per batch) = A[M,K] * B[K,N] with the epilogue applied.  K-splits > 1 are chosen
-// automatically for accumulate epilogues when the tile count is below the SM count.
+// automatically for store / accumulate epilogues when the tile count is below the SM count;
+// their partial sums are added in a fixed order (the result does not depend on scheduling),
+// through a workspace held per (device, stream) and grown on first need.  force_splits = 1
+// disables splitting (no workspace is touched).
 int gemm_tf32(cudaStream_t stream, int M, int N, int K, int batch, const GemmOperand& A,
               const GemmOperand& B, const GemmEpi& epi, int* dev_flags, int precision = GEMM_TF32X3,
               int force_splits = 0);
@@ -84,6 +92,10 @@ int tensor_map_f32(CUtensorMap* map, const GemmOperand& op, long inner, long row
 
 // True when gemm_tf32 can take these operands (TMA needs 16-byte pitches and bases).
 bool gemm_tf32_supported(const GemmOperand& A, const GemmOperand& B);
+
+// Frees the split-K workspace held for `st` on the current device (call before destroying a
+// stream that ran GEMMs).
+void gemm_release_stream(cudaStream_t st);
 
 // Forces the output-tile width (64/128/192/256; 0 = automatic) and the kernel (pair = 1: CTA
 // pair, 0: single CTA, -1: automatic) of every later gemm_tf32 call.

@@ -144,10 +144,24 @@ void free_workspace(turt_model* m) {
 // probabilities of every layer fit the budget, else the fused CUDA-core kernels.
 constexpr size_t kAttnScoreBudget = (size_t)16 << 30;  // bytes
 
+// Model GEMMs run on the tensor cores: FP32 (CUDA-core) precision applies to op-level calls only.
+inline int mp(const turt_model* m) { return m->ctx->precision == 0 ? GEMM_TF32X3 : m->ctx->precision; }
+
+// True when the tensor-core attention runs the online-softmax kernels (row log-sum-exp kept for
+// the backward pass) instead of keeping [B*H][T][pitch] probabilities: on request, or by default
+// for sequences longer than the single-pass fused kernels hold.
+bool attention_online(const turt_model* m, int T) {
+  const int hd = m->cfg.n_embd / m->cfg.n_head;
+  if (m->attn_mode == TURT_ATTN_TENSOR_ONLINE) return true;
+  return m->attn_mode != TURT_ATTN_FLASH && attention_tc_prefers_online(T, hd, mp(m));
+}
+bool attention_keeps_P(const turt_model* m, int T) { return !attention_online(m, T); }
+
 bool use_tensor_attention(const turt_model* m, int B, int T) {
   const int hd = m->cfg.n_embd / m->cfg.n_head;
   if (m->attn_mode == TURT_ATTN_FLASH || !attention_tc_supported(hd)) return false;
-  if (m->attn_mode == TURT_ATTN_TENSOR) return true;
+  if (m->attn_mode == TURT_ATTN_TENSOR || m->attn_mode == TURT_ATTN_TENSOR_ONLINE || !attention_keeps_P(m, T))
+    return true;
   const size_t bytes = (size_t)m->cfg.n_layer * B * m->cfg.n_head * T * attn_pitch(T) * 4;
   return bytes <= kAttnScoreBudget;
 }
@@ -156,7 +170,7 @@ bool use_tensor_attention(const turt_model* m, int B, int T) {
 int ensure_workspace(turt_model* m, int B, int T) {
   const int N = B * T;
   const bool tc = use_tensor_attention(m, B, T);
-  const long S_need = tc ? (long)B * m->cfg.n_head * T * attn_pitch(T) : 0;
+  const long S_need = tc && attention_keeps_P(m, T) ? (long)B * m->cfg.n_head * T * attn_pitch(T) : 0;
   if (N <= m->capN && B * m->cfg.n_head * T <= m->capB && tc == m->attn_tc && S_need <= m->capS) return OK;
   if (!tc && !attention_supported_hd(m->cfg.n_embd / m->cfg.n_head)) {
     set_error("fused CUDA-core attention supports head dim 16, 32 or 64; the tensor-core path is off or over budget");
@@ -193,7 +207,7 @@ int ensure_workspace(turt_model* m, int B, int T) {
     a.mu2 = m->modern ? 0 : take(N);
     a.pre = take((size_t)N * W1);
     a.act = take((size_t)N * h);
-    a.P = tc ? take((size_t)S_need) : 0;
+    a.P = S_need ? take((size_t)S_need) : 0;
     a.qr = tc && rope ? take(NE) : 0;
     a.kr = tc && rope ? take(NE) : 0;
   }
@@ -201,7 +215,7 @@ int ensure_workspace(turt_model* m, int B, int T) {
   size_t logits = take((size_t)N * V), loss_rows = take(N);
   size_t dx = take(NE), dy = take(NE), datt = take(NE), dqkv = take(3 * NE), dpre = take((size_t)N * W1);
   size_t Dsc = take(BHT);
-  size_t dS = tc ? take((size_t)S_need) : 0;
+  size_t dS = S_need ? take((size_t)S_need) : 0;
   size_t dact = rope ? take((size_t)N * h) : 0;
   const int C = 3 * E > W1 ? 3 * E : W1;
   size_t part = take((size_t)2 * norm_parts(N) * (C > E ? C : E));
@@ -228,7 +242,7 @@ int ensure_workspace(turt_model* m, int B, int T) {
     A.mu2 = m->modern ? nullptr : F(a.mu2);
     A.pre = F(a.pre);
     A.act = F(a.act);
-    A.P = tc ? F(a.P) : nullptr;
+    A.P = S_need ? F(a.P) : nullptr;
     A.qr = tc && rope ? F(a.qr) : nullptr;
     A.kr = tc && rope ? F(a.kr) : nullptr;
   }
@@ -244,7 +258,7 @@ int ensure_workspace(turt_model* m, int B, int T) {
   m->dqkv = F(dqkv);
   m->dpre = F(dpre);
   m->Dsc = F(Dsc);
-  m->dS = tc ? F(dS) : nullptr;
+  m->dS = S_need ? F(dS) : nullptr;
   m->dact = rope ? F(dact) : nullptr;
   m->part = F(part);
   m->d_ids = reinterpret_cast<uint32_t*>(base + ids);
@@ -270,9 +284,6 @@ inline GemmEpi epi(int kind, float* C, long ldc) {
   e.ldc = ldc;
   return e;
 }
-
-// Model GEMMs run on the tensor cores: FP32 (CUDA-core) precision applies to op-level calls only.
-inline int mp(const turt_model* m) { return m->ctx->precision == 0 ? GEMM_TF32X3 : m->ctx->precision; }
 
 int stage_tokens(turt_model* m, const uint32_t* ids, const uint32_t* tgt, int N) {
   cudaStream_t st = m->ctx->stream;
@@ -314,7 +325,7 @@ int forward(turt_model* m, int B, int T, bool train, float loss_scale, bool logi
     }
     RC(gemm_tf32(st, N, 3 * E, E, 1, opK(a.y1, E), opMN(P + L.wqkv, 3 * E), e, flags, mp(m)));
     if (m->attn_tc) {
-      AttnTensors at{a.P, a.qr, a.kr};
+      AttnTensors at{a.P, a.qr, a.kr, a.lse, attention_online(m, T)};
       RC(attention_tc_fwd(st, a.qkv, m->rope_cs, a.att, at, B, T, H, hd, m->modern ? 1 : 0, rope_epi ? 1 : 0, flags,
                           mp(m)));
     } else {
@@ -457,9 +468,9 @@ int backward(turt_model* m, int B, int T) {
     if (!m->modern) RC(colsum_accum(st, m->dx, N, E, G + L.bproj, m->part));
     RC(wait_mark(3));  // dqkv is rewritten below; the previous layer's dWqkv reads it
     if (m->attn_tc) {
-      AttnTensors at{a.P, a.qr, a.kr};
-      AttnScratch sc{m->dS};
-      RC(attention_tc_bwd(st, a.qkv, m->rope_cs, m->datt, at, sc, m->dqkv, B, T, H, hd, m->modern ? 1 : 0, flags,
+      AttnTensors at{a.P, a.qr, a.kr, a.lse, attention_online(m, T)};
+      AttnScratch sc{m->dS, m->Dsc};
+      RC(attention_tc_bwd(st, a.qkv, m->rope_cs, a.att, m->datt, at, sc, m->dqkv, B, T, H, hd, m->modern ? 1 : 0, flags,
                           mp(m)));
     } else {
       RC(attention_bwd(st, a.qkv, m->rope_cs, a.att, m->datt, a.lse, m->Dsc, m->dqkv, B, T, H, hd,
@@ -591,10 +602,12 @@ int turt_model_create(turt_ctx* ctx, const turt_config* cfg, turt_model** out) {
 
 int turt_model_set_attention(turt_model* m, int mode) {
   TURT_REQUIRE(m, "null model");
-  TURT_REQUIRE(mode == TURT_ATTN_AUTO || mode == TURT_ATTN_TENSOR || mode == TURT_ATTN_FLASH,
-               "attention mode must be 0 (auto), 1 (tensor) or 2 (flash)");
+  TURT_REQUIRE(mode >= TURT_ATTN_AUTO && mode <= TURT_ATTN_TENSOR_ONLINE,
+               "attention mode must be 0 (auto), 1 (tensor), 2 (flash) or 3 (tensor online)");
   const int hd = m->cfg.n_embd / m->cfg.n_head;
   if (mode == TURT_ATTN_TENSOR) TURT_REQUIRE(attention_tc_supported(hd), "tensor-core attention needs hd % 16 == 0");
+  if (mode == TURT_ATTN_TENSOR_ONLINE)
+    TURT_REQUIRE(attention_flash_supported(1, hd), "online-softmax tensor-core attention needs hd of 32 or 64");
   if (mode == TURT_ATTN_FLASH) TURT_REQUIRE(attention_supported_hd(hd), "flash attention needs hd of 16, 32 or 64");
   m->attn_mode = mode;
   return OK;
@@ -605,6 +618,7 @@ int turt_model_destroy(turt_model* m) {
   cudaStreamSynchronize(m->ctx->stream);
   if (m->wg) {
     cudaStreamSynchronize(m->wg);
+    gemm_release_stream(m->wg);
     cudaStreamDestroy(m->wg);
   }
   for (auto& e : m->wg_ring)

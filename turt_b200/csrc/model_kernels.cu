@@ -36,19 +36,101 @@ __global__ void k_embed(const float* __restrict__ wte, const float* __restrict__
   }
 }
 
-// dwte[ids[n],:] += dx[n,:] (and dwpe[n % T,:] += dx[n,:]); GATHER_BWD, autograd.ts:428-438,
-// as atomics over the N*E gradient elements instead of the reference's O(V*N) scan.
-__global__ void k_embed_bwd(const float* __restrict__ dx, const uint32_t* __restrict__ ids, float* __restrict__ dwte,
-                            float* __restrict__ dwpe, int N, int T, int E, int V) {
+// dwte[v,:] += sum of dx[i,:] over the positions i with ids[i] == v, added one position at a
+// time in increasing i onto the running value, exactly the order of GATHER_BWD (one thread per
+// vocab row scanning all positions, autograd.ts:428-438), so the result is deterministic.
+// One warp per vocab row; the block stages the ids in shared memory (kIdTile at a time) and
+// each warp finds its row's positions 128 ids per step: every lane compares four ids, a ballot
+// marks the lanes with a match and each match's 4-bit mask is read from its lane in turn.
+// Rows no position uses are not touched.  Ids >= V match no row (the forward flags them).
+constexpr int kIdTile = 8192;        // ids staged per pass (32 KB)
+constexpr int kEmbedRowsPerBlock = 16;
+
+template <int NJ>
+__global__ void __launch_bounds__(32 * kEmbedRowsPerBlock)
+    k_embed_bwd_rows(const float* __restrict__ dx, const uint32_t* __restrict__ ids, float* __restrict__ dwte, int N,
+                     int E, int V) {
+  __shared__ __align__(16) uint32_t sid[kIdTile];
   pdl_trigger();
   pdl_wait();
-  GRID_STRIDE(i, (size_t)N * E) {
-    const int n = (int)(i / E), c = (int)(i % E);
-    const uint32_t id = ids[n];
-    const float g = dx[i];
-    if (id < (uint32_t)V) atomicAdd(dwte + (size_t)id * E + c, g);
-    if (dwpe) atomicAdd(dwpe + (size_t)(n % T) * E + c, g);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t v = (uint32_t)(blockIdx.x * kEmbedRowsPerBlock + warp);
+  const int E4 = E / 4;
+  float4 acc[NJ];
+  bool any = false;  // warp-uniform: every lane sees the same matches
+  for (int base = 0; base < N; base += kIdTile) {
+    const int cnt = min(kIdTile, N - base);
+    const int padded = (cnt + 127) & ~127;
+    __syncthreads();  // the previous tile has been scanned
+    for (int k = threadIdx.x; k < padded; k += blockDim.x) sid[k] = k < cnt ? ids[base + k] : 0xFFFFFFFFu;
+    __syncthreads();
+    if (v >= (uint32_t)V) continue;
+    const uint4* sid4 = reinterpret_cast<const uint4*>(sid);
+    for (int c = 0; c < padded / 128; c++) {
+      const uint4 q = sid4[c * 32 + lane];  // ids base + 128c + 4 lane .. + 3
+      const uint32_t nib = (q.x == v ? 1u : 0u) | (q.y == v ? 2u : 0u) | (q.z == v ? 4u : 0u) | (q.w == v ? 8u : 0u);
+      uint32_t m = __ballot_sync(0xffffffffu, nib != 0);
+      while (m) {
+        const int src = __ffs(m) - 1;
+        m &= m - 1;
+        uint32_t bits = __shfl_sync(0xffffffffu, nib, src);
+        while (bits) {
+          const int k = __ffs(bits) - 1;
+          bits &= bits - 1;
+          const float4* g = reinterpret_cast<const float4*>(dx + (size_t)(base + 128 * c + 4 * src + k) * E);
+          if (!any) {
+            const float4* w = reinterpret_cast<const float4*>(dwte + (size_t)v * E);
+#pragma unroll
+            for (int j = 0; j < NJ; j++)
+              if (lane + 32 * j < E4) acc[j] = w[lane + 32 * j];
+            any = true;
+          }
+#pragma unroll
+          for (int j = 0; j < NJ; j++)
+            if (lane + 32 * j < E4) {
+              const float4 t = g[lane + 32 * j];
+              acc[j].x += t.x, acc[j].y += t.y, acc[j].z += t.z, acc[j].w += t.w;
+            }
+        }
+      }
+    }
   }
+  if (any) {
+    float4* w = reinterpret_cast<float4*>(dwte + (size_t)v * E);
+#pragma unroll
+    for (int j = 0; j < NJ; j++)
+      if (lane + 32 * j < E4) w[lane + 32 * j] = acc[j];
+  }
+}
+
+// dwpe[t,:] += dx[b*T + t,:] for b = 0, 1, ... in order (the learned positions' share of the
+// gpt2 embedding backward, deterministic): one warp per position.
+template <int NJ>
+__global__ void __launch_bounds__(256) k_pos_bwd(const float* __restrict__ dx, float* __restrict__ dwpe, int N, int T,
+                                                 int E) {
+  pdl_trigger();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= T || t >= N) return;
+  const int E4 = E / 4;
+  float4* w = reinterpret_cast<float4*>(dwpe + (size_t)t * E);
+  float4 acc[NJ];
+#pragma unroll
+  for (int j = 0; j < NJ; j++)
+    if (lane + 32 * j < E4) acc[j] = w[lane + 32 * j];
+  for (int n = t; n < N; n += T) {
+    const float4* g = reinterpret_cast<const float4*>(dx + (size_t)n * E);
+#pragma unroll
+    for (int j = 0; j < NJ; j++)
+      if (lane + 32 * j < E4) {
+        const float4 x = g[lane + 32 * j];
+        acc[j].x += x.x, acc[j].y += x.y, acc[j].z += x.z, acc[j].w += x.w;
+      }
+  }
+#pragma unroll
+  for (int j = 0; j < NJ; j++)
+    if (lane + 32 * j < E4) w[lane + 32 * j] = acc[j];
 }
 
 // ------------------------------------------------------------------ norms
@@ -663,13 +745,7 @@ int embed_fwd(cudaStream_t st, const float* wte, const float* wpe, const uint32_
   TURT_LAUNCH_CHECK();
   return OK;
 }
-int embed_bwd(cudaStream_t st, const float* dx, const uint32_t* ids, float* dwte, float* dwpe, int N, int T, int E,
-              int V) {
-  const size_t n = (size_t)N * E;
-  TURT_CHECK_CUDA((launch_pdl(k_embed_bwd, dim3((int)std::min<size_t>((n + 255) / 256, 148 * 32)), dim3(256), 0, st, dx, ids, dwte, dwpe, N, T, E, V)));
-  TURT_LAUNCH_CHECK();
-  return OK;
-}
+
 namespace {
 int sm_count() {
   static int n = 0;
@@ -694,6 +770,26 @@ int sm_count() {
     default: CALL(8); break;    \
   }
 }  // namespace
+
+int embed_bwd(cudaStream_t st, const float* dx, const uint32_t* ids, float* dwte, float* dwpe, int N, int T, int E,
+              int V) {
+  TURT_REQUIRE(E % 4 == 0 && E <= 1024, "embedding width must be a multiple of 4, at most 1024");
+  const dim3 grid_rows((V + kEmbedRowsPerBlock - 1) / kEmbedRowsPerBlock);
+#define TURT_EMBED_BWD(NJV)                                                                                     \
+  TURT_CHECK_CUDA((launch_pdl(k_embed_bwd_rows<NJV>, grid_rows, dim3(32 * kEmbedRowsPerBlock), 0, st, dx, ids, \
+                              dwte, N, E, V)));
+  TURT_NJ_SWITCH(E, TURT_EMBED_BWD)
+#undef TURT_EMBED_BWD
+  TURT_LAUNCH_CHECK();
+  if (dwpe) {
+#define TURT_POS_BWD(NJV) \
+  TURT_CHECK_CUDA((launch_pdl(k_pos_bwd<NJV>, dim3((T + 7) / 8), dim3(256), 0, st, dx, dwpe, N, T, E)));
+    TURT_NJ_SWITCH(E, TURT_POS_BWD)
+#undef TURT_POS_BWD
+    TURT_LAUNCH_CHECK();
+  }
+  return OK;
+}
 
 int rms_fwd(cudaStream_t st, const float* x, const float* g, float* y, float* rstd, int rows, int E, float eps) {
   TURT_REQUIRE(E % 32 == 0 && E <= 32 * MAXV, "norm width must be a multiple of 32, at most 1024");

@@ -110,7 +110,8 @@ extern "C" int turt_host_matmul_noalloc(turt_ctx* ctx, const float* a, int m, in
       epi.C = dc;
       epi.ldc = (long)np;
       epi.strideC = (long)(m * np);
-      rc = gemm_tf32(st, m, n, k, 1, A, B, epi, ctx->flags, ctx->precision);
+      // one pass over K: a split would stage partial sums in a workspace allocated on demand
+      rc = gemm_tf32(st, m, n, k, 1, A, B, epi, ctx->flags, ctx->precision, /*force_splits=*/1);
     }
     if (rc) return rc;
   }

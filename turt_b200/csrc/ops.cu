@@ -213,16 +213,28 @@ __global__ void k_gather(const float* table, const uint32_t* idx, float* out, in
     out[i] = table[(size_t)r * d + col];
   }
 }
+// GATHER_BWD (autograd.ts:428-438): dTable[v,:] = dTable[v,:] + gOut[i,:] for each position i
+// with idx[i] == v, in increasing i -- the reference's order, so the result is deterministic and
+// matches its arithmetic.  One warp per vocab row: lanes compare 32 ids at a time and a ballot
+// lists the matching positions; each match is added in place, lane-strided over the columns.
+// Ids >= vocab raise the range flag (block 0 checks them) and match no row.
 __global__ void k_gather_bwd(const uint32_t* idx, const float* go, float* dt, int n, int d, int vocab, int* flags) {
-  size_t total = (size_t)n * d;
-  GRID_STRIDE(i, total) {
-    size_t row = i / d, col = i % d;
-    uint32_t r = idx[row];
-    if (r >= (uint32_t)vocab) {
-      atomicExch(&flags[FLAG_RANGE], 1);
-      continue;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+      if (idx[i] >= (uint32_t)vocab) atomicExch(&flags[FLAG_RANGE], 1);
+  const uint32_t v = (uint32_t)(blockIdx.x * (blockDim.x >> 5) + warp);
+  if (v >= (uint32_t)vocab) return;
+  float* row = dt + (size_t)v * d;
+  for (int base = 0; base < n; base += 32) {
+    const int i = base + lane;
+    uint32_t m = __ballot_sync(0xffffffffu, i < n && idx[i] == v);
+    while (m) {
+      const int k = __ffs(m) - 1;
+      m &= m - 1;
+      const float* g = go + (size_t)(base + k) * d;
+      for (int c = lane; c < d; c += 32) row[c] = row[c] + g[c];
     }
-    atomicAdd(&dt[(size_t)r * d + col], go[i]);
   }
 }
 // Cross-entropy: one block per row (logsumexp - logit[target]).
@@ -431,7 +443,10 @@ int op_gather(cudaStream_t st, const float* table, const uint32_t* idx, float* o
 }
 int op_gather_bwd(cudaStream_t st, const uint32_t* idx, const float* go, float* dt, int n, int d, int vocab,
                   int* flags) {
-  LAUNCH_1D(k_gather_bwd, (size_t)n * d, idx, go, dt, n, d, vocab, flags);
+  if (n <= 0 || d <= 0 || vocab <= 0) return OK;
+  k_gather_bwd<<<ceil_div(vocab, 8), 256, 0, st>>>(idx, go, dt, n, d, vocab, flags);
+  TURT_LAUNCH_CHECK();
+  return OK;
 }
 int op_ce_fwd(cudaStream_t st, const float* logits, const uint32_t* tgt, float* per_row, int rows, int vocab,
               int* flags) {

@@ -104,11 +104,12 @@ class Model:
     def handle(self):
         return self._h
 
-    ATTN_AUTO, ATTN_TENSOR, ATTN_FLASH = 0, 1, 2
+    ATTN_AUTO, ATTN_TENSOR, ATTN_FLASH, ATTN_TENSOR_ONLINE = 0, 1, 2, 3
 
     def set_attention(self, mode: int) -> None:
-        """Attention implementation: ATTN_AUTO, ATTN_TENSOR (tensor-core, materialised
-        probabilities) or ATTN_FLASH (fused CUDA-core online softmax)."""
+        """Attention implementation: ATTN_AUTO, ATTN_TENSOR (tensor-core, probabilities kept for
+        the backward pass), ATTN_FLASH (fused CUDA-core online softmax) or ATTN_TENSOR_ONLINE
+        (tensor-core online softmax, probabilities recomputed in the backward pass)."""
         check(lib().turt_model_set_attention(self._h, mode))
 
     def num_params(self) -> int:
@@ -258,4 +259,92 @@ class Model:
     def close(self) -> None:
         if self._h:
             lib().turt_model_destroy(self._h)
+            self._h = C.c_void_p()
+
+
+class Group:
+    """Several GPUs driven from this one process: one model replica per device, the batch split
+    into contiguous shards and the gradients summed over NCCL inside the backward pass (the
+    reference's in-process worker pool, scripts/train-gpt.ts:66-123,200-219)."""
+
+    def __init__(self, devices, cfg: TurtConfig):
+        devs = (C.c_int * len(devices))(*devices)
+        self.cfg = cfg
+        self.devices = list(devices)
+        self._h = C.c_void_p()
+        check(lib().turt_group_create(len(devices), devs, C.byref(cfg), C.byref(self._h)))
+        rep = C.c_void_p()
+        check(lib().turt_group_model(self._h, 0, C.byref(rep)))
+        n = C.c_int()
+        check(lib().turt_param_count(rep, C.byref(n)))
+        self.names, self.shapes = [], []
+        buf = C.create_string_buffer(64)
+        shp = (C.c_int * 2)()
+        nd = C.c_int()
+        for i in range(n.value):
+            check(lib().turt_param_info(rep, i, buf, 64, shp, C.byref(nd)))
+            self.names.append(buf.value.decode())
+            self.shapes.append((shp[0], shp[1]) if nd.value == 2 else (shp[0],))
+
+    def sizes(self):
+        return [int(np.prod(s)) for s in self.shapes]
+
+    def replica(self, i: int) -> int:
+        """turt_model handle of replica i (for per-device reads)."""
+        rep = C.c_void_p()
+        check(lib().turt_group_model(self._h, i, C.byref(rep)))
+        return rep
+
+    def load_flat(self, flat: np.ndarray) -> None:
+        flat = f32(flat)
+        off = 0
+        for i, n in enumerate(self.sizes()):
+            seg = np.ascontiguousarray(flat[off:off + n])
+            check(lib().turt_group_param_upload(self._h, i, ptr(seg), n))
+            off += n
+
+    def _download_flat(self, fn, handle) -> np.ndarray:
+        out = np.empty(sum(self.sizes()), dtype=np.float32)
+        off = 0
+        for i, n in enumerate(self.sizes()):
+            seg = np.empty(n, dtype=np.float32)
+            check(fn(handle, i, ptr(seg), n))
+            out[off:off + n] = seg
+            off += n
+        return out
+
+    def grads_flat(self, replica=None) -> np.ndarray:
+        if replica is None:
+            return self._download_flat(lib().turt_group_grad_download, self._h)
+        return self._download_flat(lib().turt_grad_download, self.replica(replica))
+
+    def params_flat(self, replica=None) -> np.ndarray:
+        if replica is None:
+            return self._download_flat(lib().turt_group_param_download, self._h)
+        return self._download_flat(lib().turt_param_download, self.replica(replica))
+
+    def zero_grad(self) -> None:
+        check(lib().turt_group_zero_grad(self._h))
+
+    def defer(self, defer: bool) -> None:
+        check(lib().turt_group_defer(self._h, 1 if defer else 0))
+
+    def forward_backward(self, ids, targets, b: int, t: int, loss_scale: float = 1.0, want_loss=True):
+        ids, targets = u32(ids), u32(targets)
+        if ids.size != b * t or targets.size != b * t:
+            raise ValueError(f"expected {b * t} ids and targets")
+        loss = C.c_float()
+        check(lib().turt_group_forward_backward(self._h, ptr(ids), ptr(targets), b, t, loss_scale,
+                                                C.byref(loss) if want_loss else None))
+        return loss.value if want_loss else None
+
+    def adamw_step(self, lr, b1, b2, eps, wd, bc1, bc2, clip=0.0) -> None:
+        check(lib().turt_group_adamw_step(self._h, lr, b1, b2, eps, wd, bc1, bc2, clip))
+
+    def synchronize(self) -> None:
+        check(lib().turt_group_synchronize(self._h))
+
+    def close(self) -> None:
+        if self._h:
+            lib().turt_group_destroy(self._h)
             self._h = C.c_void_p()
