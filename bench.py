@@ -34,6 +34,8 @@ WORKLOADS = {
                             global_batch=True),
     "gpt-tiny-4L-128d": dict(V=8192, T=128, L=4, H=4, E=128, arch="modern", hidden=352, batch=8, micro=8),
 }
+# turt_model_set_attention modes
+ATTENTION_MODES = {"auto": 0, "tensor": 1, "flash": 2, "online": 3}
 CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -224,6 +226,59 @@ def time_gemm(ctx, M, N, K, reps, precision):
     return ms
 
 
+def train_throughput(name: str, steps: int, warmup: int, attention: str = "auto"):
+    """Device-resident train steps (fwd + bwd + clip + AdamW) of workload `name` on this
+    process's current GPU, the whole batch of one GPU per step (micro-batches accumulated):
+    tokens/s and ms per step from CUDA events on the library's stream."""
+    import numpy as np
+    import torch
+
+    from turt_b200.runtime import Context, Model, make_config
+    w = WORKLOADS[name]
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx = Context(torch.cuda.current_device())
+    ctx.set_stream(stream.cuda_stream)
+    model = Model(ctx, make_config(w["V"], w["T"], w["L"], w["H"], w["E"], w["arch"], w["hidden"]))
+    model.set_attention(ATTENTION_MODES[attention])
+    init_weights(model, w, 1234)
+    seqs, micro, T = w["batch"], w["micro"], w["T"]
+    rng = np.random.default_rng(7)
+    ids = torch.from_numpy(rng.integers(0, w["V"], seqs * T).astype(np.int32)).cuda()
+    tgt = torch.from_numpy(rng.integers(0, w["V"], seqs * T).astype(np.int32)).cuda()
+    k = [0]
+
+    def step():
+        model.zero_grad()
+        for j in range(seqs // micro):
+            off = j * micro * T * 4
+            model.forward_backward_device(ids.data_ptr() + off, tgt.data_ptr() + off, micro, T, loss_scale=micro / seqs)
+        k[0] += 1
+        model.adamw_step(3e-4, 0.9, 0.95, 1e-8, 0.1, 1 - 0.9 ** k[0], 1 - 0.95 ** k[0], clip=1.0)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    loss = model.read_loss()
+    model.close()
+    ctx.close()
+    del ids, tgt
+    torch.cuda.empty_cache()
+    tok = seqs * T / (ms / 1000.0)
+    peaks = measured_peaks()
+    tflops = flops_per_token(w) * tok / 1e12
+    return {"value": tok, "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "warmup": warmup,
+            "global_batch": seqs, "micro_batch": micro, "seq_len": T, "attention": attention, "last_loss": loss,
+            "achieved_tflops": tflops, "frac_of_sustained_tf32": tflops / (peaks["bf16_tflops_sustained"] / 2.0)}
+
+
 def run_gpu(args, w, rank: int, world: int, local_rank: int) -> None:
     import numpy as np
     import torch
@@ -242,6 +297,7 @@ def run_gpu(args, w, rank: int, world: int, local_rank: int) -> None:
     ctx.set_stream(stream.cuda_stream)
     ctx.set_precision(args.precision)
     model = Model(ctx, make_config(w["V"], w["T"], w["L"], w["H"], w["E"], w["arch"], w["hidden"]))
+    model.set_attention(ATTENTION_MODES[args.attention])
     init_weights(model, w, 1234)
     if world > 1:
         uid = [Model.dp_unique_id() if rank == 0 else None]
@@ -347,7 +403,7 @@ def run_gpu(args, w, rank: int, world: int, local_rank: int) -> None:
             "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "tf32x3" if args.precision == 3 else "tf32", "data": "synthetic",
             "config": {"workload": args.workload, "model": args.workload, "global_batch": global_seqs, "seq_len": T,
-                       "parallelism": f"dp{world}", "micro_batch": micro,
+                       "parallelism": f"dp{world}", "micro_batch": micro, "attention": args.attention,
                        "gemm_precision": "3xTF32 (error-compensated)" if args.precision == 3 else "TF32",
                        "l2": "no flush: each step touches >1 GB of activations and weights (L2 is 126 MB)",
                        "last_loss": last_loss},
@@ -372,6 +428,16 @@ def run_gpu(args, w, rank: int, world: int, local_rank: int) -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if rank == 0 and world == 1 and args.extra_workloads:
+        # the other configurations on the same box, device-resident (no e2e), after the headline run
+        extra = {}
+        for name, steps, warm in (("gpt2-12L-768d", 5, 3), ("gpt-12L-768d-dp", 2, 3)):
+            if name != args.workload:
+                extra[name] = train_throughput(name, steps, warm)
+        kernels, total_ms, value_ops, _, _ = measure_backward_ops(10, 3)
+        extra["backward-ops"] = {"value": value_ops, "unit": "GB/s", "kernels": kernels,
+                                 "note": "each launch alone after an L2 flush; median of 10"}
+        out["extra_workloads"] = extra
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         workers = pool_workers(w)
         step, tokens = cpu_pool_sample(w, workers, 2)
@@ -426,14 +492,10 @@ def read_profile_traffic(name: str, key: str = "traffic_bytes_per_launch"):
     return int(m.group(1)) if m else None
 
 
-def run_backward_ops(args, rank: int) -> None:
+def measure_backward_ops(steps: int, warmup: int):
     """Standalone timing of the train step's fused memory-bound backward kernels on seeded
-    N(0, 1) inputs with 8192 rows; each launch timed alone with CUDA events after an L2 flush."""
-    if rank != 0:
-        return
-    import ctypes as C
-
-    import numpy as np
+    N(0, 1) inputs with 8192 rows; each launch timed alone with CUDA events after an L2 flush.
+    Returns (per-kernel results, total ms, aggregate GB/s, launches, clock summary)."""
     import torch
 
     from turt_b200._lib import check, lib
@@ -477,12 +539,12 @@ def run_backward_ops(args, rank: int) -> None:
     peaks = measured_peaks()
     kernels = {}
     launches0 = Context.launch_count()
-    with ClockSampler(0) as clk:
+    with ClockSampler(torch.cuda.current_device()) as clk:
         for name, fn in calls.items():
-            for _ in range(args.warmup):
+            for _ in range(warmup):
                 fn()
             times = []
-            for _ in range(args.steps):
+            for _ in range(steps):
                 flush.fill_(1.0)  # evict: 256 MB of writes
                 flush_rd.sum()    # ... then 256 MB of reads, so no dirty line is written back inside the launch
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -498,6 +560,16 @@ def run_backward_ops(args, rank: int) -> None:
     total_ms = sum(k["ms"] for k in kernels.values())
     total_bytes = sum(nbytes.values())
     value = total_bytes / (total_ms / 1000.0) / 1e9
+    ctx.close()
+    return kernels, total_ms, value, launches, clk.summary()
+
+
+def run_backward_ops(args, rank: int) -> None:
+    if rank != 0:
+        return
+    kernels, total_ms, value, launches, clocks = measure_backward_ops(args.steps, args.warmup)
+    peaks = measured_peaks()
+    N = OP_ROWS
     top = "softmax_ce_grad [8192,8192]"
     out = {
         "metric": "standalone backward-op kernels: algorithmic HBM bytes / time", "value": value, "unit": "GB/s",
@@ -512,9 +584,8 @@ def run_backward_ops(args, rank: int) -> None:
                      "traffic": read_profile_traffic("backward_ops_8192rows.md", "k_ce_fused_traffic_bytes_per_launch"),
                      "peak_source": f"{peaks['source']} HBM copy"},
         "gpu_launches": launches,
-        "clocks": clk.summary(),
+        "clocks": clocks,
     }
-    ctx.close()
     if not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_ops_baseline()
     out["e2e"] = {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0,
@@ -792,6 +863,11 @@ def main():
     ap.add_argument("--gemm", default="8192,8192,384", help="M,N,K of the gemm workload")
     ap.add_argument("--precision", type=int, default=3, choices=[1, 3])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra-workloads", dest="extra_workloads", action="store_false",
+                    help="skip timing the gpt2-12L-768d, 12L-768d data-parallel (1 GPU) and backward-op "
+                         "workloads after the headline run (N = 1 only)")
+    ap.add_argument("--attention", default="auto", choices=sorted(ATTENTION_MODES),
+                    help="attention kernels of the train step (turt_model_set_attention)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
