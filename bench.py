@@ -33,6 +33,8 @@ WORKLOADS = {
     "gpt-12L-768d-dp": dict(V=8192, T=1024, L=12, H=12, E=768, arch="modern", hidden=2048, batch=256, micro=16,
                             global_batch=True),
     "gpt-tiny-4L-128d": dict(V=8192, T=128, L=4, H=4, E=128, arch="modern", hidden=352, batch=8, micro=8),
+    # two layers of the gpt2 workload: a small case of its kernels for profiler captures
+    "gpt2-2L-768d": dict(V=8192, T=512, L=2, H=12, E=768, arch="gpt2", hidden=3072, batch=16, micro=16),
 }
 # turt_model_set_attention modes
 ATTENTION_MODES = {"auto": 0, "tensor": 1, "flash": 2, "online": 3}

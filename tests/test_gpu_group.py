@@ -45,9 +45,13 @@ def test_group_matches_full_batch(ndev, b, arch):
     g = Group(list(range(ndev)), make_config(V, T, L, H, E, arch))
     try:
         g.load_flat(params)
-        g.zero_grad()
-        loss = g.forward_backward(ids, tgt, b, t)
-        grads = [g.grads_flat(r) for r in range(ndev)]
+        # the first call of a shape reduces after the whole backward, later ones per layer
+        for _ in range(2):
+            g.zero_grad()
+            loss = g.forward_backward(ids, tgt, b, t)
+            grads = [g.grads_flat(r) for r in range(ndev)]
+            assert max_rel_err([loss], [ref_loss]) <= 1e-4, (loss, ref_loss)
+            assert max_rel_err(grads[0], ref_g) <= 2e-3
         g.adamw_step(3e-4, 0.9, 0.95, 1e-8, 0.1, 0.1, 0.05, clip=1.0)
         g.synchronize()
         new = [g.params_flat(r) for r in range(ndev)]

@@ -12,6 +12,7 @@
 // the reference's weighting exactly, so the optimizer step needs no further scaling.
 #include <condition_variable>
 #include <deque>
+#include <set>
 #include <functional>
 #include <mutex>
 #include <string>
@@ -101,6 +102,7 @@ struct turt_group {
   std::vector<turt_model*> model;
   std::vector<turt::DeviceWorker*> workers;
   bool defer = false;
+  std::set<std::pair<int, int>> shapes_seen;  // (b, t) of batches already run with reduction
 };
 
 using namespace turt;
@@ -182,7 +184,7 @@ int turt_group_create(int ndev, const int* devs, const turt_config* cfg, turt_gr
   g->ctx.assign(ndev, nullptr);
   g->model.assign(ndev, nullptr);
   for (int i = 0; i < ndev; i++) g->workers.push_back(new DeviceWorker(devs[i]));
-  int rc = run_all(g, [g, cfg](int i) {
+  int rc = run_all(g, [g, cfg](int i) -> int {
     RC(turt_init(g->devs[i], &g->ctx[i]));
     return turt_model_create(g->ctx[i], cfg, &g->model[i]);
   });
@@ -272,13 +274,23 @@ int turt_group_forward_backward(turt_group* g, const uint32_t* ids, const uint32
   std::vector<float> loss(g->n, 0.f);
   const bool defer = g->defer;
   const bool want = loss_out != nullptr;
-  int rc = run_all(g, [&](int i) {
-    RC(turt_dp_defer(g->model[i], defer ? 1 : 0));
+  // The first reducing call of a batch shape enqueues its whole backward pass before any
+  // collective (then one all-reduce of the gradient buffer): kernels are loaded on their first
+  // launch, and a load must not wait behind a collective that spins for a peer device whose host
+  // thread is itself still launching.  Later calls overlap the per-layer reductions.
+  const bool first = g->n > 1 && !defer && !g->shapes_seen.count({b, t});
+  int rc = run_all(g, [&](int i) -> int {
+    RC(turt_dp_defer(g->model[i], (defer || first) ? 1 : 0));
     const size_t off = (size_t)row0[i] * t;
-    return turt_forward_backward(g->model[i], ids + off, targets + off, rows[i], t,
-                                 loss_scale * (float)rows[i] / (float)b, want ? &loss[i] : nullptr);
+    RC(turt_forward_backward(g->model[i], ids + off, targets + off, rows[i], t,
+                             loss_scale * (float)rows[i] / (float)b, (want && !first) ? &loss[i] : nullptr));
+    if (!first) return OK;
+    RC(turt_dp_allreduce_grads(g->model[i]));
+    RC(turt_dp_defer(g->model[i], 0));
+    return want ? turt_read_loss(g->model[i], &loss[i]) : OK;
   });
   if (rc) return rc;
+  if (first) g->shapes_seen.insert({b, t});
   if (want) {
     double l = 0;
     for (int i = 0; i < g->n; i++) l += (double)loss[i] * rows[i] / b;
