@@ -12,17 +12,13 @@
 //             recomputing P = exp(scale s - L) block by block (FlashAttention-2's split, with
 //             D = rowsum(dO * O) formed once by the dQ kernel), so every result is a sum in a
 //             fixed order: deterministic, no atomics.
-// Arithmetic: fp32 accumulation in TMEM, softmax in fp32; the products with a probability
-// operand (O = P v, dV = P^T dO) are error-compensated 3xTF32 (hi / lo splits), the others
-// (S = q k^T, dP = dO v^T, dQ = dS k, dK = dS^T q) one tf32 pass on operands rounded to nearest
-// (rn_tf32) -- the split of attention_fused.cu.
+// Arithmetic: 3xTF32 products (hi / lo splits, fp32 accumulation in TMEM), softmax in fp32.
 //
-// Shared memory cannot hold every operand tile of a head dim of 64 with its lo part, so every A
+// Shared memory cannot hold the hi and lo copies of every operand at head dim 64, so every A
 // operand lives in tensor memory and the MMAs read it from there (tcgen05.mma with A in TMEM):
-// Q (forward, dQ), dO (dQ), V (dK / dV) are rounded and stored into TMEM by the row warps at
-// the start; P (hi and lo) and dS (rounded) are written back over the scores they come from.
-// Only B operands (K, V, Q, dO tiles) stream through shared memory, by TMA, rounded in place or
-// split into lo parts by converter warps.
+// Q (forward, dQ), dO (dQ), V (dK / dV) are split and stored into TMEM by the row warps at the
+// start; P and dS are written back over the scores they come from.  Only B operands (K, V, Q,
+// dO tiles) stream through shared memory, by TMA, with the lo parts made by converter warps.
 #include "attention.cuh"
 #include "gemm.cuh"
 #include "tcgen05.cuh"
@@ -42,27 +38,6 @@ __device__ __forceinline__ void mma_tf32_ts(uint32_t tmem_d, uint32_t tmem_a, ui
 }
 
 __device__ __forceinline__ float tf32_lo(float x) { return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
-// Nearest tf32 value (ties away from zero): one-pass products on rounded operands are unbiased.
-__device__ __forceinline__ float rn_tf32(float x) {
-  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
-}
-
-// x = rn_tf32(x) for `bytes` of fp32 at `base` (128 converter threads).
-__device__ __forceinline__ void round_inplace(uint8_t* base, int bytes, int ct) {
-  float4* p = reinterpret_cast<float4*>(base);
-#pragma unroll 4
-  for (int e = ct; e < bytes / 16; e += 128) {
-    const float4 v = p[e];
-    p[e] = make_float4(rn_tf32(v.x), rn_tf32(v.y), rn_tf32(v.z), rn_tf32(v.w));
-  }
-}
-
-// Stores 32 floats of this thread's row, rounded to tf32, into TMEM columns [col, col + 32).
-__device__ __forceinline__ void tmem_st_rn(uint32_t col, float* v) {
-#pragma unroll
-  for (int j = 0; j < 32; j++) v[j] = rn_tf32(v[j]);
-  tmem_st32(col, v);
-}
 
 // lo = x - tf32(x) for `bytes` of fp32 at `hi`, written `lo_off` bytes further (128 converter threads).
 __device__ __forceinline__ void split_lo(uint8_t* hi_base, int bytes, int lo_off, int ct) {
@@ -118,11 +93,11 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int n, bool b_mn) {
 //   warp 1      TMEM allocator + MMA issuer: S_j = Q K_j^T into one of two score buffers,
 //               then O += P_{j-1} V_{j-1}, so the scores of block j + 1 are on the tensor cores
 //               while the row warps work on block j
-//   warps 2..5  converters: K rounded in place, lo parts of V
+//   warps 2..5  lo-part converters for the K and V stages
 //   warps 6..9  row warps: warp w owns TMEM lanes (query rows) 32 (w % 4) .. + 31; they load Q
-//               (rounded) into TMEM, run the online softmax and write O and L
-// TMEM columns: Q [0, HD), S / P-hi [HD, HD + 128), P-lo [HD + 128, HD + 256), O [HD + 256,
-// 2 HD + 256).
+//               into TMEM, run the online softmax and write O and L
+// TMEM columns: Q hi | Q lo [0, 2 HD), S / P-hi [2 HD, 2 HD + 128), P-lo [2 HD + 128,
+// 2 HD + 256), O [2 HD + 256, 3 HD + 256).
 template <int HD>
 struct FlashFwd {
   static constexpr int KB = 64;                   // keys per block
@@ -132,10 +107,10 @@ struct FlashFwd {
   static constexpr int V_BOX = 32 * 32 * 4;       // MN-major box: 32 head-dim values x 32 keys
   static constexpr int V_SLAB = SLABS * V_BOX;    // 32 keys
   static constexpr int V_HI = 2 * V_SLAB;         // 64 keys
-  static constexpr int STAGE = K_HI + 2 * V_HI;  // K (rounded) | V hi | V lo
+  static constexpr int STAGE = 2 * K_HI + 2 * V_HI;  // K hi | K lo | V hi | V lo
   static constexpr int STAGES = 3;
   static constexpr int SMEM = STAGES * STAGE + 1024 + 512;
-  static constexpr uint32_t C_Q = 0, C_S = HD, C_PLO = HD + 2 * KB, C_O = HD + 4 * KB;
+  static constexpr uint32_t C_Q = 0, C_S = 2 * HD, C_PLO = 2 * HD + 2 * KB, C_O = 2 * HD + 4 * KB;
   static_assert(C_O + HD <= kFlashCols, "flash forward: TMEM columns");
 };
 
@@ -203,7 +178,7 @@ __global__ void __launch_bounds__(320, 1)
         mbar_arrive_expect_tx(&k_full[s], S::K_HI);
         for (int sl = 0; sl < S::SLABS; sl++) tma_load_4d(sk + sl * S::K_SLAB, &tmK, 32 * sl, j * KB, h, b, &k_full[s]);
         if (j >= ST && !mbar_wait(&v_empty[s], ((j / ST) - 1) & 1, flags, 302)) break;
-        const uint32_t sv = sk + S::K_HI;
+        const uint32_t sv = sk + 2 * S::K_HI;
         mbar_arrive_expect_tx(&v_full[s], S::V_HI);
         for (int hf = 0; hf < 2; hf++)
           for (int sl = 0; sl < S::SLABS; sl++)
@@ -221,7 +196,7 @@ __global__ void __launch_bounds__(320, 1)
         if (!mbar_wait(&p_ready[c & 1], (c >> 1) & 1, flags, 304) || !mbar_wait(&v_conv[s], (c / ST) & 1, flags, 305))
           return false;
         tc_fence_after();
-        const uint32_t sv = smem_u32(smem + s * S::STAGE + S::K_HI);
+        const uint32_t sv = smem_u32(smem + s * S::STAGE + 2 * S::K_HI);
         const uint64_t lov = (uint64_t)(S::V_HI >> 4);
         const uint32_t a_hi = tmem + S::C_S + (c & 1) * KB, a_lo = tmem + S::C_PLO + (c & 1) * KB;
 #pragma unroll
@@ -248,11 +223,14 @@ __global__ void __launch_bounds__(320, 1)
         }
         tc_fence_after();
         const uint32_t sk = smem_u32(smem + s * S::STAGE);
+        const uint64_t lok = (uint64_t)(S::K_HI >> 4);
         const uint32_t d = tmem + S::C_S + (j & 1) * KB;
 #pragma unroll
         for (int kk = 0; kk < HD / 8; kk++) {
           const uint64_t db = smem_desc(sk + (kk >> 2) * S::K_SLAB + (kk & 3) * 32, 16, 1024, kLayoutSW128);
-          mma_tf32_ts(d, tmem + S::C_Q + 8 * kk, db, idesc_s, kk > 0 ? 1u : 0u);
+          mma_tf32_ts(d, tmem + S::C_Q + HD + 8 * kk, db, idesc_s, kk > 0 ? 1u : 0u);
+          mma_tf32_ts(d, tmem + S::C_Q + 8 * kk, db + lok, idesc_s, 1u);
+          mma_tf32_ts(d, tmem + S::C_Q + 8 * kk, db, idesc_s, 1u);
         }
         mma_commit(&s_full[j & 1]);
         mma_commit(&k_empty[s]);
@@ -267,12 +245,12 @@ __global__ void __launch_bounds__(320, 1)
       const int s = j % ST;
       uint8_t* st = smem + s * S::STAGE;
       if (!mbar_wait(&k_full[s], (j / ST) & 1, flags, 308)) break;
-      round_inplace(st, S::K_HI, ct);
+      split_lo(st, S::K_HI, S::K_HI, ct);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&k_conv[s]);
       if (!mbar_wait(&v_full[s], (j / ST) & 1, flags, 309)) break;
-      split_lo(st + S::K_HI, S::V_HI, S::V_HI, ct);
+      split_lo(st + 2 * S::K_HI, S::V_HI, S::V_HI, ct);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&v_conv[s]);
@@ -283,14 +261,14 @@ __global__ void __launch_bounds__(320, 1)
     const int row = qd * 32 + lane, i = q0 + row;
     const int n = min(i + 1, T);  // keys this row sees
     const uint32_t lrow = (uint32_t)(qd * 32) << 16;
-    // Q row -> TMEM, rounded to tf32; rows past T are zero
+    // Q row -> TMEM (hi | lo); rows past T are zero
     {
       const float* src = q.ptr + (long)b * q.stride_hi + (long)h * q.stride + (long)(i < T ? i : 0) * q.ld;
 #pragma unroll 1
       for (int c = 0; c < HD; c += 32) {
         float v[32];
         ld_row32(src + c, i < T, v);
-        tmem_st_rn(tmem + lrow + S::C_Q + c, v);
+        tmem_st_split(tmem + lrow + S::C_Q + c, tmem + lrow + S::C_Q + HD + c, v);
       }
       tc_fence_before();
       __syncwarp();
@@ -387,11 +365,11 @@ __global__ void __launch_bounds__(320, 1)
 //   warp 0      producer: per 32-key block K (K-major: B of S = Q K^T), V (K-major: B of
 //               dP = dO V^T) and K again MN-major (B of dQ += dS K); four-stage ring
 //   warp 1      MMA issuer: S_j and dP_j into buffer j & 1, then dQ += dS_{j-1} K_{j-1}
-//   warps 2..5  converters: every stage rounded to tf32 in place (all three products are one-pass)
-//   warps 6..9  row warps: Q and dO (rounded) into TMEM, D = rowsum(dO * O) (also written out
-//               for the dK / dV kernel), P = exp(scale s - L), dS = P (dP - D) scale written
-//               (rounded) over S, and at the end dQ (rotated back by -theta for RoPE) into dqkv
-// TMEM columns: Q, dO, S / dS 2 x 32, dP 2 x 32, dQ.
+//   warps 2..5  lo-part converters
+//   warps 6..9  row warps: Q and dO into TMEM, D = rowsum(dO * O) (also written out for the
+//               dK / dV kernel), P = exp(scale s - L), dS = P (dP - D) scale written over S,
+//               and at the end dQ (rotated back by -theta for RoPE) into dqkv
+// TMEM columns: Q hi | lo, dO hi | lo, S / dS-hi 2 x 32, dP 2 x 32, dS-lo 2 x 32, dQ.
 template <int HD>
 struct FlashDq {
   static constexpr int KB = 32;
@@ -400,11 +378,12 @@ struct FlashDq {
   static constexpr int K_HI = SLABS * K_SLAB;
   static constexpr int MN_BOX = 32 * 32 * 4;   // 32 head-dim values x 32 keys, MN-major
   static constexpr int KM_HI = SLABS * MN_BOX;
-  static constexpr int HI = 2 * K_HI + KM_HI;  // K | V | K (MN-major), all rounded in place
-  static constexpr int STAGE = HI;
-  static constexpr int STAGES = 6;
+  static constexpr int HI = 2 * K_HI + KM_HI;  // K | V | K (MN-major)
+  static constexpr int STAGE = 2 * HI;
+  static constexpr int STAGES = 4;
   static constexpr int SMEM = STAGES * STAGE + 1024 + 512;
-  static constexpr uint32_t C_Q = 0, C_DO = HD, C_S = 2 * HD, C_DP = 2 * HD + 2 * KB, C_DQ = 2 * HD + 4 * KB;
+  static constexpr uint32_t C_Q = 0, C_DO = 2 * HD, C_S = 4 * HD, C_DP = 4 * HD + 2 * KB, C_DSLO = 4 * HD + 4 * KB,
+                            C_DQ = 4 * HD + 6 * KB;
   static_assert(C_DQ + HD <= kFlashCols, "flash dQ: TMEM columns");
 };
 
@@ -419,15 +398,15 @@ __global__ void __launch_bounds__(320, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + ST * S::STAGE);
-  uint64_t* full = bars;                 // [ST]
-  uint64_t* conv = bars + ST;            // [ST]
-  uint64_t* empty = bars + 2 * ST;       // [ST]
-  uint64_t* sd_full = bars + 3 * ST;     // [2] S and dP of a block ready
-  uint64_t* ds_ready = bars + 3 * ST + 2;   // [2] dS written
-  uint64_t* dq_done = bars + 3 * ST + 4;    // [2] dQ product of a block ran
-  uint64_t* qd_ready = bars + 3 * ST + 6;
-  uint64_t* dq_full = bars + 3 * ST + 7;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * ST + 8);
+  uint64_t* full = bars;            // [ST]
+  uint64_t* conv = bars + 4;        // [ST]
+  uint64_t* empty = bars + 8;       // [ST]
+  uint64_t* sd_full = bars + 12;    // [2] S and dP of a block ready
+  uint64_t* ds_ready = bars + 14;   // [2] dS written
+  uint64_t* dq_done = bars + 16;    // [2] dQ product of a block ran
+  uint64_t* qd_ready = bars + 18;
+  uint64_t* dq_full = bars + 19;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
@@ -476,16 +455,19 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_tf32(KB, false);
       constexpr uint32_t idesc_q = idesc_tf32(HD, true);
+      constexpr uint64_t lo = (uint64_t)(S::HI >> 4);
       bool ok = mbar_wait(qd_ready, 0, flags, 322);
       auto issue_dq = [&](int c) -> bool {
         if (!mbar_wait(&ds_ready[c & 1], (c >> 1) & 1, flags, 323)) return false;
         tc_fence_after();
         const uint32_t skm = smem_u32(smem + (c % ST) * S::STAGE + 2 * S::K_HI);
-        const uint32_t a = tmem + S::C_S + (c & 1) * KB;
+        const uint32_t a_hi = tmem + S::C_S + (c & 1) * KB, a_lo = tmem + S::C_DSLO + (c & 1) * KB;
 #pragma unroll
         for (int kk = 0; kk < KB / 8; kk++) {
           const uint64_t db = smem_desc(skm + kk * 1024, S::MN_BOX, 512, kLayoutSW128Atom32);
-          mma_tf32_ts(tmem + S::C_DQ, a + 8 * kk, db, idesc_q, (c > 0 || kk > 0) ? 1u : 0u);
+          mma_tf32_ts(tmem + S::C_DQ, a_lo + 8 * kk, db, idesc_q, (c > 0 || kk > 0) ? 1u : 0u);
+          mma_tf32_ts(tmem + S::C_DQ, a_hi + 8 * kk, db + lo, idesc_q, 1u);
+          mma_tf32_ts(tmem + S::C_DQ, a_hi + 8 * kk, db, idesc_q, 1u);
         }
         mma_commit(&dq_done[c & 1]);
         mma_commit(&empty[c % ST]);
@@ -509,8 +491,12 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t off = (kk >> 2) * S::K_SLAB + (kk & 3) * 32;
           const uint64_t dk = smem_desc(sk + off, 16, 1024, kLayoutSW128);
           const uint64_t dv = smem_desc(sv + off, 16, 1024, kLayoutSW128);
-          mma_tf32_ts(ds, tmem + S::C_Q + 8 * kk, dk, idesc_s, kk > 0 ? 1u : 0u);
-          mma_tf32_ts(dp, tmem + S::C_DO + 8 * kk, dv, idesc_s, kk > 0 ? 1u : 0u);
+          mma_tf32_ts(ds, tmem + S::C_Q + HD + 8 * kk, dk, idesc_s, kk > 0 ? 1u : 0u);
+          mma_tf32_ts(ds, tmem + S::C_Q + 8 * kk, dk + lo, idesc_s, 1u);
+          mma_tf32_ts(ds, tmem + S::C_Q + 8 * kk, dk, idesc_s, 1u);
+          mma_tf32_ts(dp, tmem + S::C_DO + HD + 8 * kk, dv, idesc_s, kk > 0 ? 1u : 0u);
+          mma_tf32_ts(dp, tmem + S::C_DO + 8 * kk, dv + lo, idesc_s, 1u);
+          mma_tf32_ts(dp, tmem + S::C_DO + 8 * kk, dv, idesc_s, 1u);
         }
         mma_commit(&sd_full[j & 1]);
         if (j >= 1 && !issue_dq(j - 1)) ok = false;
@@ -522,7 +508,7 @@ __global__ void __launch_bounds__(320, 1)
     for (int j = 0; j < nkb; j++) {
       const int s = j % ST;
       if (!mbar_wait(&full[s], (j / ST) & 1, flags, 326)) break;
-      round_inplace(smem + s * S::STAGE, S::HI, ct);
+      split_lo(smem + s * S::STAGE, S::HI, S::HI, ct);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&conv[s]);
@@ -543,12 +529,12 @@ __global__ void __launch_bounds__(320, 1)
       for (int c = 0; c < HD; c += 32) {
         float v[32], w[32];
         ld_row32(qs + c, in, v);
-        tmem_st_rn(tmem + lrow + S::C_Q + c, v);
+        tmem_st_split(tmem + lrow + S::C_Q + c, tmem + lrow + S::C_Q + HD + c, v);
         ld_row32(gs + c, in, v);
         ld_row32(os + c, in, w);
 #pragma unroll
         for (int e = 0; e < 32; e++) Drow += v[e] * w[e];
-        tmem_st_rn(tmem + lrow + S::C_DO + c, v);
+        tmem_st_split(tmem + lrow + S::C_DO + c, tmem + lrow + S::C_DO + HD + c, v);
       }
       tc_fence_before();
       __syncwarp();
@@ -573,7 +559,7 @@ __global__ void __launch_bounds__(320, 1)
         const float p = k0 + c < n ? __expf(sv[c] * scale - L) : 0.f;
         sv[c] = p * (gv[c] - Drow) * scale;
       }
-      tmem_st_rn(cs, sv);
+      tmem_st_split(cs, tmem + lrow + S::C_DSLO + (j & 1) * KB, sv);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ds_ready[j & 1]);
@@ -617,12 +603,12 @@ __global__ void __launch_bounds__(320, 1)
 //               two-stage ring
 //   warp 1      MMA issuer: S^T_i and dP^T_i into buffer i & 1, then dV += P^T_{i-1} dO_{i-1}
 //               and dK += dS^T_{i-1} Q_{i-1}
-//   warps 2..5  converters: the K tile and the Q / dO K-major tiles and the MN-major Q tile
-//               rounded in place, lo parts of the MN-major dO tile (B of the 3xTF32 dV product)
-//   warps 6..9  row warps (row = key): V (rounded) into TMEM; P^T = exp(scale s - L_q) (hi and
-//               lo) and dS^T = P^T (dP^T - D_q) scale (rounded) written over S^T and dP^T; at the
-//               end dV and dK (rotated back for RoPE) into dqkv
-// TMEM columns: V, S^T / P^T-hi 2 x 32, dP^T / dS^T 2 x 32, P^T-lo 2 x 32, dV, dK.
+//   warps 2..5  lo-part converters (the K tile, then each stage)
+//   warps 6..9  row warps (row = key): V into TMEM; P^T = exp(scale s - L_q) and
+//               dS^T = P^T (dP^T - D_q) scale written over S^T and dP^T; at the end dV and dK
+//               (rotated back for RoPE) into dqkv
+// TMEM columns: V hi | lo, S^T / P^T-hi 2 x 32, dP^T / dS^T-hi 2 x 32, P^T-lo 2 x 32,
+// dS^T-lo 2 x 32, dV, dK.
 template <int HD>
 struct FlashDkv {
   static constexpr int QB = 32;
@@ -634,12 +620,12 @@ struct FlashDkv {
   static constexpr int MN_BOX = 32 * 32 * 4;
   static constexpr int QM_HI = SLABS * MN_BOX;
   static constexpr int HI = 2 * QK_HI + 2 * QM_HI;  // Q | dO (K-major) | Q | dO (MN-major)
-  static constexpr int STAGE = HI + QM_HI;          // + lo part of the MN-major dO tile
-  static constexpr int STAGES = 3;
-  static constexpr int KREG = K_HI;
+  static constexpr int STAGE = 2 * HI;
+  static constexpr int STAGES = 2;
+  static constexpr int KREG = 2 * K_HI;
   static constexpr int SMEM = KREG + STAGES * STAGE + 1024 + 512;
-  static constexpr uint32_t C_V = 0, C_S = HD, C_DP = HD + 2 * QB, C_PLO = HD + 4 * QB, C_DV = HD + 6 * QB,
-                            C_DK = 2 * HD + 6 * QB;
+  static constexpr uint32_t C_V = 0, C_S = 2 * HD, C_DP = 2 * HD + 2 * QB, C_PLO = 2 * HD + 4 * QB,
+                            C_DSLO = 2 * HD + 6 * QB, C_DV = 2 * HD + 8 * QB, C_DK = 3 * HD + 8 * QB;
   static_assert(C_DK + HD <= kFlashCols, "flash dK/dV: TMEM columns");
 };
 
@@ -656,17 +642,17 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem + S::KREG;
   uint64_t* bars = reinterpret_cast<uint64_t*>(stages + ST * S::STAGE);
-  uint64_t* full = bars;                  // [ST]
-  uint64_t* conv = bars + ST;             // [ST]
-  uint64_t* empty = bars + 2 * ST;        // [ST]
-  uint64_t* sd_full = bars + 3 * ST;      // [2]
-  uint64_t* p_ready = bars + 3 * ST + 2;  // [2]
-  uint64_t* kv_done = bars + 3 * ST + 4;  // [2]
-  uint64_t* k_full = bars + 3 * ST + 6;
-  uint64_t* k_conv = bars + 3 * ST + 7;
-  uint64_t* v_ready = bars + 3 * ST + 8;
-  uint64_t* acc_full = bars + 3 * ST + 9;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * ST + 10);
+  uint64_t* full = bars;           // [ST]
+  uint64_t* conv = bars + 2;       // [ST]
+  uint64_t* empty = bars + 4;      // [ST]
+  uint64_t* sd_full = bars + 6;    // [2]
+  uint64_t* p_ready = bars + 8;    // [2]
+  uint64_t* kv_done = bars + 10;   // [2]
+  uint64_t* k_full = bars + 12;
+  uint64_t* k_conv = bars + 13;
+  uint64_t* v_ready = bars + 14;
+  uint64_t* acc_full = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.x, b = bh / H, h = bh % H, E = H * HD;
@@ -720,7 +706,7 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_tf32(QB, false);
       constexpr uint32_t idesc_a = idesc_tf32(HD, true);
-      constexpr uint64_t lo = (uint64_t)(S::QM_HI >> 4);  // the MN-major dO tile's lo part follows it
+      constexpr uint64_t lo = (uint64_t)(S::HI >> 4), lok = (uint64_t)(S::K_HI >> 4);
       bool ok = mbar_wait(k_conv, 0, flags, 342) && mbar_wait(v_ready, 0, flags, 343);
       auto issue_kv = [&](int c) -> bool {
         if (!mbar_wait(&p_ready[c & 1], (c >> 1) & 1, flags, 344)) return false;
@@ -728,7 +714,7 @@ __global__ void __launch_bounds__(320, 1)
         const uint32_t base = smem_u32(stages + (c % ST) * S::STAGE);
         const uint32_t sqm = base + 2 * S::QK_HI, som = sqm + S::QM_HI;
         const uint32_t p_hi = tmem + S::C_S + (c & 1) * QB, p_lo = tmem + S::C_PLO + (c & 1) * QB;
-        const uint32_t g = tmem + S::C_DP + (c & 1) * QB;
+        const uint32_t g_hi = tmem + S::C_DP + (c & 1) * QB, g_lo = tmem + S::C_DSLO + (c & 1) * QB;
 #pragma unroll
         for (int kk = 0; kk < QB / 8; kk++) {
           const uint64_t dO = smem_desc(som + kk * 1024, S::MN_BOX, 512, kLayoutSW128Atom32);
@@ -737,7 +723,9 @@ __global__ void __launch_bounds__(320, 1)
           mma_tf32_ts(tmem + S::C_DV, p_lo + 8 * kk, dO, idesc_a, first);
           mma_tf32_ts(tmem + S::C_DV, p_hi + 8 * kk, dO + lo, idesc_a, 1u);
           mma_tf32_ts(tmem + S::C_DV, p_hi + 8 * kk, dO, idesc_a, 1u);
-          mma_tf32_ts(tmem + S::C_DK, g + 8 * kk, dQ, idesc_a, first);
+          mma_tf32_ts(tmem + S::C_DK, g_lo + 8 * kk, dQ, idesc_a, first);
+          mma_tf32_ts(tmem + S::C_DK, g_hi + 8 * kk, dQ + lo, idesc_a, 1u);
+          mma_tf32_ts(tmem + S::C_DK, g_hi + 8 * kk, dQ, idesc_a, 1u);
         }
         mma_commit(&kv_done[c & 1]);
         mma_commit(&empty[c % ST]);
@@ -763,8 +751,12 @@ __global__ void __launch_bounds__(320, 1)
           const uint64_t dq = smem_desc(base + (kk >> 2) * S::QK_SLAB + (kk & 3) * 32, 16, 1024, kLayoutSW128);
           const uint64_t dd = smem_desc(base + S::QK_HI + (kk >> 2) * S::QK_SLAB + (kk & 3) * 32, 16, 1024,
                                         kLayoutSW128);
-          mma_tf32(ds, da, dq, idesc_s, kk > 0 ? 1u : 0u);
-          mma_tf32_ts(dp, tmem + S::C_V + 8 * kk, dd, idesc_s, kk > 0 ? 1u : 0u);
+          mma_tf32(ds, da + lok, dq, idesc_s, kk > 0 ? 1u : 0u);
+          mma_tf32(ds, da, dq + lo, idesc_s, 1u);
+          mma_tf32(ds, da, dq, idesc_s, 1u);
+          mma_tf32_ts(dp, tmem + S::C_V + HD + 8 * kk, dd, idesc_s, kk > 0 ? 1u : 0u);
+          mma_tf32_ts(dp, tmem + S::C_V + 8 * kk, dd + lo, idesc_s, 1u);
+          mma_tf32_ts(dp, tmem + S::C_V + 8 * kk, dd, idesc_s, 1u);
         }
         mma_commit(&sd_full[i & 1]);
         if (i >= 1 && !issue_kv(i - 1)) ok = false;
@@ -774,16 +766,14 @@ __global__ void __launch_bounds__(320, 1)
   } else if (warp < 6) {
     const int ct = threadIdx.x - 64;
     if (mbar_wait(k_full, 0, flags, 347)) {
-      round_inplace(smem, S::K_HI, ct);
+      split_lo(smem, S::K_HI, S::K_HI, ct);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(k_conv);
       for (int i = 0; i < nqb; i++) {
         const int s = i % ST;
         if (!mbar_wait(&full[s], (i / ST) & 1, flags, 348)) break;
-        uint8_t* st = stages + s * S::STAGE;
-        round_inplace(st, 2 * S::QK_HI + S::QM_HI, ct);                      // Q, dO (K-major), Q (MN)
-        split_lo(st + 2 * S::QK_HI + S::QM_HI, S::QM_HI, S::QM_HI, ct);     // dO (MN): lo follows it
+        split_lo(stages + s * S::STAGE, S::HI, S::HI, ct);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) mbar_arrive(&conv[s]);
@@ -800,7 +790,7 @@ __global__ void __launch_bounds__(320, 1)
       for (int c = 0; c < HD; c += 32) {
         float x[32];
         ld_row32(vs + c, in, x);
-        tmem_st_rn(tmem + lrow + S::C_V + c, x);
+        tmem_st_split(tmem + lrow + S::C_V + c, tmem + lrow + S::C_V + HD + c, x);
       }
       tc_fence_before();
       __syncwarp();
@@ -831,7 +821,7 @@ __global__ void __launch_bounds__(320, 1)
         gv[c] = p * (gv[c] - Dqv) * scale;
       }
       tmem_st_split(cs, tmem + lrow + S::C_PLO + (i & 1) * QB, sv);
-      tmem_st_rn(cd, gv);
+      tmem_st_split(cd, tmem + lrow + S::C_DSLO + (i & 1) * QB, gv);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_ready[i & 1]);

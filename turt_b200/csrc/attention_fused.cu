@@ -5,11 +5,9 @@
 // place, O = P V reading P back.  With T <= 256 a tile of 128 query rows meets at most 256 keys,
 // so its whole score block fits the tensor memory (256 fp32 columns of the 512): this kernel
 // computes S there, takes the row softmax in registers, writes P once (the backward pass keeps
-// using it) and multiplies P by V from shared memory, 64 keys at a time.  Arithmetic: fp32
-// accumulation in TMEM; the products with a probability operand (O = P v here, dV = P^T dO in
-// the backward) are error-compensated 3xTF32, the others (S = q k^T, dP = dO v^T, dQ = dS k,
-// dK = dS^T q) one tf32 pass on operands rounded to nearest (see rn_tf32); softmax of
-// scale * s minus the row maximum, P = exp(.) / sum, zeros right of the diagonal.
+// using it) and multiplies P by V from shared memory, 64 keys at a time.  The arithmetic is the
+// unfused path's: 3xTF32 products with fp32 accumulation, softmax of scale * s minus the row
+// maximum, P = exp(.) / sum, zeros right of the diagonal.
 //
 // One CTA per (query tile of 128 rows, batch entry, head); 448 threads:
 //   warp 0       TMA producer: Q and K tiles, then V in 64-key chunks (two buffers)
@@ -17,8 +15,8 @@
 //   warps 2..9   softmax and output: warp w owns TMEM lanes (query rows) 32*(w%4) .. +31 and
 //                the 32-key column blocks of parity (w - 2) / 4 (two warps per row, so the
 //                exponentials of a 128-row tile run on 256 threads)
-//   warps 10..13 converters: Q and K rounded to tf32 in place, lo parts of each V chunk
-// Shared memory holds Q|K (the lo halves of the region unused) during the score product, then the same bytes hold two
+//   warps 10..13 lo-part converters for Q, K and each V chunk (3xTF32 splits)
+// Shared memory holds Q|K (hi and lo) during the score product, then the same bytes hold two
 // P chunks and two V chunks (hi and lo): 192 KB for a head dim of 64.
 #include "attention.cuh"
 #include "gemm.cuh"
@@ -68,22 +66,6 @@ __device__ __forceinline__ void lo_split(uint8_t* hi_base, int bytes, int lo_off
     r.w = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
     lo[e] = r;
   }
-}
-
-// Round to the nearest tf32 value in place (ties away from zero): the products whose operands
-// carry no probability -- S = q k^T, dP = dO v^T, dQ = dS k, dK = dS^T q -- run as one tf32 MMA on
-// rounded operands (unbiased, error ~2^-12 per operand), while the products with a probability
-// operand -- O = P v, dV = P^T dO -- keep the 3xTF32 split (rounding P alone leaves a 1e-2 error
-// in the gradients; the split keeps ~3e-5).  Measured on the oracle at the headline shape: max
-// gradient error 2e-4 against the 2e-3 bar.
-__device__ __forceinline__ float rn_tf32(float x) {
-  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
-}
-__device__ __forceinline__ float4 rn4(float4 v) { return make_float4(rn_tf32(v.x), rn_tf32(v.y), rn_tf32(v.z), rn_tf32(v.w)); }
-__device__ __forceinline__ void round_inplace(uint8_t* base, int bytes, int ct) {
-  float4* p = reinterpret_cast<float4*>(base);
-#pragma unroll 4
-  for (int e = ct; e < bytes / 16; e += 128) p[e] = rn4(p[e]);
 }
 
 __device__ __forceinline__ float4 lo4(float4 v) {
@@ -198,11 +180,14 @@ __global__ void __launch_bounds__(kFThreads, 1)
         const uint32_t idesc_s = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(nkr >> 3) << 17) |
                                  ((uint32_t)(kFQ >> 4) << 24);
         const uint32_t sq = smem_u32(smem + S::Q_HI), sk = smem_u32(smem + S::K_HI);
+        const uint64_t loq = (uint64_t)(S::Q_BYTES >> 4), lok = (uint64_t)(S::K_BYTES >> 4);
 #pragma unroll
         for (int kk = 0; kk < HD / 8; kk++) {
           const uint64_t da = smem_desc(sq + (kk >> 2) * S::Q_SLAB + (kk & 3) * 32, 16, 1024, kLayoutSW128);
           const uint64_t db = smem_desc(sk + (kk >> 2) * S::K_SLAB + (kk & 3) * 32, 16, 1024, kLayoutSW128);
-          mma_tf32(tmem, da, db, idesc_s, kk > 0 ? 1u : 0u);
+          mma_tf32(tmem, da + loq, db, idesc_s, kk > 0 ? 1u : 0u);
+          mma_tf32(tmem, da, db + lok, idesc_s, 1u);
+          mma_tf32(tmem, da, db, idesc_s, 1u);
         }
         mma_commit(s_full);
       }
@@ -236,8 +221,8 @@ __global__ void __launch_bounds__(kFThreads, 1)
     const int ct = threadIdx.x - 320;
     bool ok = mbar_wait(qk_full, 0, flags, 136);
     if (ok) {
-      round_inplace(smem + S::Q_HI, S::Q_BYTES, ct);
-      for (int sl = 0; sl < S::SLABS; sl++) round_inplace(smem + S::K_HI + sl * S::K_SLAB, nbox * 16384, ct);
+      lo_split(smem + S::Q_HI, S::Q_BYTES, S::Q_BYTES, ct);
+      for (int sl = 0; sl < S::SLABS; sl++) lo_split(smem + S::K_HI + sl * S::K_SLAB, nbox * 16384, S::K_BYTES, ct);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(qk_conv);
@@ -496,29 +481,37 @@ __global__ void __launch_bounds__(kFThreads, 1)
         const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(nkr >> 3) << 17) |
                                ((uint32_t)(kFQ >> 4) << 24);
         const uint32_t sq = smem_u32(smem + S::Q_HI), sk = smem_u32(smem + S::K_HI);
+        const uint64_t loq = (uint64_t)(S::Q_BYTES >> 4), lok = (uint64_t)(S::K_BYTES >> 4);
 #pragma unroll
         for (int kk = 0; kk < HD / 8; kk++) {
           const uint64_t da = smem_desc(sq + (kk >> 2) * S::Q_SLAB + (kk & 3) * 32, 16, 1024, kLayoutSW128);
           const uint64_t db = smem_desc(sk + (kk >> 2) * S::K_SLAB + (kk & 3) * 32, 16, 1024, kLayoutSW128);
-          mma_tf32(tmem, da, db, idesc, kk > 0 ? 1u : 0u);
+          mma_tf32(tmem, da + loq, db, idesc, kk > 0 ? 1u : 0u);
+          mma_tf32(tmem, da, db + lok, idesc, 1u);
+          mma_tf32(tmem, da, db, idesc, 1u);
         }
         mma_commit(s_full);
       }
       constexpr uint32_t idesc_q = (1u << 4) | (2u << 7) | (2u << 10) | (1u << 16) | ((uint32_t)(HD >> 3) << 17) |
                                    ((uint32_t)(kFQ >> 4) << 24);
+      const uint64_t lok = (uint64_t)(S::V_BYTES >> 4);
       for (int c = 0; c < nch && ok; c++) {
         if (!mbar_wait(ds_ready, c & 1, flags, 158) || !mbar_wait(k_conv, c & 1, flags, 159)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        // dS chunk c (rounded to tf32) in slabs 2c, 2c+1 of the P tile, k chunk rounded in place
+        // dS chunk c: hi in slabs 2c, 2c+1 of the P tile, lo in the DL buffer
         const uint32_t sd = smem_u32(smem) + 2 * c * S::P_SLAB, sk = smem_u32(smem + D::KC);
+        const uint64_t lod = (uint64_t)((D::DL - 2 * c * S::P_SLAB) >> 4);
 #pragma unroll
         for (int kk = 0; kk < 8; kk++) {
           const uint64_t da = smem_desc(sd + (kk >> 2) * S::P_SLAB + (kk & 3) * 32, 16, 1024, kLayoutSW128);
           const uint64_t db = smem_desc(sk + (kk >> 2) * S::V_SLAB + (kk & 3) * 1024, S::V_BOX, 512, kLayoutSW128Atom32);
-          mma_tf32(tmem + kFTmemO, da, db, idesc_q, (c > 0 || kk > 0) ? 1u : 0u);
+          const uint32_t first = (c > 0 || kk > 0) ? 1u : 0u;
+          mma_tf32(tmem + kFTmemO, da + lod, db, idesc_q, first);
+          mma_tf32(tmem + kFTmemO, da, db + lok, idesc_q, 1u);
+          mma_tf32(tmem + kFTmemO, da, db, idesc_q, 1u);
         }
         mma_commit(dsl_free);
         mma_commit(k_empty);
@@ -530,15 +523,15 @@ __global__ void __launch_bounds__(kFThreads, 1)
     const int ct = threadIdx.x - 320;
     bool ok = mbar_wait(qk_full, 0, flags, 153);
     if (ok) {
-      round_inplace(smem + S::Q_HI, S::Q_BYTES, ct);
-      for (int sl = 0; sl < S::SLABS; sl++) round_inplace(smem + S::K_HI + sl * S::K_SLAB, nbox * 16384, ct);
+      lo_split(smem + S::Q_HI, S::Q_BYTES, S::Q_BYTES, ct);
+      for (int sl = 0; sl < S::SLABS; sl++) lo_split(smem + S::K_HI + sl * S::K_SLAB, nbox * 16384, S::K_BYTES, ct);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(qk_conv);
     }
     for (int c = 0; c < nch && ok; c++) {
       if (!mbar_wait(k_full, c & 1, flags, 160)) break;
-      round_inplace(smem + D::KC, S::V_BYTES, ct);
+      lo_split(smem + D::KC, S::V_BYTES, S::V_BYTES, ct);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(k_conv);
@@ -574,9 +567,15 @@ __global__ void __launch_bounds__(kFThreads, 1)
       softmax_sync();
       Dsum = red[row] + red[128 + row];
       for (int c = 0; c < nch; c++) {
-        // chunk c's dS goes over its own P slabs: nothing waits for the dQ products of earlier chunks
+        if (c >= 1) {  // the dS lo buffer is free once the dQ products of chunk c - 1 ran
+          if (issuer) *sm_ok = mbar_wait(dsl_free, (c - 1) & 1, flags, 161) ? 1 : 0;
+          softmax_sync();
+          ok = *sm_ok != 0;
+          if (!ok) break;
+        }
         const int cc = 2 * c + half;
         uint8_t* prow = smem + cc * S::P_SLAB + row * 128;
+        uint8_t* lrow = smem + D::DL + half * S::P_SLAB + row * 128;
         if (cc * 32 <= warp_last) {  // warp-uniform
           float g[32];
           tmem_ld32(trow + cc * 32, g);
@@ -590,11 +589,15 @@ __global__ void __launch_bounds__(kFThreads, 1)
                                          j + 1 < n ? p.y * (g[4 * k + 1] - Dsum) * scale : 0.f,
                                          j + 2 < n ? p.z * (g[4 * k + 2] - Dsum) * scale : 0.f,
                                          j + 3 < n ? p.w * (g[4 * k + 3] - Dsum) * scale : 0.f);
-            *pp = rn4(x);  // the operand of dQ here and of dK (stored) in the next kernel
+            *pp = x;
+            *reinterpret_cast<float4*>(lrow + off) = lo4(x);
           }
         } else {
 #pragma unroll
-          for (int k = 0; k < 8; k++) *reinterpret_cast<float4*>(prow + 16 * k) = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int k = 0; k < 8; k++) {
+            *reinterpret_cast<float4*>(prow + 16 * k) = make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(lrow + 16 * k) = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         softmax_sync();
@@ -809,7 +812,9 @@ __global__ void __launch_bounds__(320, 1)
           mma_tf32(tmem, dp + lo, dO, idesc, first);
           mma_tf32(tmem, dp, dO + lo, idesc, 1u);
           mma_tf32(tmem, dp, dO, idesc, 1u);
-          mma_tf32(tmem + 128, ds, dq, idesc, first);  // dS^T arrives rounded, q is rounded in place
+          mma_tf32(tmem + 128, ds + lo, dq, idesc, first);
+          mma_tf32(tmem + 128, ds, dq + lo, idesc, 1u);
+          mma_tf32(tmem + 128, ds, dq, idesc, 1u);
         }
         mma_commit(&empty[s]);
       }
@@ -820,10 +825,7 @@ __global__ void __launch_bounds__(320, 1)
     for (int sl = 0; sl < nsl; sl++) {
       const int s = sl & 1;
       if (!mbar_wait(&full[s], (sl >> 1) & 1, flags, 173)) break;
-      uint8_t* st = smem + s * S::STAGE;  // P^T | dS^T | dO | q, lo parts HI further
-      lo_split(st, S::A_BYTES, S::HI, ct);
-      lo_split(st + 2 * S::A_BYTES, S::B_BYTES, S::HI, ct);
-      round_inplace(st + 2 * S::A_BYTES + S::B_BYTES, S::B_BYTES, ct);
+      lo_split(smem + s * S::STAGE, S::HI, S::HI, ct);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&conv[s]);

@@ -15,6 +15,7 @@
 #include <atomic>
 #include <map>
 #include <mutex>
+#include <vector>
 
 #include "gemm.cuh"
 #include "tcgen05.cuh"
@@ -500,6 +501,10 @@ __global__ void __launch_bounds__(GemmShape<BN, BK, X3, MINB>::THREADS, MINB)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
   // set-up done: from here on global memory is touched (PDL; no-ops under a plain launch)
   pdl_trigger();
   pdl_wait();
@@ -850,6 +855,10 @@ __global__ void __launch_bounds__(352, 1)
   cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any cross-CTA use
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
   pdl_trigger();
   pdl_wait();
   // shared::cluster addresses of the even CTA's relay targets
@@ -1404,6 +1413,7 @@ std::atomic<int> g_pair_override{-1};
 struct SplitWorkspace {
   float* ws = nullptr;
   size_t floats = 0;
+  std::vector<float*> retired;  // outgrown buffers, freed with the stream's workspace
 };
 std::mutex g_split_mu;
 std::map<std::pair<int, cudaStream_t>, SplitWorkspace> g_split_ws;
@@ -1420,8 +1430,9 @@ int split_workspace(cudaStream_t st, size_t floats, float** ws) {
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     TURT_CHECK_CUDA(cudaStreamIsCapturing(st, &cs));
     if (cs != cudaStreamCaptureStatusNone) return ERR_UNSUPPORTED;
-    TURT_CHECK_CUDA(cudaStreamSynchronize(st));  // the old buffer is no longer in use
-    if (w.ws) cudaFree(w.ws);
+    // The outgrown buffer is kept, not freed: cudaFree waits for the whole device (and its peers),
+    // which could stall behind a collective of the backward pass that waits for another device.
+    if (w.ws) w.retired.push_back(w.ws);
     w.ws = nullptr;
     w.floats = 0;
     const size_t nf = std::max(floats, (size_t)1 << 20);
@@ -1442,6 +1453,7 @@ void gemm_release_stream(cudaStream_t st) {
   if (it == g_split_ws.end()) return;
   cudaStreamSynchronize(st);
   if (it->second.ws) cudaFree(it->second.ws);
+  for (float* p : it->second.retired) cudaFree(p);
   g_split_ws.erase(it);
 }
 

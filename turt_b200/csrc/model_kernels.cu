@@ -50,19 +50,57 @@ template <int NJ>
 __global__ void __launch_bounds__(32 * kEmbedRowsPerBlock)
     k_embed_bwd_rows(const float* __restrict__ dx, const uint32_t* __restrict__ ids, float* __restrict__ dwte, int N,
                      int E, int V) {
+  constexpr int kList = 32;  // matching positions a warp collects before adding them
   __shared__ __align__(16) uint32_t sid[kIdTile];
+  __shared__ int plist[kEmbedRowsPerBlock][kList];
   pdl_trigger();
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t v = (uint32_t)(blockIdx.x * kEmbedRowsPerBlock + warp);
   const int E4 = E / 4;
+  int* pl = plist[warp];
   float4 acc[NJ];
   bool any = false;  // warp-uniform: every lane sees the same matches
+  int cnt = 0;       // warp-uniform
+  // Adds the collected rows in list (= position) order; their loads are issued four at a time.
+  auto flush = [&]() {
+    if (!cnt) return;
+    __syncwarp();
+    if (!any) {
+      const float4* w = reinterpret_cast<const float4*>(dwte + (size_t)v * E);
+#pragma unroll
+      for (int j = 0; j < NJ; j++)
+        if (lane + 32 * j < E4) acc[j] = w[lane + 32 * j];
+      any = true;
+    }
+    for (int k0 = 0; k0 < cnt; k0 += 4) {
+      float4 r[4][NJ];
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+        if (k0 + u < cnt) {
+          const float4* g = reinterpret_cast<const float4*>(dx + (size_t)pl[k0 + u] * E);
+#pragma unroll
+          for (int j = 0; j < NJ; j++)
+            if (lane + 32 * j < E4) r[u][j] = g[lane + 32 * j];
+        }
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+        if (k0 + u < cnt) {
+#pragma unroll
+          for (int j = 0; j < NJ; j++)
+            if (lane + 32 * j < E4) {
+              acc[j].x += r[u][j].x, acc[j].y += r[u][j].y, acc[j].z += r[u][j].z, acc[j].w += r[u][j].w;
+            }
+        }
+    }
+    cnt = 0;
+    __syncwarp();
+  };
   for (int base = 0; base < N; base += kIdTile) {
-    const int cnt = min(kIdTile, N - base);
-    const int padded = (cnt + 127) & ~127;
+    const int tile = min(kIdTile, N - base);
+    const int padded = (tile + 127) & ~127;
     __syncthreads();  // the previous tile has been scanned
-    for (int k = threadIdx.x; k < padded; k += blockDim.x) sid[k] = k < cnt ? ids[base + k] : 0xFFFFFFFFu;
+    for (int k = threadIdx.x; k < padded; k += blockDim.x) sid[k] = k < tile ? ids[base + k] : 0xFFFFFFFFu;
     __syncthreads();
     if (v >= (uint32_t)V) continue;
     const uint4* sid4 = reinterpret_cast<const uint4*>(sid);
@@ -77,24 +115,14 @@ __global__ void __launch_bounds__(32 * kEmbedRowsPerBlock)
         while (bits) {
           const int k = __ffs(bits) - 1;
           bits &= bits - 1;
-          const float4* g = reinterpret_cast<const float4*>(dx + (size_t)(base + 128 * c + 4 * src + k) * E);
-          if (!any) {
-            const float4* w = reinterpret_cast<const float4*>(dwte + (size_t)v * E);
-#pragma unroll
-            for (int j = 0; j < NJ; j++)
-              if (lane + 32 * j < E4) acc[j] = w[lane + 32 * j];
-            any = true;
-          }
-#pragma unroll
-          for (int j = 0; j < NJ; j++)
-            if (lane + 32 * j < E4) {
-              const float4 t = g[lane + 32 * j];
-              acc[j].x += t.x, acc[j].y += t.y, acc[j].z += t.z, acc[j].w += t.w;
-            }
+          if (cnt == kList) flush();
+          if (lane == 0) pl[cnt] = base + 128 * c + 4 * src + k;
+          cnt++;
         }
       }
     }
   }
+  flush();
   if (any) {
     float4* w = reinterpret_cast<float4*>(dwte + (size_t)v * E);
 #pragma unroll
@@ -119,6 +147,7 @@ __global__ void __launch_bounds__(256) k_pos_bwd(const float* __restrict__ dx, f
 #pragma unroll
   for (int j = 0; j < NJ; j++)
     if (lane + 32 * j < E4) acc[j] = w[lane + 32 * j];
+#pragma unroll 4
   for (int n = t; n < N; n += T) {
     const float4* g = reinterpret_cast<const float4*>(dx + (size_t)n * E);
 #pragma unroll
