@@ -402,7 +402,8 @@ def run_gpu(args, w, rank: int, world: int, local_rank: int) -> None:
         out = {
             "metric": "train tokens/sec (fwd+bwd+clip+AdamW)",
             "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if w.get("global_batch") else "weak", "vs_baseline": None,
             "dtype": "tf32x3" if args.precision == 3 else "tf32", "data": "synthetic",
             "config": {"workload": args.workload, "model": args.workload, "global_batch": global_seqs, "seq_len": T,
                        "parallelism": f"dp{world}", "micro_batch": micro, "attention": args.attention,
@@ -627,6 +628,8 @@ def run_gemm_table(args, rank: int) -> None:
     ctx = Context(0)
     ctx.set_stream(stream.cuda_stream)
     ctx.set_precision(args.precision)
+    bn, pair = (int(x) for x in args.force_tile.split(","))
+    check(lib().turt_gemm_set_tile(bn, pair))
     peaks = measured_peaks()
     tf32 = peaks["bf16_tflops"] / 2.0
     issue = 3 if args.precision == 3 else 1
@@ -669,7 +672,7 @@ def run_gemm_table(args, rank: int) -> None:
            "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms,
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
            "dtype": "tf32x3" if issue == 3 else "tf32", "data": "synthetic",
-           "config": {"workload": "gemm-table", "model": args.table_workload,
+           "config": {"workload": "gemm-table", "model": args.table_workload, "tile": args.force_tile,
                       "l2": "not flushed: back-to-back launches on the same operands, median per shape"},
            "shapes": rows,
            "roofline": {"bound": "tensor", "kernel": "all step GEMM shapes", "achieved": agg, "peak": tf32,
@@ -862,6 +865,8 @@ def main():
                     choices=sorted(WORKLOADS) + ["backward-ops", "gemm", "gemm-table", "decode"])
     ap.add_argument("--table-workload", default="gpt-6L-384d", choices=sorted(WORKLOADS),
                     help="model whose train-step GEMM shapes --workload gemm-table times")
+    ap.add_argument("--force-tile", default="0,-1",
+                    help="BN,PAIR for --workload gemm-table (turt_gemm_set_tile; 0,-1 = the planner's choice)")
     ap.add_argument("--gemm", default="8192,8192,384", help="M,N,K of the gemm workload")
     ap.add_argument("--precision", type=int, default=3, choices=[1, 3])
     ap.add_argument("--no-cpu-baseline", action="store_true")

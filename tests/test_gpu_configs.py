@@ -98,6 +98,15 @@ def test_modern_head_dim64_T1024(ctx, orc, attn, t):
     assert ge <= GRAD_TOL, (ge, name)
 
 
+@pytest.mark.parametrize("arch", ["modern", "gpt2"])
+def test_width_768(ctx, orc, arch):
+    """Rows of 768 (the 12-layer / 768-d workloads' width): the norm backwards run one row per
+    warp iteration with one block per SM, 12 heads of 64; 1 layer, b 4 x 64."""
+    le, ge, name, losses = _parity(ctx, orc, 512, 64, 1, 12, 768, arch, 4, 64)
+    assert le <= LOSS_TOL, losses
+    assert ge <= GRAD_TOL, (ge, name)
+
+
 @pytest.mark.parametrize("arch", ["modern", "gpt2", "modern-T1024"])
 def test_gradients_bit_identical_across_runs(ctx, orc, arch):
     """Two identical train steps give bit-identical losses and gradients: the embedding

@@ -55,9 +55,14 @@ def _dev(ctx, a):
     return p
 
 
-@pytest.mark.parametrize("rows,E", [(8192, 384), (1024, 384), (100, 32), (37, 768)])
+@pytest.mark.parametrize("rows,E", [(8192, 384), (1024, 384), (1000, 384), (100, 32), (37, 768), (8192, 768),
+                                    (2500, 640)])
 @pytest.mark.parametrize("with_res", [False, True])
 def test_rms_bwd(ctx, orc, rows, E, with_res):
+    """RMSNorm backward with the dgamma column sum finished in the same launch (per-group then
+    final sums, counters left zero).  Called twice: dgamma accumulates both calls, so a counter
+    that was not reset or a group summed twice would show.  1000 rows give a ragged last group;
+    E 640 / 768 use one row per warp iteration."""
     from turt_b200._lib import check, lib
     rng = np.random.default_rng(rows + E)
     x = rng.standard_normal((rows, E)).astype(np.float32)
@@ -72,12 +77,13 @@ def test_rms_bwd(ctx, orc, rows, E, with_res):
     bufs = [_dev(ctx, a) for a in (x, dy, gam, rstd, dg0)]
     dx = ctx.buffer(rows * E)
     dr = _dev(ctx, dres) if with_res else None
-    check(lib().turt_fused_rms_bwd(ctx.handle, bufs[0], bufs[1], bufs[2], bufs[3], dr, dx, bufs[4], rows, E))
+    for _ in range(2):
+        check(lib().turt_fused_rms_bwd(ctx.handle, bufs[0], bufs[1], bufs[2], bufs[3], dr, dx, bufs[4], rows, E))
     got_dx = ctx.download(dx, rows * E).reshape(rows, E)
     got_dg = ctx.download(bufs[4], E)
     assert _ok(got_dx, ref_dx)
-    abs_terms = np.abs(dy.astype(np.float64) * x * rstd[:, None]).sum(axis=0) + np.abs(dg0)
-    assert _ok_sum(got_dg, ref_dg + dg0, abs_terms)
+    abs_terms = 2 * np.abs(dy.astype(np.float64) * x * rstd[:, None]).sum(axis=0) + np.abs(dg0)
+    assert _ok_sum(got_dg, 2 * ref_dg.astype(np.float64) + dg0, abs_terms)
 
 
 @pytest.mark.parametrize("n", [8192 * 1024, 8192 * 1024 // 64, 1003])

@@ -413,11 +413,8 @@ __global__ void __launch_bounds__(256) k_attn_bwd_q(const float* __restrict__ qk
 template <int HD>
 int launch_fwd(cudaStream_t st, const float* qkv, const float2* cs, float* out, float* lse, const AttnShape& s) {
   const int smem = (2 * HD * (64 + PAD) + 64 * (HD + PAD) + 64 * (64 + PAD)) * 4;
-  static bool cfg = false;
-  if (!cfg) {
-    TURT_CHECK_CUDA(cudaFuncSetAttribute(k_attn_fwd<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    cfg = true;
-  }
+  static std::atomic<uint64_t> cfg{0};
+  RC(smem_attr_per_device(cfg, k_attn_fwd<HD>, smem));
   dim3 grid(ceil_div(s.T, BQ), s.B * s.H);
   k_attn_fwd<HD><<<grid, 256, smem, st>>>(qkv, cs, out, lse, s);
   TURT_LAUNCH_CHECK();
@@ -432,12 +429,9 @@ int launch_bwd(cudaStream_t st, const float* qkv, const float2* cs, const float*
   TURT_LAUNCH_CHECK();
   const int smem_kv = (4 * HD * (64 + PAD) + 2 * 64 * (HD + PAD) + 2 * 64 * (64 + PAD) + 128) * 4;
   const int smem_q = (4 * HD * (64 + PAD) + 64 * (HD + PAD) + 64 * (64 + PAD)) * 4;
-  static bool cfg = false;
-  if (!cfg) {
-    TURT_CHECK_CUDA(cudaFuncSetAttribute(k_attn_bwd_kv<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv));
-    TURT_CHECK_CUDA(cudaFuncSetAttribute(k_attn_bwd_q<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q));
-    cfg = true;
-  }
+  static std::atomic<uint64_t> cfg_kv{0}, cfg_q{0};
+  RC(smem_attr_per_device(cfg_kv, k_attn_bwd_kv<HD>, smem_kv));
+  RC(smem_attr_per_device(cfg_q, k_attn_bwd_q<HD>, smem_q));
   dim3 grid(ceil_div(s.T, 64), s.B * s.H);
   k_attn_bwd_kv<HD><<<grid, 256, smem_kv, st>>>(qkv, cs, dout, lse, D, dqkv, s);
   TURT_LAUNCH_CHECK();

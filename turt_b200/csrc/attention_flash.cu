@@ -862,22 +862,13 @@ __global__ void __launch_bounds__(320, 1)
   }
 }
 
-template <typename K>
-int set_smem(K kfn, int bytes) {
-  TURT_CHECK_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-  return OK;
-}
-
 template <int HD>
 int flash_fwd(cudaStream_t st, const GemmOperand& q, const GemmOperand& k, const GemmOperand& v, float* out,
               long ld_out, float* lse, int B, int T, int H, float scale, int* flags) {
   using S = FlashFwd<HD>;
   static_assert(S::SMEM <= 232448, "flash forward: shared memory budget exceeded");
-  static bool attr = false;
-  if (!attr) {
-    RC(set_smem(k_flash_fwd<HD>, S::SMEM));
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr{0};
+  RC(smem_attr_per_device(attr, k_flash_fwd<HD>, S::SMEM));
   CUtensorMap mk, mv;
   RC(tensor_map_f32(&mk, k, HD, T, H, B * H, 32, S::KB, false));
   RC(tensor_map_f32(&mv, v, HD, T, H, B * H, 32, 32, true));
@@ -894,12 +885,9 @@ int flash_bwd(cudaStream_t st, const GemmOperand& q, const GemmOperand& k, const
   using SQ = FlashDq<HD>;
   using SK = FlashDkv<HD>;
   static_assert(SQ::SMEM <= 232448 && SK::SMEM <= 232448, "flash backward: shared memory budget exceeded");
-  static bool attr = false;
-  if (!attr) {
-    RC(set_smem(k_flash_dq<HD>, SQ::SMEM));
-    RC(set_smem(k_flash_dkv<HD>, SK::SMEM));
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr_q{0}, attr_kv{0};
+  RC(smem_attr_per_device(attr_q, k_flash_dq<HD>, SQ::SMEM));
+  RC(smem_attr_per_device(attr_kv, k_flash_dkv<HD>, SK::SMEM));
   CUtensorMap mk, mv, mkm;
   RC(tensor_map_f32(&mk, k, HD, T, H, B * H, 32, SQ::KB, false));
   RC(tensor_map_f32(&mv, v, HD, T, H, B * H, 32, SQ::KB, false));

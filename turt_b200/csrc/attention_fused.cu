@@ -668,11 +668,8 @@ int launch_fused(cudaStream_t st, const CUtensorMap& mq, const CUtensorMap& mk, 
   using S = FShape<HD>;
   static_assert(S::SMEM <= 232448, "fused attention: shared memory budget exceeded");
   auto kfn = k_attn_fwd_fused<HD>;
-  static bool attr = false;
-  if (!attr) {
-    TURT_CHECK_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM));
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr{0};
+  RC(smem_attr_per_device(attr, kfn, S::SMEM));
   TURT_CHECK_CUDA((launch_pdl(kfn, dim3(B * H, ceil_div(T, kFQ)), dim3(kFThreads), S::SMEM, st, mq, mk, mv, mp, pitch,
                               out, ld_out, T, H, scale, flags)));
   TURT_LAUNCH_CHECK();
@@ -686,11 +683,8 @@ int launch_dsoftmax(cudaStream_t st, const CUtensorMap& mo, const CUtensorMap& m
   using Dsh = DShape<HD>;
   static_assert(Dsh::SMEM <= 232448, "fused softmax backward: shared memory budget exceeded");
   auto kfn = k_attn_dsoftmax_fused<HD>;
-  static bool attr = false;
-  if (!attr) {
-    TURT_CHECK_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, Dsh::SMEM));
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr{0};
+  RC(smem_attr_per_device(attr, kfn, Dsh::SMEM));
   TURT_CHECK_CUDA((launch_pdl(kfn, dim3(B * H, ceil_div(T, kFQ)), dim3(kFThreads), Dsh::SMEM, st, mo, mv, mp, ms, mk,
                               pitch, dq, ld_dq, rope, T, H, scale, flags)));
   TURT_LAUNCH_CHECK();
@@ -878,11 +872,8 @@ int launch_dkv(cudaStream_t st, const CUtensorMap& mp, const CUtensorMap& ms, co
   using Sh = KVShape<HD>;
   static_assert(Sh::SMEM <= 232448, "fused dK/dV: shared memory budget exceeded");
   auto kfn = k_attn_dkv_fused<HD>;
-  static bool attr = false;
-  if (!attr) {
-    TURT_CHECK_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, Sh::SMEM));
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr{0};
+  RC(smem_attr_per_device(attr, kfn, Sh::SMEM));
   TURT_CHECK_CUDA((launch_pdl(kfn, dim3(B * H, ceil_div(T, 128)), dim3(320), Sh::SMEM, st, mp, ms, mo, mq, dqkv, ld,
                               rope, T, H, flags)));
   TURT_LAUNCH_CHECK();

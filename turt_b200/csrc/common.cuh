@@ -5,6 +5,7 @@
 #include <stdint.h>
 #include <stdio.h>
 
+#include <atomic>
 #include <string>
 
 #ifndef __CUDA_ARCH__
@@ -52,6 +53,21 @@ void note_launch(int n = 1);
     int rc__ = (x);        \
     if (rc__) return rc__; \
   } while (0)
+
+// Raises a kernel's dynamic shared-memory limit on the current device, once per device.
+// Function attributes belong to each device's context, so a kernel launched from several
+// device worker threads must be configured on every device; `done` is that kernel's own bit
+// set of configured devices (a racing second set on the same device is harmless).
+template <typename K>
+int smem_attr_per_device(std::atomic<uint64_t>& done, K kfn, int bytes) {
+  int dev = 0;
+  TURT_CHECK_CUDA(cudaGetDevice(&dev));
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return OK;
+  TURT_CHECK_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.fetch_or(bit, std::memory_order_acq_rel);
+  return OK;
+}
 
 #define TURT_REQUIRE(cond, msg)             \
   do {                                      \

@@ -14,6 +14,7 @@
 #include <nccl.h>
 
 #include <chrono>
+#include <mutex>
 #include <string>
 #include <thread>
 #include <vector>
@@ -41,6 +42,8 @@ NcclApi& api() {
 }
 
 int load_nccl() {
+  static std::mutex mu;  // device worker threads may load it concurrently
+  std::lock_guard<std::mutex> lock(mu);
   NcclApi& a = api();
   if (a.h) return OK;
   void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);

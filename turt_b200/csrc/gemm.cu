@@ -338,6 +338,28 @@ __device__ __forceinline__ void epi_tile(const GemmEpi& epi, const EpiVec& vec, 
   }
 }
 
+// While the accumulator of a unit is still being computed, pulls the global rows its epilogue
+// will read (the residual R, or C itself when accumulating) into L2, so that the epilogue's
+// chunk-by-chunk loads do not each wait a DRAM round trip.
+template <int BN>
+__device__ __forceinline__ void epi_prefetch(const GemmEpi& epi, long row, int M, int N, int n0, long cboff) {
+  if (row >= M) return;
+  const float* src = nullptr;
+  long ld = 0;
+  if (epi.kind == EPI_ADD_RES || epi.kind == EPI_GELU_BWD) {
+    src = epi.R + (epi.kind == EPI_ADD_RES ? cboff : 0);
+    ld = epi.ldr;
+  } else if (epi.kind == EPI_ACCUM) {
+    src = epi.C + cboff;
+    ld = epi.ldc;
+  }
+  if (!src) return;
+  const float* p = src + row * ld + n0;
+  const int cols = min(BN, N - n0);
+#pragma unroll 1
+  for (int c = 0; c < cols; c += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(p + c));
+}
+
 // ------------------------------------------------------------ split-K
 // A split's partial of one 32-row x BN piece (rows rowbase.., columns n0..) goes to its own
 // dense plane of the workspace, [batch][split][M][N], through L2 (st.global.cg).
@@ -682,6 +704,9 @@ __global__ void __launch_bounds__(GemmShape<BN, BK, X3, MINB>::THREADS, MINB)
       if (!decode(u, m0, n0, b, kt0, nkt)) continue;
       const int acc = t & 1, use = t >> 1;
       t++;
+      if (ksplits == 1)
+        epi_prefetch<BN>(epi, m0 + q * 32 + lane, M, N, n0,
+                         (long)(b % bdiv) * epi.strideC + (long)(b / bdiv) * epi.strideC_hi);
       if (!mbar_wait(&tfull[acc], use & 1, flags, 103)) {
         *abort_flag = 1;
         break;
@@ -1079,6 +1104,9 @@ __global__ void __launch_bounds__(352, 1)
       if (!decode(u, m0, n0, b, kt0, nkt)) continue;
       const int acc = t & 1, use = t >> 1;
       t++;
+      if (ksplits == 1)
+        epi_prefetch<BN>(epi, m0 + (int)rank * BM + q * 32 + lane, M, N, n0,
+                         (long)(b % bdiv) * epi.strideC + (long)(b / bdiv) * epi.strideC_hi);
       if (!mbar_wait(&tfull[acc], use & 1, flags, 113)) {
         *abort_flag = 1;
         break;
@@ -1204,12 +1232,14 @@ int make_map(CUtensorMap* map, const float* base, long inner, long rows, long n_
 }
 
 int num_sms() {
-  static int n = 0;
+  static std::atomic<int> cached{0};  // every device of one node has the same SM count
+  int n = cached.load(std::memory_order_relaxed);
   if (!n) {
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     if (n <= 0) n = 148;
+    cached.store(n, std::memory_order_relaxed);
   }
   return n;
 }
@@ -1227,12 +1257,9 @@ int launch(const LaunchArgs& a) {
   using S = GemmShape<BN, BK, X3, MINB>;
   static_assert(S::SMEM <= S::SMEM_CAP, "gemm: shared memory budget exceeded");
   static_assert(S::STAGES >= 2, "gemm: fewer than two pipeline stages fit");
-  static bool configured = false;
+  static std::atomic<uint64_t> configured{0};
   auto kfn = k_gemm_tf32<BN, BK, A_MN, B_MN, X3, MINB>;
-  if (!configured) {
-    TURT_CHECK_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM));
-    configured = true;
-  }
+  RC(smem_attr_per_device(configured, kfn, S::SMEM));
   const long units = (long)ceil_div(a.M, BM) * ceil_div(a.N, BN) * a.batch * a.ks;
   const long slots = (long)MINB * num_sms();
   const int grid = (int)(units < slots ? units : slots);
@@ -1271,9 +1298,15 @@ int launch_pair(const LaunchArgs& a) {
   static_assert(S::SMEM <= 232448, "gemm: shared memory budget exceeded");
   static_assert(S::STAGES >= 3, "gemm: fewer than three pipeline stages fit");
   auto kfn = k_gemm_tf32_pair<BN, A_MN, B_MN>;
-  static int max_pairs = 0;
+  // Per device: the attribute and the co-resident pair count belong to each device's context.
+  static std::atomic<uint64_t> configured{0};
+  static std::atomic<int> max_pairs_dev[64];
+  int dev = 0;
+  TURT_CHECK_CUDA(cudaGetDevice(&dev));
+  std::atomic<int>& max_pairs_slot = max_pairs_dev[dev & 63];
+  int max_pairs = max_pairs_slot.load(std::memory_order_acquire);
   if (!max_pairs) {
-    TURT_CHECK_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM));
+    RC(smem_attr_per_device(configured, kfn, S::SMEM));
     cudaLaunchConfig_t q = {};
     cudaLaunchAttribute qa[1];
     qa[0].id = cudaLaunchAttributeClusterDimension;
@@ -1291,6 +1324,7 @@ int launch_pair(const LaunchArgs& a) {
       n = num_sms() / 2;
     }
     max_pairs = n;
+    max_pairs_slot.store(n, std::memory_order_release);
   }
   const long units = (long)ceil_div(a.M, 2 * BM) * ceil_div(a.N, BN) * a.batch * a.ks;
   const int pairs = (int)(units < max_pairs ? units : max_pairs);

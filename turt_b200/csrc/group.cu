@@ -10,6 +10,8 @@
 // batch holds floor(b/n) sequences, plus one for i < b mod n (the reference's shard()); its
 // mean-loss gradient is scaled by rows_i / b before the all-reduce sums the replicas, which is
 // the reference's weighting exactly, so the optimizer step needs no further scaling.
+#include <cstdio>
+#include <cstdlib>
 #include <condition_variable>
 #include <deque>
 #include <set>
@@ -24,6 +26,18 @@
 
 namespace turt {
 namespace {
+
+// TURT_GROUP_TRACE=1 in the environment prints each phase of each replica's work to stderr.
+bool trace_on() {
+  static const bool on = [] {
+    const char* v = getenv("TURT_GROUP_TRACE");
+    return v && v[0] == '1';
+  }();
+  return on;
+}
+void trace(int dev, const char* what) {
+  if (trace_on()) fprintf(stderr, "[turt group] device %d: %s\n", dev, what);
+}
 
 // One host thread per device, running posted jobs in order with that device current.
 class DeviceWorker {
@@ -185,14 +199,22 @@ int turt_group_create(int ndev, const int* devs, const turt_config* cfg, turt_gr
   g->model.assign(ndev, nullptr);
   for (int i = 0; i < ndev; i++) g->workers.push_back(new DeviceWorker(devs[i]));
   int rc = run_all(g, [g, cfg](int i) -> int {
+    trace(g->devs[i], "context");
     RC(turt_init(g->devs[i], &g->ctx[i]));
+    trace(g->devs[i], "model");
     return turt_model_create(g->ctx[i], cfg, &g->model[i]);
   });
   if (rc == OK && ndev > 1) {
     char uid[128];
     rc = turt_dp_unique_id(uid);
     // every rank joins the communicator concurrently (ncclCommInitRank blocks until all have)
-    if (rc == OK) rc = run_all(g, [g, &uid, ndev](int i) { return turt_dp_init(g->model[i], i, ndev, uid); });
+    if (rc == OK)
+      rc = run_all(g, [g, &uid, ndev](int i) -> int {
+        trace(g->devs[i], "communicator init");
+        const int r = turt_dp_init(g->model[i], i, ndev, uid);
+        trace(g->devs[i], "communicator ready");
+        return r;
+      });
   }
   if (rc) {
     const std::string msg = last_error();
@@ -274,22 +296,37 @@ int turt_group_forward_backward(turt_group* g, const uint32_t* ids, const uint32
   std::vector<float> loss(g->n, 0.f);
   const bool defer = g->defer;
   const bool want = loss_out != nullptr;
-  // The first reducing call of a batch shape enqueues its whole backward pass before any
-  // collective (then one all-reduce of the gradient buffer): kernels are loaded on their first
-  // launch, and a load must not wait behind a collective that spins for a peer device whose host
-  // thread is itself still launching.  Later calls overlap the per-layer reductions.
+  // The first call of a batch shape allocates (workspace, pinned staging, split-K partials) and
+  // loads kernels on their first launch.  In one process with peer access enabled, an allocation
+  // may wait for every device, including a peer whose collective already spins for this device's
+  // part of it: so that call enqueues every replica's whole backward pass first (reductions
+  // deferred) and only then, once all host threads are past their allocations, one all-reduce of
+  // the gradient buffers.  Later calls of the shape allocate nothing and overlap the per-layer
+  // reductions with the backward pass.
   const bool first = g->n > 1 && !defer && !g->shapes_seen.count({b, t});
   int rc = run_all(g, [&](int i) -> int {
+    const int dev = g->devs[i];
     RC(turt_dp_defer(g->model[i], (defer || first) ? 1 : 0));
     const size_t off = (size_t)row0[i] * t;
+    trace(dev, first ? "forward / backward (reduction after every replica's)" : "forward / backward");
     RC(turt_forward_backward(g->model[i], ids + off, targets + off, rows[i], t,
                              loss_scale * (float)rows[i] / (float)b, (want && !first) ? &loss[i] : nullptr));
-    if (!first) return OK;
-    RC(turt_dp_allreduce_grads(g->model[i]));
-    RC(turt_dp_defer(g->model[i], 0));
-    return want ? turt_read_loss(g->model[i], &loss[i]) : OK;
+    trace(dev, "forward / backward enqueued");
+    return OK;
   });
   if (rc) return rc;
+  if (first) {
+    rc = run_all(g, [&](int i) -> int {
+      const int dev = g->devs[i];
+      RC(turt_dp_allreduce_grads(g->model[i]));
+      trace(dev, "all-reduce enqueued");
+      RC(turt_dp_defer(g->model[i], 0));
+      const int r = want ? turt_read_loss(g->model[i], &loss[i]) : OK;
+      trace(dev, "step done");
+      return r;
+    });
+    if (rc) return rc;
+  }
   if (first) g->shapes_seen.insert({b, t});
   if (want) {
     double l = 0;

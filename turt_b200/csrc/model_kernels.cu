@@ -206,12 +206,13 @@ __global__ void __launch_bounds__(256) k_rms_fwd(const float* __restrict__ x, co
   }
 }
 
-// Block partial of a per-column sum: the 8 warps' register partials (lane chunks) are combined
-// in shared memory in fixed order and written column-major as part[c][blockIdx.x] (nparts =
-// gridDim.x entries per column), so that the final reduction reads each column contiguously.
+// Block partial written as a row: part_row[c] = sum over the block's 8 warps (fixed order) of
+// their register partials.  Consecutive threads write consecutive columns.
 template <int NJ>
-__device__ __forceinline__ void block_partial(const float4 (&acc)[NJ], float* sm, float* __restrict__ part, int E) {
+__device__ __forceinline__ void block_partial_row(const float4 (&acc)[NJ], float* sm, float* __restrict__ part_row,
+                                                  int E) {
   const int w = threadIdx.x / 32, lane = threadIdx.x & 31, n4 = E / 4;
+  __syncthreads();  // sm may still be read by an earlier call
 #pragma unroll
   for (int j = 0; j < NJ; j++) {
     const int i = lane + 32 * j;
@@ -222,20 +223,87 @@ __device__ __forceinline__ void block_partial(const float4 (&acc)[NJ], float* sm
     float t = 0.f;
 #pragma unroll
     for (int q = 0; q < kNormWarps; q++) t += sm[q * E + c];
-    part[(size_t)c * gridDim.x + blockIdx.x] = t;
+    part_row[c] = t;
   }
 }
 
+// Column sums of the block partials, finished inside the kernel that wrote them (no second
+// launch).  part[b][c] holds block b's partial (nb = gridDim.x rows of C).  Blocks are grouped by
+// kPartGroup: the last block of a group to finish adds the group's rows in block order into
+// gpart[group][c]; the last group to finish adds the group rows in group order to out[c].  Every
+// sum runs in a fixed order, so the result does not depend on which block finishes last.  ctr
+// holds ng + 1 counters that are zero on entry and are left zero.  part2 / gpart2 / out2, when
+// out2 is non-null, are a second column sum finished alongside (LayerNorm's dbeta).
+constexpr int kPartGroup = 8;
+__device__ __forceinline__ void finish_column_sums(const float* part, float* gpart, float* out, const float* part2,
+                                                   float* gpart2, float* out2, int C, unsigned* ctr) {
+  __shared__ unsigned ticket;
+  const int nb = gridDim.x, ng = (nb + kPartGroup - 1) / kPartGroup, grp = blockIdx.x / kPartGroup;
+  const int b0 = grp * kPartGroup, gsize = min(kPartGroup, nb - b0);
+  __threadfence();  // this thread's partial stores are visible device-wide before the count
+  __syncthreads();
+  if (threadIdx.x == 0) ticket = atomicAdd(&ctr[grp], 1u);
+  __syncthreads();
+  if (ticket != (unsigned)(gsize - 1)) return;
+  __threadfence();
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float t = 0.f, t2 = 0.f;
+    for (int b = b0; b < b0 + gsize; b++) {
+      t += __ldcg(part + (size_t)b * C + c);
+      if (out2) t2 += __ldcg(part2 + (size_t)b * C + c);
+    }
+    gpart[(size_t)grp * C + c] = t;
+    if (out2) gpart2[(size_t)grp * C + c] = t2;
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    ctr[grp] = 0u;
+    ticket = atomicAdd(&ctr[ng], 1u);
+  }
+  __syncthreads();
+  if (ticket != (unsigned)(ng - 1)) return;
+  __threadfence();
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float t = 0.f, t2 = 0.f;
+#pragma unroll 8
+    for (int q = 0; q < ng; q++) {
+      t += __ldcg(gpart + (size_t)q * C + c);
+      if (out2) t2 += __ldcg(gpart2 + (size_t)q * C + c);
+    }
+    out[c] += t;
+    if (out2) out2[c] += t2;
+  }
+  if (threadIdx.x == 0) ctr[ng] = 0u;
+}
+
+// Pulls a row of E floats into L2 ahead of its loads (one prefetch per 128-byte line, spread
+// over the warp's lanes).
+__device__ __forceinline__ void prefetch_row_l2(const float* row, int E, int lane) {
+  for (int k = lane * 32; k < E; k += 32 * 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(row + k));
+}
+
+// Register budget of the norm backwards: two 256-thread blocks per SM up to E = 512, one block
+// per SM (more registers per thread) for the wider rows.
+template <int NJ>
+struct NormBwdCfg {
+  static constexpr int kMinBlocks = NJ <= 4 ? 2 : 1;
+  static constexpr int kRows = NJ <= 3 ? 2 : 1;  // RMSNorm rows per warp iteration
+};
+
 // RMSNorm backward with the residual gradient fused in:
 //   dx = dres + rs*g*dy - (rs^3/E) * (sum_j dy_j g_j x_j) * x      (RMS_DX, autograd.ts:331-351)
-// and per-block partial dgamma = sum_rows dy * x * rs              (RMS_DG, :352-365).
-// dx may alias dres.  Rows are dealt to warps grid-stride, two rows per iteration so that each
-// warp keeps 6*NJ independent 16-byte loads in flight.
+// and dgamma += sum_rows dy * x * rs                               (RMS_DG, :352-365),
+// the column sum finished in this launch (finish_column_sums).  dx may alias dres.  Rows are
+// dealt to warps grid-stride, R rows per iteration: x, dy and dres of those rows are loaded
+// together (3*R*NJ independent 16-byte loads in flight per lane) and the next iteration's rows
+// are prefetched into L2 first.
 template <int NJ>
-__global__ void __launch_bounds__(256, 2) k_rms_bwd(const float* __restrict__ x, const float* __restrict__ dy,
-                                                 const float* __restrict__ g, const float* __restrict__ rstd,
-                                                 const float* dres, float* dx, float* __restrict__ dg_part, int rows,
-                                                 int E) {
+__global__ void __launch_bounds__(256, NormBwdCfg<NJ>::kMinBlocks)
+    k_rms_bwd(const float* __restrict__ x, const float* __restrict__ dy, const float* __restrict__ g,
+              const float* __restrict__ rstd, const float* dres, float* dx, float* __restrict__ part, float* dg_accum,
+              unsigned* ctr, int rows, int E) {
+  constexpr int R = NormBwdCfg<NJ>::kRows;
   pdl_trigger();
   pdl_wait();
   extern __shared__ float sm[];
@@ -248,13 +316,25 @@ __global__ void __launch_bounds__(256, 2) k_rms_bwd(const float* __restrict__ x,
     gv[j] = i < n4 ? ld4(g, i) : make_float4(0.f, 0.f, 0.f, 0.f);
     dgl[j] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  for (int r0 = blockIdx.x * kNormWarps + threadIdx.x / 32; r0 < rows; r0 += 2 * stride) {
-    const int rr[2] = {r0, r0 + stride};
-    float4 xv[2][NJ], dv[2][NJ];
-    float s[2] = {0.f, 0.f}, rs[2];
+  for (int r0 = blockIdx.x * kNormWarps + threadIdx.x / 32; r0 < rows; r0 += R * stride) {
+    int rr[R];
 #pragma unroll
-    for (int q = 0; q < 2; q++) {
+    for (int q = 0; q < R; q++) rr[q] = r0 + q * stride;
+#pragma unroll
+    for (int q = R; q < 2 * R; q++) {
+      const int rn = r0 + q * stride;
+      if (rn < rows) {
+        prefetch_row_l2(x + (size_t)rn * E, E, lane);
+        prefetch_row_l2(dy + (size_t)rn * E, E, lane);
+        if (dres) prefetch_row_l2(dres + (size_t)rn * E, E, lane);
+      }
+    }
+    float4 xv[R][NJ], dv[R][NJ], tv[R][NJ];
+    float s[R], rs[R];
+#pragma unroll
+    for (int q = 0; q < R; q++) {
       const bool ok = rr[q] < rows;
+      s[q] = 0.f;
       rs[q] = ok ? rstd[rr[q]] : 0.f;
 #pragma unroll
       for (int j = 0; j < NJ; j++) {
@@ -262,10 +342,11 @@ __global__ void __launch_bounds__(256, 2) k_rms_bwd(const float* __restrict__ x,
         const bool in = ok && i < n4;
         xv[q][j] = in ? ld4(x + (size_t)rr[q] * E, i) : make_float4(0.f, 0.f, 0.f, 0.f);
         dv[q][j] = in ? ld4(dy + (size_t)rr[q] * E, i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        tv[q][j] = in && dres ? ld4(dres + (size_t)rr[q] * E, i) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
 #pragma unroll
-    for (int q = 0; q < 2; q++)
+    for (int q = 0; q < R; q++)
 #pragma unroll
       for (int j = 0; j < NJ; j++) {
         const float4 a = xv[q][j], d = dv[q][j], gg = gv[j];
@@ -276,31 +357,24 @@ __global__ void __launch_bounds__(256, 2) k_rms_bwd(const float* __restrict__ x,
         dgl[j].w += d.w * a.w * rs[q];
       }
 #pragma unroll
-    for (int q = 0; q < 2; q++) {
+    for (int q = 0; q < R; q++) {
       if (rr[q] >= rows) continue;  // warp-uniform
       const float sum = warp_sum(s[q]);
       const float kf = rs[q] * rs[q] * rs[q] * sum / E;
-      const float* dr = dres ? dres + (size_t)rr[q] * E : nullptr;
       float* dxr = dx + (size_t)rr[q] * E;
 #pragma unroll
       for (int j = 0; j < NJ; j++) {
         const int i = lane + 32 * j;
         if (i >= n4) continue;
-        const float4 a = xv[q][j], d = dv[q][j], gg = gv[j];
-        float4 o = make_float4(rs[q] * d.x * gg.x - kf * a.x, rs[q] * d.y * gg.y - kf * a.y,
-                               rs[q] * d.z * gg.z - kf * a.z, rs[q] * d.w * gg.w - kf * a.w);
-        if (dr) {
-          const float4 t = ld4(dr, i);
-          o.x += t.x;
-          o.y += t.y;
-          o.z += t.z;
-          o.w += t.w;
-        }
-        st4(dxr, i, o);
+        const float4 a = xv[q][j], d = dv[q][j], gg = gv[j], t = tv[q][j];
+        st4(dxr, i,
+            make_float4(rs[q] * d.x * gg.x - kf * a.x + t.x, rs[q] * d.y * gg.y - kf * a.y + t.y,
+                        rs[q] * d.z * gg.z - kf * a.z + t.z, rs[q] * d.w * gg.w - kf * a.w + t.w));
       }
     }
   }
-  block_partial<NJ>(dgl, sm, dg_part, E);
+  block_partial_row<NJ>(dgl, sm, part + (size_t)blockIdx.x * E, E);
+  finish_column_sums(part, part + (size_t)2 * gridDim.x * E, dg_accum, nullptr, nullptr, nullptr, E, ctr);
 }
 
 // LayerNorm forward (biased variance), autograd.ts:256-274.
@@ -352,13 +426,14 @@ __global__ void __launch_bounds__(256) k_ln_fwd(const float* __restrict__ x, con
 }
 
 // LayerNorm backward (LN_DX + LN_DGB, autograd.ts:275-308) with the residual gradient fused;
-// partial dgamma / dbeta per block.  One row per warp iteration, grid-stride.
+// dgamma / dbeta column sums finished in this launch (finish_column_sums).  One row per warp
+// iteration, grid-stride.
 template <int NJ>
-__global__ void __launch_bounds__(256, 2) k_ln_bwd(const float* __restrict__ x, const float* __restrict__ dy,
+__global__ void __launch_bounds__(256, NormBwdCfg<NJ>::kMinBlocks) k_ln_bwd(const float* __restrict__ x, const float* __restrict__ dy,
                                                 const float* __restrict__ g, const float* __restrict__ mean,
                                                 const float* __restrict__ rstd, const float* dres, float* dx,
-                                                float* __restrict__ dg_part, float* __restrict__ db_part, int rows,
-                                                int E) {
+                                                float* __restrict__ part, float* dg_accum, float* db_accum,
+                                                unsigned* ctr, int rows, int E) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ float sm[];
@@ -417,9 +492,10 @@ __global__ void __launch_bounds__(256, 2) k_ln_bwd(const float* __restrict__ x, 
       st4(dxr, i, o);
     }
   }
-  block_partial<NJ>(dgl, sm, dg_part, E);
-  __syncthreads();
-  block_partial<NJ>(dbl, sm, db_part, E);
+  const size_t nbE = (size_t)gridDim.x * E, ngE = (size_t)((gridDim.x + kPartGroup - 1) / kPartGroup) * E;
+  block_partial_row<NJ>(dgl, sm, part + (size_t)blockIdx.x * E, E);
+  block_partial_row<NJ>(dbl, sm, part + nbE + (size_t)blockIdx.x * E, E);
+  finish_column_sums(part, part + 2 * nbE, dg_accum, part + nbE, part + 2 * nbE + ngE, db_accum, E, ctr);
 }
 
 // out[c] += sum_b part[c][b] (column-major partials, fixed order: deterministic).  One warp per
@@ -777,12 +853,14 @@ int embed_fwd(cudaStream_t st, const float* wte, const float* wpe, const uint32_
 
 namespace {
 int sm_count() {
-  static int n = 0;
+  static std::atomic<int> cached{0};  // every device of one node has the same SM count
+  int n = cached.load(std::memory_order_relaxed);
   if (!n) {
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     if (n <= 0) n = 148;
+    cached.store(n, std::memory_order_relaxed);
   }
   return n;
 }
@@ -828,21 +906,25 @@ int rms_fwd(cudaStream_t st, const float* x, const float* g, float* y, float* rs
   TURT_LAUNCH_CHECK();
   return OK;
 }
-// Partial-sum rows a norm backward writes: one per block, at most two blocks per SM.
+// Partial-sum rows a norm backward writes: one per block, at most two blocks per SM (and at most
+// kPartGroup * (kNormCounters - 1) blocks, so that the group counters fit).
 int norm_parts(int rows) {
   const int b = ceil_div(rows, kNormWarps);
-  return b < 2 * sm_count() ? b : 2 * sm_count();
+  const int cap = std::min(2 * sm_count(), kPartGroup * (kNormCounters - 1));
+  return b < cap ? b : cap;
+}
+size_t norm_bwd_part_floats(int rows, int E) {
+  const size_t nb = norm_parts(rows), ng = (nb + kPartGroup - 1) / kPartGroup;
+  return 2 * (nb + ng) * (size_t)E;
 }
 int rms_bwd(cudaStream_t st, const float* x, const float* dy, const float* g, const float* rstd, const float* dres,
-            float* dx, float* dg_accum, float* part, int rows, int E) {
+            float* dx, float* dg_accum, float* part, unsigned* ctr, int rows, int E) {
   TURT_REQUIRE(E % 32 == 0 && E <= 32 * MAXV, "norm width must be a multiple of 32, at most 1024");
   const int nb = norm_parts(rows);
   const size_t smem = (size_t)kNormWarps * E * 4;
-#define CALL(NJ) TURT_CHECK_CUDA((launch_pdl(k_rms_bwd<NJ>, dim3(nb), dim3(256), smem, st, x, dy, g, rstd, dres, dx, part, rows, E)))
+#define CALL(NJ) TURT_CHECK_CUDA((launch_pdl(k_rms_bwd<NJ>, dim3(nb), dim3(256), smem, st, x, dy, g, rstd, dres, dx, part, dg_accum, ctr, rows, E)))
   TURT_NJ_SWITCH(E, CALL)
 #undef CALL
-  TURT_LAUNCH_CHECK();
-  TURT_CHECK_CUDA((launch_pdl(k_reduce_parts, dim3(ceil_div(E, 8)), dim3(256), 0, st, part, nb, E, dg_accum)));
   TURT_LAUNCH_CHECK();
   return OK;
 }
@@ -856,18 +938,15 @@ int ln_fwd(cudaStream_t st, const float* x, const float* g, const float* b, floa
   return OK;
 }
 int ln_bwd(cudaStream_t st, const float* x, const float* dy, const float* g, const float* mean, const float* rstd,
-           const float* dres, float* dx, float* dg_accum, float* db_accum, float* part, int rows, int E) {
+           const float* dres, float* dx, float* dg_accum, float* db_accum, float* part, unsigned* ctr, int rows,
+           int E) {
   TURT_REQUIRE(E % 32 == 0 && E <= 32 * MAXV, "norm width must be a multiple of 32, at most 1024");
   const int nb = norm_parts(rows);
   const size_t smem = (size_t)kNormWarps * E * 4;
 #define CALL(NJ) \
-  TURT_CHECK_CUDA((launch_pdl(k_ln_bwd<NJ>, dim3(nb), dim3(256), smem, st, x, dy, g, mean, rstd, dres, dx, part, part + (size_t)nb * E, rows, E)))
+  TURT_CHECK_CUDA((launch_pdl(k_ln_bwd<NJ>, dim3(nb), dim3(256), smem, st, x, dy, g, mean, rstd, dres, dx, part, dg_accum, db_accum, ctr, rows, E)))
   TURT_NJ_SWITCH(E, CALL)
 #undef CALL
-  TURT_LAUNCH_CHECK();
-  TURT_CHECK_CUDA((launch_pdl(k_reduce_parts, dim3(ceil_div(E, 8)), dim3(256), 0, st, part, nb, E, dg_accum)));
-  TURT_LAUNCH_CHECK();
-  TURT_CHECK_CUDA((launch_pdl(k_reduce_parts, dim3(ceil_div(E, 8)), dim3(256), 0, st, part + (size_t)nb * E, nb, E, db_accum)));
   TURT_LAUNCH_CHECK();
   return OK;
 }
