@@ -27,6 +27,16 @@ def _ok(got, ref):
     return max_rel_err(got, ref) < TOL and norm < NORM_TOL
 
 
+def _ok_terms(got, ref, abs_terms, coef=1e-5):
+    """Entries that are sums of a few fp32 terms (RMSNorm's dx = rs*g*dy - k*x + dres): each within
+    1e-5 of the sum of its terms' magnitudes.  The oracle restates the reference's autograd chain
+    with an fp32 rounding after every operation, a different path from the kernel's one-pass
+    formula; an fp32 emulation of the kernel at [8192,768] sits 3.7e-6 of sum|terms| from it and
+    reaches maxRelErr 1.4e-3 on entries the residual add cancels to ~1e-3."""
+    got, ref = np.asarray(got, np.float64), np.asarray(ref, np.float64)
+    return bool(np.all(np.abs(got - ref) <= coef * np.asarray(abs_terms, np.float64) + 1e-7))
+
+
 def _ok_sum(got, ref, abs_terms):
     """For a column sum over many rows computed in fp32: each entry within 1e-6 of the sum of
     its terms' magnitudes (about 16 fp32 ulps of that sum; a plain blocked fp32 sum of 8192
@@ -59,10 +69,9 @@ def _dev(ctx, a):
                                     (2500, 640)])
 @pytest.mark.parametrize("with_res", [False, True])
 def test_rms_bwd(ctx, orc, rows, E, with_res):
-    """RMSNorm backward with the dgamma column sum finished in the same launch (per-group then
-    final sums, counters left zero).  Called twice: dgamma accumulates both calls, so a counter
-    that was not reset or a group summed twice would show.  1000 rows give a ragged last group;
-    E 640 / 768 use one row per warp iteration."""
+    """RMSNorm backward (residual gradient optional) and its dgamma column sum.  Called twice:
+    dgamma accumulates both calls and dx is rewritten identically.  1000 rows leave the last block
+    short; E 640 / 768 run one row per warp iteration with one block per SM."""
     from turt_b200._lib import check, lib
     rng = np.random.default_rng(rows + E)
     x = rng.standard_normal((rows, E)).astype(np.float32)
@@ -81,7 +90,12 @@ def test_rms_bwd(ctx, orc, rows, E, with_res):
         check(lib().turt_fused_rms_bwd(ctx.handle, bufs[0], bufs[1], bufs[2], bufs[3], dr, dx, bufs[4], rows, E))
     got_dx = ctx.download(dx, rows * E).reshape(rows, E)
     got_dg = ctx.download(bufs[4], E)
-    assert _ok(got_dx, ref_dx)
+    x64, rs64 = x.astype(np.float64), rstd.astype(np.float64)
+    k64 = rs64 ** 3 * (dy.astype(np.float64) * gam * x64).sum(axis=1) / E
+    dx_terms = np.abs(rs64[:, None] * dy * gam) + np.abs(k64[:, None] * x64) + (np.abs(dres) if with_res else 0.0)
+    assert _ok_terms(got_dx, ref_dx, dx_terms)
+    assert max_rel_err(got_dx, ref_dx) < 2e-3  # the model's gradient bar
+    assert np.max(np.abs(got_dx - ref_dx)) / np.max(np.abs(ref_dx)) < NORM_TOL
     abs_terms = 2 * np.abs(dy.astype(np.float64) * x * rstd[:, None]).sum(axis=0) + np.abs(dg0)
     assert _ok_sum(got_dg, 2 * ref_dg.astype(np.float64) + dg0, abs_terms)
 

@@ -8,7 +8,6 @@
 #include "../../include/turt_cuda.h"
 #include "ctx.cuh"
 #include "gemm.cuh"
-#include "model_kernels.cuh"
 #include "ops.cuh"
 
 namespace turt {
@@ -89,8 +88,6 @@ int turt_init(int device, turt_ctx** out) {
   c->own_stream = true;
   TURT_CHECK_CUDA(cudaMalloc(&c->flags, sizeof(int) * FLAG_COUNT));
   TURT_CHECK_CUDA(cudaMemset(c->flags, 0, sizeof(int) * FLAG_COUNT));
-  TURT_CHECK_CUDA(cudaMalloc(&c->counters, sizeof(unsigned) * kNormCounters));
-  TURT_CHECK_CUDA(cudaMemset(c->counters, 0, sizeof(unsigned) * kNormCounters));
   // Reserve turt_host_matmul_noalloc's fixed staging array now.  Best effort: a failure here
   // is reported again by that entry point's first call, and is no reason to refuse a context.
   if (noalloc_setup(device) != OK) (void)cudaGetLastError();
@@ -104,7 +101,6 @@ int turt_ctx_destroy(turt_ctx* ctx) {
   for (void* p : ctx->pending_free) cudaFree(p);
   for (void* p : ctx->live_set) cudaFree(p);
   cudaFree(ctx->flags);
-  cudaFree(ctx->counters);
   if (ctx->scratch) cudaFree(ctx->scratch);
   gemm_release_stream(ctx->stream);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);

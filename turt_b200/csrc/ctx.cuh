@@ -12,7 +12,6 @@ struct turt_ctx {
   cudaStream_t stream = nullptr;
   bool own_stream = false;
   int* flags = nullptr;  // FLAG_COUNT device ints raised by kernels
-  unsigned* counters = nullptr;  // zeroed completion counters of the standalone norm backward
   std::unordered_set<void*> live_set;
   std::vector<void*> pending_free;
   int live = 0, peak = 0;

@@ -96,8 +96,8 @@ extern "C" int turt_fused_rms_bwd(turt_ctx* ctx, const float* x, const float* dy
   TURT_REQUIRE(aligned16(x) && aligned16(dy) && aligned16(g) && aligned16(dx) && (!dres || aligned16(dres)),
                "fused_rms_bwd: buffers must be 16-byte aligned");
   void* part = nullptr;
-  RC(scratch(ctx, norm_bwd_part_floats(rows, E) * 4, &part));
-  return rms_bwd(ctx->stream, x, dy, g, rstd, dres, dx, dg, static_cast<float*>(part), ctx->counters, rows, E);
+  RC(scratch(ctx, (size_t)norm_parts(rows) * E * 4, &part));
+  return rms_bwd(ctx->stream, x, dy, g, rstd, dres, dx, dg, static_cast<float*>(part), rows, E);
 }
 
 extern "C" int turt_fused_swiglu_bwd(turt_ctx* ctx, const float* gate, const float* up, const float* dact,

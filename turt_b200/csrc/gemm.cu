@@ -338,28 +338,6 @@ __device__ __forceinline__ void epi_tile(const GemmEpi& epi, const EpiVec& vec, 
   }
 }
 
-// While the accumulator of a unit is still being computed, pulls the global rows its epilogue
-// will read (the residual R, or C itself when accumulating) into L2, so that the epilogue's
-// chunk-by-chunk loads do not each wait a DRAM round trip.
-template <int BN>
-__device__ __forceinline__ void epi_prefetch(const GemmEpi& epi, long row, int M, int N, int n0, long cboff) {
-  if (row >= M) return;
-  const float* src = nullptr;
-  long ld = 0;
-  if (epi.kind == EPI_ADD_RES || epi.kind == EPI_GELU_BWD) {
-    src = epi.R + (epi.kind == EPI_ADD_RES ? cboff : 0);
-    ld = epi.ldr;
-  } else if (epi.kind == EPI_ACCUM) {
-    src = epi.C + cboff;
-    ld = epi.ldc;
-  }
-  if (!src) return;
-  const float* p = src + row * ld + n0;
-  const int cols = min(BN, N - n0);
-#pragma unroll 1
-  for (int c = 0; c < cols; c += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(p + c));
-}
-
 // ------------------------------------------------------------ split-K
 // A split's partial of one 32-row x BN piece (rows rowbase.., columns n0..) goes to its own
 // dense plane of the workspace, [batch][split][M][N], through L2 (st.global.cg).
@@ -704,9 +682,6 @@ __global__ void __launch_bounds__(GemmShape<BN, BK, X3, MINB>::THREADS, MINB)
       if (!decode(u, m0, n0, b, kt0, nkt)) continue;
       const int acc = t & 1, use = t >> 1;
       t++;
-      if (ksplits == 1)
-        epi_prefetch<BN>(epi, m0 + q * 32 + lane, M, N, n0,
-                         (long)(b % bdiv) * epi.strideC + (long)(b / bdiv) * epi.strideC_hi);
       if (!mbar_wait(&tfull[acc], use & 1, flags, 103)) {
         *abort_flag = 1;
         break;
@@ -1104,9 +1079,6 @@ __global__ void __launch_bounds__(352, 1)
       if (!decode(u, m0, n0, b, kt0, nkt)) continue;
       const int acc = t & 1, use = t >> 1;
       t++;
-      if (ksplits == 1)
-        epi_prefetch<BN>(epi, m0 + (int)rank * BM + q * 32 + lane, M, N, n0,
-                         (long)(b % bdiv) * epi.strideC + (long)(b / bdiv) * epi.strideC_hi);
       if (!mbar_wait(&tfull[acc], use & 1, flags, 113)) {
         *abort_flag = 1;
         break;

@@ -218,12 +218,10 @@ int ensure_workspace(turt_model* m, int B, int T) {
   size_t dS = S_need ? take((size_t)S_need) : 0;
   size_t dact = rope ? take((size_t)N * h) : 0;
   const int C = 3 * E > W1 ? 3 * E : W1;
-  size_t part = take(std::max((size_t)2 * norm_parts(N) * (C > E ? C : E), norm_bwd_part_floats(N, E)));
-  size_t norm_ctr = take(kNormCounters);
+  size_t part = take((size_t)2 * norm_parts(N) * (C > E ? C : E));
   size_t ids = take(N), tgt = take(N);
   void* ws = nullptr;
   TURT_CHECK_CUDA(cudaMalloc(&ws, off));
-  TURT_CHECK_CUDA(cudaMemset(static_cast<char*>(ws) + norm_ctr, 0, kNormCounters * sizeof(unsigned)));
   m->ws = ws;
   char* base = static_cast<char*>(ws);
   auto F = [&](size_t o) { return reinterpret_cast<float*>(base + o); };
@@ -263,7 +261,6 @@ int ensure_workspace(turt_model* m, int B, int T) {
   m->dS = S_need ? F(dS) : nullptr;
   m->dact = rope ? F(dact) : nullptr;
   m->part = F(part);
-  m->norm_ctr = reinterpret_cast<unsigned*>(base + norm_ctr);
   m->d_ids = reinterpret_cast<uint32_t*>(base + ids);
   m->d_tgt = reinterpret_cast<uint32_t*>(base + tgt);
   if (m->h_ids) cudaFreeHost(m->h_ids);
@@ -422,9 +419,9 @@ int backward(turt_model* m, int B, int T) {
   RC(fork());
   RC(gemm_tf32(wg, V, E, N, 1, opMN(m->logits, V), opMN(m->yf, E), epi(EPI_ACCUM, G + m->wte, E), flags, mp(m)));
   if (m->modern)
-    RC(rms_bwd(st, m->xL, m->dy, P + m->lnfg, m->rsf, nullptr, m->dx, G + m->lnfg, m->part, m->norm_ctr, N, E));
+    RC(rms_bwd(st, m->xL, m->dy, P + m->lnfg, m->rsf, nullptr, m->dx, G + m->lnfg, m->part, N, E));
   else
-    RC(ln_bwd(st, m->xL, m->dy, P + m->lnfg, m->muf, m->rsf, nullptr, m->dx, G + m->lnfg, G + m->lnfb, m->part, m->norm_ctr, N, E));
+    RC(ln_bwd(st, m->xL, m->dy, P + m->lnfg, m->muf, m->rsf, nullptr, m->dx, G + m->lnfg, G + m->lnfb, m->part, N, E));
   for (int l = m->cfg.n_layer - 1; l >= 0; l--) {
     const LayerOff& L = m->layers[l];
     LayerAct& a = m->act[l];
@@ -460,9 +457,9 @@ int backward(turt_model* m, int B, int T) {
     }
     RC(wait_mark(0));  // dx is rewritten in place below; dW2 reads it
     if (m->modern)
-      RC(rms_bwd(st, a.h, m->dy, P + L.ln2g, a.rs2, m->dx, m->dx, G + L.ln2g, m->part, m->norm_ctr, N, E));
+      RC(rms_bwd(st, a.h, m->dy, P + L.ln2g, a.rs2, m->dx, m->dx, G + L.ln2g, m->part, N, E));
     else
-      RC(ln_bwd(st, a.h, m->dy, P + L.ln2g, a.mu2, a.rs2, m->dx, m->dx, G + L.ln2g, G + L.ln2b, m->part, m->norm_ctr, N, E));
+      RC(ln_bwd(st, a.h, m->dy, P + L.ln2g, a.mu2, a.rs2, m->dx, m->dx, G + L.ln2g, G + L.ln2b, m->part, N, E));
     // ---- attention
     RC(gemm_tf32(st, N, E, E, 1, opK(m->dx, E), opK(P + L.wproj, E), epi(EPI_STORE, m->datt, E), flags, mp(m)));
     RC(fork());
@@ -487,9 +484,9 @@ int backward(turt_model* m, int B, int T) {
     RC(set_mark(3));
     RC(wait_mark(2));  // dx is rewritten in place below; dWproj reads it
     if (m->modern)
-      RC(rms_bwd(st, a.x, m->dy, P + L.ln1g, a.rs1, m->dx, m->dx, G + L.ln1g, m->part, m->norm_ctr, N, E));
+      RC(rms_bwd(st, a.x, m->dy, P + L.ln1g, a.rs1, m->dx, m->dx, G + L.ln1g, m->part, N, E));
     else
-      RC(ln_bwd(st, a.x, m->dy, P + L.ln1g, a.mu1, a.rs1, m->dx, m->dx, G + L.ln1g, G + L.ln1b, m->part, m->norm_ctr, N, E));
+      RC(ln_bwd(st, a.x, m->dy, P + L.ln1g, a.mu1, a.rs1, m->dx, m->dx, G + L.ln1g, G + L.ln1b, m->part, N, E));
     if (dp_active(m) && !m->dp_defer) RC(dp_after_layer(m, l));
   }
   // the embedding backward accumulates into the wte gradient that the head's dW GEMM (on wg)

@@ -58,7 +58,6 @@ struct turt_model {
   float *xL = nullptr, *yf = nullptr, *rsf = nullptr, *muf = nullptr, *logits = nullptr, *loss_rows = nullptr;
   float *dx = nullptr, *dy = nullptr, *datt = nullptr, *dqkv = nullptr, *dpre = nullptr, *Dsc = nullptr,
         *part = nullptr;
-  unsigned* norm_ctr = nullptr;  // kNormCounters zeroed counters of the norm backwards
   float* dS = nullptr;    // tensor-core attention backward scratch
   float* dact = nullptr;  // d(SwiGLU output) [N][h] (modern arch)
   uint32_t *d_ids = nullptr, *d_tgt = nullptr;

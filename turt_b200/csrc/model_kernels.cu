@@ -50,57 +50,19 @@ template <int NJ>
 __global__ void __launch_bounds__(32 * kEmbedRowsPerBlock)
     k_embed_bwd_rows(const float* __restrict__ dx, const uint32_t* __restrict__ ids, float* __restrict__ dwte, int N,
                      int E, int V) {
-  constexpr int kList = 32;  // matching positions a warp collects before adding them
   __shared__ __align__(16) uint32_t sid[kIdTile];
-  __shared__ int plist[kEmbedRowsPerBlock][kList];
   pdl_trigger();
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t v = (uint32_t)(blockIdx.x * kEmbedRowsPerBlock + warp);
   const int E4 = E / 4;
-  int* pl = plist[warp];
   float4 acc[NJ];
   bool any = false;  // warp-uniform: every lane sees the same matches
-  int cnt = 0;       // warp-uniform
-  // Adds the collected rows in list (= position) order; their loads are issued four at a time.
-  auto flush = [&]() {
-    if (!cnt) return;
-    __syncwarp();
-    if (!any) {
-      const float4* w = reinterpret_cast<const float4*>(dwte + (size_t)v * E);
-#pragma unroll
-      for (int j = 0; j < NJ; j++)
-        if (lane + 32 * j < E4) acc[j] = w[lane + 32 * j];
-      any = true;
-    }
-    for (int k0 = 0; k0 < cnt; k0 += 4) {
-      float4 r[4][NJ];
-#pragma unroll
-      for (int u = 0; u < 4; u++)
-        if (k0 + u < cnt) {
-          const float4* g = reinterpret_cast<const float4*>(dx + (size_t)pl[k0 + u] * E);
-#pragma unroll
-          for (int j = 0; j < NJ; j++)
-            if (lane + 32 * j < E4) r[u][j] = g[lane + 32 * j];
-        }
-#pragma unroll
-      for (int u = 0; u < 4; u++)
-        if (k0 + u < cnt) {
-#pragma unroll
-          for (int j = 0; j < NJ; j++)
-            if (lane + 32 * j < E4) {
-              acc[j].x += r[u][j].x, acc[j].y += r[u][j].y, acc[j].z += r[u][j].z, acc[j].w += r[u][j].w;
-            }
-        }
-    }
-    cnt = 0;
-    __syncwarp();
-  };
   for (int base = 0; base < N; base += kIdTile) {
-    const int tile = min(kIdTile, N - base);
-    const int padded = (tile + 127) & ~127;
+    const int cnt = min(kIdTile, N - base);
+    const int padded = (cnt + 127) & ~127;
     __syncthreads();  // the previous tile has been scanned
-    for (int k = threadIdx.x; k < padded; k += blockDim.x) sid[k] = k < tile ? ids[base + k] : 0xFFFFFFFFu;
+    for (int k = threadIdx.x; k < padded; k += blockDim.x) sid[k] = k < cnt ? ids[base + k] : 0xFFFFFFFFu;
     __syncthreads();
     if (v >= (uint32_t)V) continue;
     const uint4* sid4 = reinterpret_cast<const uint4*>(sid);
@@ -115,14 +77,24 @@ __global__ void __launch_bounds__(32 * kEmbedRowsPerBlock)
         while (bits) {
           const int k = __ffs(bits) - 1;
           bits &= bits - 1;
-          if (cnt == kList) flush();
-          if (lane == 0) pl[cnt] = base + 128 * c + 4 * src + k;
-          cnt++;
+          const float4* g = reinterpret_cast<const float4*>(dx + (size_t)(base + 128 * c + 4 * src + k) * E);
+          if (!any) {
+            const float4* w = reinterpret_cast<const float4*>(dwte + (size_t)v * E);
+#pragma unroll
+            for (int j = 0; j < NJ; j++)
+              if (lane + 32 * j < E4) acc[j] = w[lane + 32 * j];
+            any = true;
+          }
+#pragma unroll
+          for (int j = 0; j < NJ; j++)
+            if (lane + 32 * j < E4) {
+              const float4 t = g[lane + 32 * j];
+              acc[j].x += t.x, acc[j].y += t.y, acc[j].z += t.z, acc[j].w += t.w;
+            }
         }
       }
     }
   }
-  flush();
   if (any) {
     float4* w = reinterpret_cast<float4*>(dwte + (size_t)v * E);
 #pragma unroll
@@ -206,13 +178,12 @@ __global__ void __launch_bounds__(256) k_rms_fwd(const float* __restrict__ x, co
   }
 }
 
-// Block partial written as a row: part_row[c] = sum over the block's 8 warps (fixed order) of
-// their register partials.  Consecutive threads write consecutive columns.
+// Block partial of a per-column sum: the 8 warps' register partials (lane chunks) are combined
+// in shared memory in fixed order and written column-major as part[c][blockIdx.x] (nparts =
+// gridDim.x entries per column), so that the final reduction reads each column contiguously.
 template <int NJ>
-__device__ __forceinline__ void block_partial_row(const float4 (&acc)[NJ], float* sm, float* __restrict__ part_row,
-                                                  int E) {
+__device__ __forceinline__ void block_partial(const float4 (&acc)[NJ], float* sm, float* __restrict__ part, int E) {
   const int w = threadIdx.x / 32, lane = threadIdx.x & 31, n4 = E / 4;
-  __syncthreads();  // sm may still be read by an earlier call
 #pragma unroll
   for (int j = 0; j < NJ; j++) {
     const int i = lane + 32 * j;
@@ -223,64 +194,8 @@ __device__ __forceinline__ void block_partial_row(const float4 (&acc)[NJ], float
     float t = 0.f;
 #pragma unroll
     for (int q = 0; q < kNormWarps; q++) t += sm[q * E + c];
-    part_row[c] = t;
+    part[(size_t)c * gridDim.x + blockIdx.x] = t;
   }
-}
-
-// Column sums of the block partials, finished inside the kernel that wrote them (no second
-// launch).  part[b][c] holds block b's partial (nb = gridDim.x rows of C).  Blocks are grouped by
-// kPartGroup: the last block of a group to finish adds the group's rows in block order into
-// gpart[group][c]; the last group to finish adds the group rows in group order to out[c].  Every
-// sum runs in a fixed order, so the result does not depend on which block finishes last.  ctr
-// holds ng + 1 counters that are zero on entry and are left zero.  part2 / gpart2 / out2, when
-// out2 is non-null, are a second column sum finished alongside (LayerNorm's dbeta).
-constexpr int kPartGroup = 8;
-__device__ __forceinline__ void finish_column_sums(const float* part, float* gpart, float* out, const float* part2,
-                                                   float* gpart2, float* out2, int C, unsigned* ctr) {
-  __shared__ unsigned ticket;
-  const int nb = gridDim.x, ng = (nb + kPartGroup - 1) / kPartGroup, grp = blockIdx.x / kPartGroup;
-  const int b0 = grp * kPartGroup, gsize = min(kPartGroup, nb - b0);
-  __threadfence();  // this thread's partial stores are visible device-wide before the count
-  __syncthreads();
-  if (threadIdx.x == 0) ticket = atomicAdd(&ctr[grp], 1u);
-  __syncthreads();
-  if (ticket != (unsigned)(gsize - 1)) return;
-  __threadfence();
-  for (int c = threadIdx.x; c < C; c += blockDim.x) {
-    float t = 0.f, t2 = 0.f;
-    for (int b = b0; b < b0 + gsize; b++) {
-      t += __ldcg(part + (size_t)b * C + c);
-      if (out2) t2 += __ldcg(part2 + (size_t)b * C + c);
-    }
-    gpart[(size_t)grp * C + c] = t;
-    if (out2) gpart2[(size_t)grp * C + c] = t2;
-  }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    ctr[grp] = 0u;
-    ticket = atomicAdd(&ctr[ng], 1u);
-  }
-  __syncthreads();
-  if (ticket != (unsigned)(ng - 1)) return;
-  __threadfence();
-  for (int c = threadIdx.x; c < C; c += blockDim.x) {
-    float t = 0.f, t2 = 0.f;
-#pragma unroll 8
-    for (int q = 0; q < ng; q++) {
-      t += __ldcg(gpart + (size_t)q * C + c);
-      if (out2) t2 += __ldcg(gpart2 + (size_t)q * C + c);
-    }
-    out[c] += t;
-    if (out2) out2[c] += t2;
-  }
-  if (threadIdx.x == 0) ctr[ng] = 0u;
-}
-
-// Pulls a row of E floats into L2 ahead of its loads (one prefetch per 128-byte line, spread
-// over the warp's lanes).
-__device__ __forceinline__ void prefetch_row_l2(const float* row, int E, int lane) {
-  for (int k = lane * 32; k < E; k += 32 * 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(row + k));
 }
 
 // Register budget of the norm backwards: two 256-thread blocks per SM up to E = 512, one block
@@ -293,16 +208,15 @@ struct NormBwdCfg {
 
 // RMSNorm backward with the residual gradient fused in:
 //   dx = dres + rs*g*dy - (rs^3/E) * (sum_j dy_j g_j x_j) * x      (RMS_DX, autograd.ts:331-351)
-// and dgamma += sum_rows dy * x * rs                               (RMS_DG, :352-365),
-// the column sum finished in this launch (finish_column_sums).  dx may alias dres.  Rows are
-// dealt to warps grid-stride, R rows per iteration: x, dy and dres of those rows are loaded
-// together (3*R*NJ independent 16-byte loads in flight per lane) and the next iteration's rows
-// are prefetched into L2 first.
+// and per-block partial dgamma = sum_rows dy * x * rs              (RMS_DG, :352-365).
+// dx may alias dres.  Rows are dealt to warps grid-stride, R rows per iteration (two for rows of
+// up to 384 floats, so that each warp keeps 6*NJ independent 16-byte loads in flight; one for
+// wider rows, whose registers would spill otherwise).
 template <int NJ>
 __global__ void __launch_bounds__(256, NormBwdCfg<NJ>::kMinBlocks)
     k_rms_bwd(const float* __restrict__ x, const float* __restrict__ dy, const float* __restrict__ g,
-              const float* __restrict__ rstd, const float* dres, float* dx, float* __restrict__ part, float* dg_accum,
-              unsigned* ctr, int rows, int E) {
+              const float* __restrict__ rstd, const float* dres, float* dx, float* __restrict__ dg_part, int rows,
+              int E) {
   constexpr int R = NormBwdCfg<NJ>::kRows;
   pdl_trigger();
   pdl_wait();
@@ -318,21 +232,11 @@ __global__ void __launch_bounds__(256, NormBwdCfg<NJ>::kMinBlocks)
   }
   for (int r0 = blockIdx.x * kNormWarps + threadIdx.x / 32; r0 < rows; r0 += R * stride) {
     int rr[R];
-#pragma unroll
-    for (int q = 0; q < R; q++) rr[q] = r0 + q * stride;
-#pragma unroll
-    for (int q = R; q < 2 * R; q++) {
-      const int rn = r0 + q * stride;
-      if (rn < rows) {
-        prefetch_row_l2(x + (size_t)rn * E, E, lane);
-        prefetch_row_l2(dy + (size_t)rn * E, E, lane);
-        if (dres) prefetch_row_l2(dres + (size_t)rn * E, E, lane);
-      }
-    }
-    float4 xv[R][NJ], dv[R][NJ], tv[R][NJ];
+    float4 xv[R][NJ], dv[R][NJ];
     float s[R], rs[R];
 #pragma unroll
     for (int q = 0; q < R; q++) {
+      rr[q] = r0 + q * stride;
       const bool ok = rr[q] < rows;
       s[q] = 0.f;
       rs[q] = ok ? rstd[rr[q]] : 0.f;
@@ -342,7 +246,6 @@ __global__ void __launch_bounds__(256, NormBwdCfg<NJ>::kMinBlocks)
         const bool in = ok && i < n4;
         xv[q][j] = in ? ld4(x + (size_t)rr[q] * E, i) : make_float4(0.f, 0.f, 0.f, 0.f);
         dv[q][j] = in ? ld4(dy + (size_t)rr[q] * E, i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        tv[q][j] = in && dres ? ld4(dres + (size_t)rr[q] * E, i) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
 #pragma unroll
@@ -361,20 +264,27 @@ __global__ void __launch_bounds__(256, NormBwdCfg<NJ>::kMinBlocks)
       if (rr[q] >= rows) continue;  // warp-uniform
       const float sum = warp_sum(s[q]);
       const float kf = rs[q] * rs[q] * rs[q] * sum / E;
+      const float* dr = dres ? dres + (size_t)rr[q] * E : nullptr;
       float* dxr = dx + (size_t)rr[q] * E;
 #pragma unroll
       for (int j = 0; j < NJ; j++) {
         const int i = lane + 32 * j;
         if (i >= n4) continue;
-        const float4 a = xv[q][j], d = dv[q][j], gg = gv[j], t = tv[q][j];
-        st4(dxr, i,
-            make_float4(rs[q] * d.x * gg.x - kf * a.x + t.x, rs[q] * d.y * gg.y - kf * a.y + t.y,
-                        rs[q] * d.z * gg.z - kf * a.z + t.z, rs[q] * d.w * gg.w - kf * a.w + t.w));
+        const float4 a = xv[q][j], d = dv[q][j], gg = gv[j];
+        float4 o = make_float4(rs[q] * d.x * gg.x - kf * a.x, rs[q] * d.y * gg.y - kf * a.y,
+                               rs[q] * d.z * gg.z - kf * a.z, rs[q] * d.w * gg.w - kf * a.w);
+        if (dr) {
+          const float4 t = ld4(dr, i);
+          o.x += t.x;
+          o.y += t.y;
+          o.z += t.z;
+          o.w += t.w;
+        }
+        st4(dxr, i, o);
       }
     }
   }
-  block_partial_row<NJ>(dgl, sm, part + (size_t)blockIdx.x * E, E);
-  finish_column_sums(part, part + (size_t)2 * gridDim.x * E, dg_accum, nullptr, nullptr, nullptr, E, ctr);
+  block_partial<NJ>(dgl, sm, dg_part, E);
 }
 
 // LayerNorm forward (biased variance), autograd.ts:256-274.
@@ -426,14 +336,13 @@ __global__ void __launch_bounds__(256) k_ln_fwd(const float* __restrict__ x, con
 }
 
 // LayerNorm backward (LN_DX + LN_DGB, autograd.ts:275-308) with the residual gradient fused;
-// dgamma / dbeta column sums finished in this launch (finish_column_sums).  One row per warp
-// iteration, grid-stride.
+// partial dgamma / dbeta per block.  One row per warp iteration, grid-stride.
 template <int NJ>
 __global__ void __launch_bounds__(256, NormBwdCfg<NJ>::kMinBlocks) k_ln_bwd(const float* __restrict__ x, const float* __restrict__ dy,
                                                 const float* __restrict__ g, const float* __restrict__ mean,
                                                 const float* __restrict__ rstd, const float* dres, float* dx,
-                                                float* __restrict__ part, float* dg_accum, float* db_accum,
-                                                unsigned* ctr, int rows, int E) {
+                                                float* __restrict__ dg_part, float* __restrict__ db_part, int rows,
+                                                int E) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ float sm[];
@@ -492,10 +401,9 @@ __global__ void __launch_bounds__(256, NormBwdCfg<NJ>::kMinBlocks) k_ln_bwd(cons
       st4(dxr, i, o);
     }
   }
-  const size_t nbE = (size_t)gridDim.x * E, ngE = (size_t)((gridDim.x + kPartGroup - 1) / kPartGroup) * E;
-  block_partial_row<NJ>(dgl, sm, part + (size_t)blockIdx.x * E, E);
-  block_partial_row<NJ>(dbl, sm, part + nbE + (size_t)blockIdx.x * E, E);
-  finish_column_sums(part, part + 2 * nbE, dg_accum, part + nbE, part + 2 * nbE + ngE, db_accum, E, ctr);
+  block_partial<NJ>(dgl, sm, dg_part, E);
+  __syncthreads();
+  block_partial<NJ>(dbl, sm, db_part, E);
 }
 
 // out[c] += sum_b part[c][b] (column-major partials, fixed order: deterministic).  One warp per
@@ -906,25 +814,21 @@ int rms_fwd(cudaStream_t st, const float* x, const float* g, float* y, float* rs
   TURT_LAUNCH_CHECK();
   return OK;
 }
-// Partial-sum rows a norm backward writes: one per block, at most two blocks per SM (and at most
-// kPartGroup * (kNormCounters - 1) blocks, so that the group counters fit).
+// Partial-sum rows a norm backward writes: one per block, at most two blocks per SM.
 int norm_parts(int rows) {
   const int b = ceil_div(rows, kNormWarps);
-  const int cap = std::min(2 * sm_count(), kPartGroup * (kNormCounters - 1));
-  return b < cap ? b : cap;
-}
-size_t norm_bwd_part_floats(int rows, int E) {
-  const size_t nb = norm_parts(rows), ng = (nb + kPartGroup - 1) / kPartGroup;
-  return 2 * (nb + ng) * (size_t)E;
+  return b < 2 * sm_count() ? b : 2 * sm_count();
 }
 int rms_bwd(cudaStream_t st, const float* x, const float* dy, const float* g, const float* rstd, const float* dres,
-            float* dx, float* dg_accum, float* part, unsigned* ctr, int rows, int E) {
+            float* dx, float* dg_accum, float* part, int rows, int E) {
   TURT_REQUIRE(E % 32 == 0 && E <= 32 * MAXV, "norm width must be a multiple of 32, at most 1024");
   const int nb = norm_parts(rows);
   const size_t smem = (size_t)kNormWarps * E * 4;
-#define CALL(NJ) TURT_CHECK_CUDA((launch_pdl(k_rms_bwd<NJ>, dim3(nb), dim3(256), smem, st, x, dy, g, rstd, dres, dx, part, dg_accum, ctr, rows, E)))
+#define CALL(NJ) TURT_CHECK_CUDA((launch_pdl(k_rms_bwd<NJ>, dim3(nb), dim3(256), smem, st, x, dy, g, rstd, dres, dx, part, rows, E)))
   TURT_NJ_SWITCH(E, CALL)
 #undef CALL
+  TURT_LAUNCH_CHECK();
+  TURT_CHECK_CUDA((launch_pdl(k_reduce_parts, dim3(ceil_div(E, 8)), dim3(256), 0, st, part, nb, E, dg_accum)));
   TURT_LAUNCH_CHECK();
   return OK;
 }
@@ -938,15 +842,18 @@ int ln_fwd(cudaStream_t st, const float* x, const float* g, const float* b, floa
   return OK;
 }
 int ln_bwd(cudaStream_t st, const float* x, const float* dy, const float* g, const float* mean, const float* rstd,
-           const float* dres, float* dx, float* dg_accum, float* db_accum, float* part, unsigned* ctr, int rows,
-           int E) {
+           const float* dres, float* dx, float* dg_accum, float* db_accum, float* part, int rows, int E) {
   TURT_REQUIRE(E % 32 == 0 && E <= 32 * MAXV, "norm width must be a multiple of 32, at most 1024");
   const int nb = norm_parts(rows);
   const size_t smem = (size_t)kNormWarps * E * 4;
 #define CALL(NJ) \
-  TURT_CHECK_CUDA((launch_pdl(k_ln_bwd<NJ>, dim3(nb), dim3(256), smem, st, x, dy, g, mean, rstd, dres, dx, part, dg_accum, db_accum, ctr, rows, E)))
+  TURT_CHECK_CUDA((launch_pdl(k_ln_bwd<NJ>, dim3(nb), dim3(256), smem, st, x, dy, g, mean, rstd, dres, dx, part, part + (size_t)nb * E, rows, E)))
   TURT_NJ_SWITCH(E, CALL)
 #undef CALL
+  TURT_LAUNCH_CHECK();
+  TURT_CHECK_CUDA((launch_pdl(k_reduce_parts, dim3(ceil_div(E, 8)), dim3(256), 0, st, part, nb, E, dg_accum)));
+  TURT_LAUNCH_CHECK();
+  TURT_CHECK_CUDA((launch_pdl(k_reduce_parts, dim3(ceil_div(E, 8)), dim3(256), 0, st, part + (size_t)nb * E, nb, E, db_accum)));
   TURT_LAUNCH_CHECK();
   return OK;
 }

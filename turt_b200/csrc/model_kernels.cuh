@@ -11,20 +11,12 @@ int embed_bwd(cudaStream_t st, const float* dx, const uint32_t* ids, float* dwte
               int V);
 int rms_fwd(cudaStream_t st, const float* x, const float* g, float* y, float* rstd, int rows, int E, float eps);
 int norm_parts(int rows);  // rows of partial sums a norm backward writes (each E wide)
-// Zero-initialised counters a norm backward needs (it leaves them zero).
-constexpr int kNormCounters = 64;
-// Floats of `part` a norm backward needs: block partials and group rows of dgamma and dbeta.
-size_t norm_bwd_part_floats(int rows, int E);
-// Norm backwards finish their dgamma (/ dbeta) column sums in the same launch: `part` holds
-// norm_bwd_part_floats(rows, E) floats, `ctr` kNormCounters zeroed counters (left zeroed);
-// launches using one `ctr` must be ordered on one stream.
 int rms_bwd(cudaStream_t st, const float* x, const float* dy, const float* g, const float* rstd, const float* dres,
-            float* dx, float* dg_accum, float* part, unsigned* ctr, int rows, int E);
+            float* dx, float* dg_accum, float* part, int rows, int E);
 int ln_fwd(cudaStream_t st, const float* x, const float* g, const float* b, float* y, float* mean, float* rstd, int rows,
            int E, float eps);
 int ln_bwd(cudaStream_t st, const float* x, const float* dy, const float* g, const float* mean, const float* rstd,
-           const float* dres, float* dx, float* dg_accum, float* db_accum, float* part, unsigned* ctr, int rows,
-           int E);
+           const float* dres, float* dx, float* dg_accum, float* db_accum, float* part, int rows, int E);
 int colsum_accum(cudaStream_t st, const float* g, int rows, int C, float* out_accum, float* part);
 // SwiGLU backward: d(act) [N][h] and interleaved gate|up pre-activations [N][2h] -> interleaved grads.
 int swiglu_bwd_interleaved(cudaStream_t st, const float* dact, const float* pre, float* dpre, int N, int h);
